@@ -1,0 +1,208 @@
+/*
+ * h3b200.h - C ABI of the B200-native (sm_100a) tensor-parallel W8A8 INT8 linear path.
+ *
+ * Every entry point takes raw device pointers, element counts and a cudaStream_t
+ * (passed as void*), enqueues its kernels on that stream and returns an int status
+ * (H3_OK or an H3_ERR_* code).  Nothing here allocates the caller's tensors:
+ * outputs are written into caller-provided device buffers, the way the reference's
+ * native extension (comfy_kitchen._C.cublas_gemm_int8 / dequantize_int8_linear,
+ * called from patches/optimized_tp.py:331-340 and patches/parallel_int8.py:247-259)
+ * receives DLPack tensors plus a raw stream.  Geometry is checked before any launch
+ * and rejected with H3_ERR_INVALID, the way the reference raises ValueError before
+ * either rank enters a collective (patches/tilelang_swiglu_quant.py:95-105).
+ *
+ * Conventions
+ *   - fp16 buffers are IEEE binary16 (torch.float16), passed as void*.
+ *   - Matrices are row-major and contiguous unless a stride argument says otherwise.
+ *   - int8 weight matrices are [N, K] (output channel major), as in the pre-baked
+ *     rank shards of patches/rank_local_int8.py:62-80.
+ *   - K (the reduction length) must be a multiple of 16 for the GEMMs, and widths
+ *     fed to the ConvRot256 kernels a multiple of 256.
+ */
+#ifndef H3B200_H
+#define H3B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  H3_OK = 0,
+  H3_ERR_INVALID = 1,     /* unsupported geometry, null or misaligned pointer       */
+  H3_ERR_CUDA = 2,        /* a CUDA runtime call or launch failed                    */
+  H3_ERR_TIMEOUT = 3,     /* a bounded device-side wait gave up (see h3_device_error) */
+  H3_ERR_UNSUPPORTED = 4  /* the device is not an sm_100 part                         */
+};
+
+/* FC2 producer input layouts */
+enum {
+  H3_IN_GATEUP_F16 = 0, /* fp16 [rows, 2*width] = [gate_r | up_r] (FC1 column output) */
+  H3_IN_ACT_F32 = 1,    /* fp32 [rows, width] = silu(f16 gate) * f16 up, pre-computed  */
+  H3_IN_ACT_F16 = 2     /* fp16 [rows, width] post-SwiGLU activation                    */
+};
+
+/* Quantizer division (patches/tilelang_row_quant.py:156,169) */
+enum { H3_DIV_RN = 0, H3_DIV_FAST = 1 };
+
+/* Output kinds */
+enum {
+  H3_OUT_F32 = 0,      /* fp32 store                                                   */
+  H3_OUT_F16 = 1,      /* fp16 store (round to nearest even)                           */
+  H3_OUT_RESIDUAL = 2  /* gated residual update in place: X = f16(fma(f16(y), G, X))    */
+};
+
+/* ----------------------------------------------------------------------------
+ * Library / device status
+ * ------------------------------------------------------------------------- */
+int h3_abi_version(void);
+const char* h3_status_string(int status);
+/* Reads, then clears, the device-side error word that bounded waits set when
+ * they give up.  Synchronises the device.  *code = 0 when nothing failed. */
+int h3_device_error(int device, int* code);
+
+/* ----------------------------------------------------------------------------
+ * Column path (QKV / FC1): ColumnParallelLinearINT8.forward, tp_dit.py:69-96
+ * ------------------------------------------------------------------------- */
+
+/* Activation preparation of column_linear: optional regular ConvRot256 rotation
+ * (rotated = f16(H256 x)), then per-row INT8 quantisation with
+ * scale = max(amax * f32(1/127), 1e-30), q = clamp(rint(x / scale), -128, 127).
+ * Replaces dit_column_linear.py:13-21 (_prepare_activation: Kitchen eager
+ * _rotate_activation + quantize_int8_rowwise).
+ *   x_f16 [rows, k], q [rows, k], scale [rows].  convrot: 1 = rotate, 0 = none. */
+int h3_column_quantize(const void* x_f16, int64_t rows, int64_t k, int convrot,
+                       int8_t* q, float* scale, void* stream);
+
+/* Direct INT8 GEMM, INT32 out: out[m, n] = sum_k q[m, k] * w[n, k], exact.
+ * Replaces optimized_tp.py:331-340 (native_int_mm) and parallel_int8.py:240-244. */
+int h3_int8_gemm_i32(const int8_t* q, const int8_t* w, int64_t m, int64_t n, int64_t k,
+                     int32_t* out, void* stream);
+
+/* INT8 GEMM with the ordered column dequant epilogue fused:
+ *   y[m, n] = f16( (f32(acc) *rn (row_scale[m] *rn weight_scale[n])) [+rn bias[n]] )
+ * Replaces dit_column_linear.py:138-149 (native_int_mm followed by
+ * tilelang_column_epilogue.py:11-40).  weight_scale_len is 1 (scalar) or n.
+ * bias may be NULL. */
+int h3_int8_gemm_column(const int8_t* q, const int8_t* w, int64_t m, int64_t n, int64_t k,
+                        const float* row_scale, const float* weight_scale,
+                        int64_t weight_scale_len, const float* bias, void* out_f16,
+                        void* stream);
+
+/* FC1 with the FP32 SwiGLU epilogue fused.  w is the component-packed rank shard
+ * [gate_r | up_r] of n_packed rows (patches/rank_local_int8.py:66-75); the output
+ * has n_packed/2 columns:
+ *   g = f16(col_dequant(gate)), u = f16(col_dequant(up)),
+ *   y = (g /rn (1 +rn exp(-g))) *rn u    (tilelang_swiglu_quant.py:21-24)
+ * out_kind H3_OUT_F32 stores y (same bytes as the fp16 [gate|up] store it
+ * replaces, tp_dit.py:356); H3_OUT_F16 stores f16(y).  bias ([n_packed]) may be NULL. */
+int h3_int8_gemm_swiglu(const int8_t* q, const int8_t* w, int64_t m, int64_t n_packed,
+                        int64_t k, const float* row_scale, const float* weight_scale,
+                        const float* bias, int out_kind, void* out, void* stream);
+
+/* Standalone ordered column epilogue (tilelang_column_epilogue.py:11-40):
+ *   y = f16(f32(acc) *rn (row_scale[m] *rn weight_scale[n])) */
+int h3_column_dequantize(const int32_t* acc, int64_t rows, int64_t width,
+                         const float* row_scale, const float* weight_scale,
+                         int64_t weight_scale_len, void* out_f16, void* stream);
+
+/* ----------------------------------------------------------------------------
+ * FC2 `fused_stored` producer: tilelang_swiglu_quant.py:12-92
+ * ------------------------------------------------------------------------- */
+
+/* Phase 'stored' (rotated != NULL) or 'maximum' (rotated == NULL) of fused_kernel
+ * (tilelang_swiglu_quant.py:37-51) with the group maxima already reduced to one
+ * maximum per row (prepare, :86).  x per input_kind; rotated fp32 [rows, width];
+ * row_max [rows] = max |rotated| over the local row. */
+int h3_swiglu_rotate_max(const void* x, int input_kind, int64_t rows, int64_t width,
+                         float* rotated, float* row_max, void* stream);
+
+/* Phase 'recompute' (tilelang_swiglu_quant.py:52-64): recompute the rotated values
+ * from x and quantise them with the (globally reduced) row_max using the quantizer
+ * of tilelang_row_quant.py:27-46.  q [rows, width], scale [rows]. */
+int h3_swiglu_rotate_quantize(const void* x, int input_kind, int64_t rows, int64_t width,
+                              const float* row_max, int division, int8_t* q, float* scale,
+                              void* stream);
+
+/* TP=1 single pass: rotation, row maximum and quantisation of a whole row in one
+ * kernel (no collective in between).  Writes q, scale and row_max. */
+int h3_swiglu_rotate_quantize_local(const void* x, int input_kind, int64_t rows,
+                                    int64_t width, int division, int8_t* q, float* scale,
+                                    float* row_max, void* stream);
+
+/* Row quantizer with an external (reduced) maximum: tilelang_row_quant.py:27-46.
+ * Reads rotated[r, start + c] for c < width, row pitch `stride` floats. */
+int h3_row_quantize(const float* rotated, int64_t rows, int64_t width, int64_t stride,
+                    int64_t start, const float* row_max, int division, int8_t* q,
+                    float* scale, void* stream);
+
+/* ----------------------------------------------------------------------------
+ * Row path (O / FC2): RowParallelLinearINT8.forward, tp_dit.py:141-162
+ * ------------------------------------------------------------------------- */
+
+/* Power-of-two transport shift for a full (all-rank) reduction length full_k:
+ * max(0, ceil(log2(full_k * 127 * 127 / 60000))).  Equals the reference's
+ * shift_for(local_k) (tilelang_transport_tradeoffs.py:20-22) at TP2, where
+ * full_k = 2 * local_k. */
+int h3_transport_shift(int64_t full_k);
+
+/* INT8 GEMM with the scaled-FP16 encode fused (parallel_int8.int_mm followed by
+ * tilelang_transport_tradeoffs.py:26-39 encode):  y = f16(f32(acc) *rn 2^-shift) */
+int h3_int8_gemm_row_encode(const int8_t* q, const int8_t* w, int64_t m, int64_t n,
+                            int64_t k, int shift, void* out_f16, void* stream);
+
+/* TP=1 row GEMM with the dequant fused (exact INT32, no transport):
+ *   y = (f32(acc) *rn row_scale[m]) *rn weight_scale[n]   (parallel_int8.py:260)
+ * out_kind F32/F16 store y into out; H3_OUT_RESIDUAL updates residual_f16 in place
+ * with X = f16(fma(f32(f16(y)), G[labels[m], n], f32(X))) (tilelang_dit_fusion.py:
+ * 57-77); gate == NULL means G = 1.  labels may be NULL when gate_rows == 1. */
+int h3_int8_gemm_row_dequant(const int8_t* q, const int8_t* w, int64_t m, int64_t n,
+                             int64_t k, const float* row_scale, const float* weight_scale,
+                             int out_kind, void* out, void* residual_f16, const float* gate,
+                             int64_t gate_rows, const int32_t* labels, void* stream);
+
+/* Scaled-FP16 codec (tilelang_transport_tradeoffs.py:26-39):
+ *   encode y = f16(f32(p) *rn 2^-shift);   decode p = (int32)(f32(y) *rn 2^shift) */
+int h3_fp16_encode(const int32_t* partial, int64_t n, int shift, void* out_f16,
+                   void* stream);
+int h3_fp16_decode(const void* payload_f16, int64_t n, int shift, int32_t* out,
+                   void* stream);
+
+/* Fixed-order partial reduction + fused epilogue (tilelang_transport_p2.py:15-47 and
+ * tilelang_dit_fusion.py:57-77), for the rows this rank owns:
+ *   t = f16( f32(P_0) + f32(P_1) + ... + f32(P_{world-1}) )   (fp32 sum, rank order)
+ *   restored = (int32) trunc(f32(t) *rn 2^shift)
+ *   y = (f32(restored) *rn row_scale[m]) *rn weight_scale[n]
+ * then stored per out_kind as in h3_int8_gemm_row_dequant.  parts_f16 holds `world`
+ * fp16 [rows, width] blocks, part_stride elements apart.  At world == 2 the sum is
+ * the single RN fp16 addition of NCCL's fp16 SUM; world == 1 is the reference's
+ * epilogue / row_gate_kernel applied to an already reduced payload. */
+int h3_row_reduce_finish(const void* parts_f16, int world, int64_t part_stride,
+                         int64_t rows, int64_t width, int shift, const float* row_scale,
+                         const float* weight_scale, int out_kind, void* out,
+                         void* residual_f16, const float* gate, int64_t gate_rows,
+                         const int32_t* labels, void* stream);
+
+/* INT32 dequantisation of parallel_int8.dequantize (parallel_int8.py:247-263):
+ *   y = ((f32(acc) *rn row_scale[m]) *rn weight_scale[n]) [+rn bias[n]]
+ * stored as out_kind F32 or F16. */
+int h3_dequantize_i32(const int32_t* acc, int64_t rows, int64_t width,
+                      const float* row_scale, const float* weight_scale,
+                      int64_t weight_scale_len, const float* bias, int out_kind, void* out,
+                      void* stream);
+
+/* ----------------------------------------------------------------------------
+ * Diagnostics
+ * ------------------------------------------------------------------------- */
+
+/* Evaluates the library's exponential (h3_expf) and CUDA's expf on n inputs:
+ * ours[i] = h3_expf(x[i]), cuda[i] = expf(x[i]).  Used to measure how often the
+ * oracle-pinned exponential differs from the one the reference calls. */
+int h3_expf_compare(const float* x, int64_t n, float* ours, float* cuda, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* H3B200_H */

@@ -1,0 +1,242 @@
+// Shared device helpers for the B200 tensor-parallel W8A8 INT8 linear path.
+//
+// Every floating-point step that the reference writes as an explicitly rounded
+// intrinsic (__fadd_rn, __fmul_rn, __fdiv_rn, __fmaf_rn in the TileLang sources of
+// patches/tilelang_*.py) is written the same way here, so the compiler can neither
+// contract nor reorder it.  The library is also built with --fmad=false.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+#include "../../include/h3b200.h"
+
+#define H3_DEV __device__ __forceinline__
+
+namespace h3 {
+
+// ---------------------------------------------------------------------------
+// Bit-pattern float constants (exactly the float32 values the reference uses).
+// ---------------------------------------------------------------------------
+H3_DEV float f32_bits(uint32_t b) { return __uint_as_float(b); }
+
+// float32(1/127): tilelang_row_quant.py:167, tilelang_swiglu_quant.py:58
+#define H3_INV127_BITS 0x3c010204u
+// float32(1e-30): the scale floor of the same lines
+#define H3_SCALE_FLOOR_BITS 0x0da24260u
+
+// ---------------------------------------------------------------------------
+// h3_expf: exp(x) for the SwiGLU denominator.
+//
+// The reference calls CUDA's expf (tilelang_swiglu_quant.py:22).  A CPU oracle
+// cannot reproduce that bit for bit, so the path uses its own exponential, written
+// from the Cody-Waite argument reduction (Cody & Waite, "Software Manual for the
+// Elementary Functions", 1980) with a two-part ln2 whose rounding error is carried
+// along, the degree-8 Taylor polynomial of exp(r) - 1 - r on |r| <= ln2/2, and a
+// Fast2Sum (Dekker 1971) of 1 + r so only the final addition rounds at full weight.
+// Every step is an explicit IEEE RN operation; the CPU oracle restates the same steps
+// and is bit-identical.  Measured on the CPU: <= 0.61 ulp, correctly rounded for
+// 99.3% of the fp16 inputs the SwiGLU sees.  The disagreement against CUDA expf is
+// measured on the GPU by tests/test_gpu_kernels.py.
+// ---------------------------------------------------------------------------
+H3_DEV float h3_expf(float x) {
+  if (x != x) return __fadd_rn(x, x);           // NaN in, NaN out
+  if (x > 89.0f) return __uint_as_float(0x7f800000u);
+  if (x < -104.0f) return 0.0f;
+  const float l2e = f32_bits(0x3fb8aa3bu);       // float32(1/ln 2)
+  const float ln2_hi = f32_bits(0x3f317200u);    // 16 significant bits
+  const float ln2_lo = f32_bits(0x35bfbe8eu);    // float32(ln2 - ln2_hi)
+  const float n = rintf(__fmul_rn(x, l2e));
+  const float r1 = __fmaf_rn(-n, ln2_hi, x);                 // exact
+  const float r = __fmaf_rn(-n, ln2_lo, r1);                 // rounded reduced argument
+  const float corr = __fmaf_rn(-n, ln2_lo, __fadd_rn(r1, -r));  // its rounding error
+  float t = __fmaf_rn(r, f32_bits(0x37d00d01u), f32_bits(0x39500d01u));  // 1/40320, 1/5040
+  t = __fmaf_rn(t, r, f32_bits(0x3ab60b61u));                             // 1/720
+  t = __fmaf_rn(t, r, f32_bits(0x3c088889u));                             // 1/120
+  t = __fmaf_rn(t, r, f32_bits(0x3d2aaaabu));                             // 1/24
+  t = __fmaf_rn(t, r, f32_bits(0x3e2aaaabu));                             // 1/6
+  t = __fmaf_rn(t, r, 0.5f);
+  const float s = __fmaf_rn(t, __fmul_rn(r, r), corr);
+  const float hi = __fadd_rn(1.0f, r);
+  const float lo = __fadd_rn(r, -__fadd_rn(hi, -1.0f));      // exact error of 1 + r
+  const float y = __fadd_rn(hi, __fadd_rn(lo, s));
+  const int ni = (int)n;
+  const int h = ni >> 1;                         // floor(ni / 2)
+  const float s1 = __uint_as_float((uint32_t)(h + 127) << 23);
+  const float s2 = __uint_as_float((uint32_t)(ni - h + 127) << 23);
+  return __fmul_rn(__fmul_rn(y, s1), s2);
+}
+
+// FP32 SwiGLU of one (gate, up) pair, in the order of tilelang_swiglu_quant.py:21-24:
+//   a = (gate /rn (1 +rn exp(-gate))) *rn up
+H3_DEV float swiglu_f32(float gate, float up) {
+  const float den = __fadd_rn(1.0f, h3_expf(-gate));
+  const float act = __fdiv_rn(gate, den);
+  return __fmul_rn(act, up);
+}
+
+// Row scale of the production row quantizer (tilelang_row_quant.py:166-167):
+//   scale = fmaxf(fminf(max, FLT_MAX) *rn float32(1/127), 1e-30)
+H3_DEV float row_scale_from_max(float m) {
+  const float mm = fminf(m, 3.4028234663852886e38f);
+  return fmaxf(__fmul_rn(mm, f32_bits(H3_INV127_BITS)), f32_bits(H3_SCALE_FLOOR_BITS));
+}
+
+// One INT8 code (tilelang_row_quant.py:169-173).  division: 0 = IEEE (__fdiv_rn),
+// 1 = the reference's production '__fdividef' fast division.
+H3_DEV int8_t quantize_code(float x, float scale, int division) {
+  const float scaled = division ? __fdividef(x, scale) : __fdiv_rn(x, scale);
+  const float rounded = rintf(scaled);
+  const float clipped = fminf(127.0f, fmaxf(-128.0f, rounded));
+  return (int8_t)(int)clipped;
+}
+
+// ---------------------------------------------------------------------------
+// Regular ConvRot256 butterfly: one radix-4 stage over a 16-value register block.
+// Stage stride s in {1, 4}; output digit d of each 4-point set is
+//   d=0: ((a+b)+c)-d   d=1: ((a+b)-c)+d   d=2: ((a-b)+c)+d   d=3: ((b-a)+c)+d
+// which is B[i] = ((p+q)+r)+s with the negations of tilelang_swiglu_quant.py:28-33.
+// ---------------------------------------------------------------------------
+template <int S>
+H3_DEV void radix4_stage(float (&v)[16]) {
+#pragma unroll
+  for (int base = 0; base < 16; ++base) {
+    if ((base / S) % 4 != 0) continue;
+    const float a = v[base], b = v[base + S], c = v[base + 2 * S], d = v[base + 3 * S];
+    const float ab = __fadd_rn(a, b);
+    v[base]         = __fadd_rn(__fadd_rn(ab, c), -d);
+    v[base + S]     = __fadd_rn(__fadd_rn(ab, -c), d);
+    v[base + 2 * S] = __fadd_rn(__fadd_rn(__fadd_rn(a, -b), c), d);
+    v[base + 3 * S] = __fadd_rn(__fadd_rn(__fadd_rn(-a, b), c), d);
+  }
+}
+
+// Full 256-point regular rotation of one group held by 16 consecutive lanes of a warp
+// (lane % 16 == block index b, v[j] = element 16*b + j on entry).  Stages 0-1 run on
+// the lane's own block, a transpose through shared memory hands every lane the 16
+// values {16*t + r}, stages 2-3 run on those, and a second transpose restores
+// v[j] = rotated element 16*b + j, already multiplied by 1/16.
+// tile: 16 x 17 floats of shared memory private to this half warp.
+H3_DEV void convrot256_halfwarp(float (&v)[16], float* tile, int b) {
+  radix4_stage<1>(v);
+  radix4_stage<4>(v);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) tile[b * 17 + j] = v[j];
+  __syncwarp();
+#pragma unroll
+  for (int t = 0; t < 16; ++t) v[t] = tile[t * 17 + b];
+  __syncwarp();
+  radix4_stage<1>(v);
+  radix4_stage<4>(v);
+#pragma unroll
+  for (int t = 0; t < 16; ++t) tile[t * 17 + b] = __fmul_rn(v[t], 0.0625f);
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = tile[b * 17 + j];
+  __syncwarp();
+}
+
+// ---------------------------------------------------------------------------
+// Vector load/store helpers.
+// ---------------------------------------------------------------------------
+H3_DEV void load_half16_as_float(const __half* p, float (&v)[16]) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+  uint4 u0 = __ldg(q), u1 = __ldg(q + 1);
+  const __half2* h0 = reinterpret_cast<const __half2*>(&u0);
+  const __half2* h1 = reinterpret_cast<const __half2*>(&u1);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f0 = __half22float2(h0[i]);
+    float2 f1 = __half22float2(h1[i]);
+    v[2 * i] = f0.x; v[2 * i + 1] = f0.y;
+    v[8 + 2 * i] = f1.x; v[8 + 2 * i + 1] = f1.y;
+  }
+}
+
+H3_DEV void load_float16(const float* p, float (&v)[16]) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float4 f = __ldg(q + i);
+    v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+  }
+}
+
+H3_DEV void store_float16(float* p, const float (&v)[16]) {
+  float4* q = reinterpret_cast<float4*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) q[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
+H3_DEV void store_int8x16(int8_t* p, const int8_t (&c)[16]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    w[i] = (uint32_t)(uint8_t)c[4 * i] | ((uint32_t)(uint8_t)c[4 * i + 1] << 8) |
+           ((uint32_t)(uint8_t)c[4 * i + 2] << 16) | ((uint32_t)(uint8_t)c[4 * i + 3] << 24);
+  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+H3_DEV float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// Output stage shared by the row epilogues.
+//   y: FP32 dequantised row output of one element
+// ---------------------------------------------------------------------------
+struct RowOut {
+  int kind;
+  void* out;
+  __half* residual;
+  const float* gate;
+  int64_t gate_rows;
+  const int32_t* labels;
+  int* err;
+};
+
+H3_DEV float gate_value(const RowOut& o, int64_t r, int64_t c, int64_t width) {
+  if (o.gate == nullptr) return 1.0f;
+  int64_t lab = o.labels ? (int64_t)__ldg(o.labels + r) : 0;
+  if (lab < 0 || lab >= o.gate_rows) {
+    atomicExch(o.err, H3_ERR_INVALID);
+    lab = 0;
+  }
+  return __ldg(o.gate + lab * width + c);
+}
+
+// Applies the out_kind of one element (tilelang_dit_fusion.py:68-75 for RESIDUAL).
+H3_DEV void row_store(const RowOut& o, int64_t r, int64_t c, int64_t width, float y) {
+  const int64_t idx = r * width + c;
+  if (o.kind == H3_OUT_F32) {
+    reinterpret_cast<float*>(o.out)[idx] = y;
+  } else if (o.kind == H3_OUT_F16) {
+    reinterpret_cast<__half*>(o.out)[idx] = __float2half_rn(y);
+  } else {
+    const float branch = __half2float(__float2half_rn(y));
+    const float g = gate_value(o, r, c, width);
+    const float x = __half2float(o.residual[idx]);
+    o.residual[idx] = __float2half_rn(__fmaf_rn(branch, g, x));
+  }
+}
+
+}  // namespace h3
+
+// ---------------------------------------------------------------------------
+// Host-side helpers shared by the entry points.
+// ---------------------------------------------------------------------------
+namespace h3host {
+
+int bind_device_of(const void* ptr, int* device);  // cudaSetDevice to the pointer's device
+int sm_count(int device);
+int* error_word(int device);                         // lazily created device word
+int check_launch();                                  // maps cudaGetLastError to a status
+
+inline bool aligned(const void* p, unsigned a) { return ((uintptr_t)p % a) == 0; }
+
+}  // namespace h3host

@@ -1,0 +1,654 @@
+// tcgen05 kind::i8 GEMM for sm_100a with fused epilogues.
+//
+//   C[m, n] = sum_k A[m, k] * B[n, k]      A: int8 [M, K] activations (K-major)
+//                                          B: int8 [N, K] weights     (K-major)
+//
+// Design (one CTA per SM, persistent over output tiles):
+//   - tile 128 x 256 x 128 (BM x BN x BK, BK in bytes); A and B tiles are moved
+//     global -> shared by TMA (cp.async.bulk.tensor, 128-byte swizzle, no multicast)
+//     into a 4-stage ring guarded by mbarriers;
+//   - warp 0 lane 0 issues the TMA loads; warp 1 lane 0 issues tcgen05.mma
+//     (cta_group::1, kind::i8, M=128, N=256, K=32 per instruction) into an INT32
+//     accumulator in tensor memory (TMEM); two 256-column accumulators are
+//     double-buffered so the epilogue of tile i overlaps the MMAs of tile i+1;
+//   - warps 2-5 (one per 32-lane TMEM quadrant) read the accumulator with
+//     tcgen05.ld, apply the fused epilogue and store to global memory.
+//
+// Every mbarrier wait is bounded (2 s of %globaltimer); a wait that gives up sets the
+// library's device error word (H3_ERR_TIMEOUT), raises a CTA-wide abort flag, and
+// every role then leaves its loop, waits (bounded) for its own TMA copies and MMAs in
+// flight, and the CTA frees its TMEM and returns.
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "h3_common.cuh"
+
+namespace h3 {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 128;  // bytes == int8 elements; one 128-byte swizzle atom row
+constexpr int STAGES = 4;
+constexpr int A_STAGE = BM * BK;  // 16 KiB
+constexpr int B_STAGE = BN * BK;  // 32 KiB
+constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr unsigned long long TIMEOUT_NS = 2000000000ull;
+
+// Instruction descriptor, kind::i8: D = S32 (bits 4-5 = 2), A = B = signed 8-bit
+// (bits 7-9 and 10-12 = 1), both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                           ((uint32_t)(BM >> 4) << 24);
+
+enum Epi { EPI_I32 = 0, EPI_COLUMN = 1, EPI_SWIGLU = 2, EPI_ROW_ENCODE = 3, EPI_ROW_DEQUANT = 4 };
+
+struct Args {
+  int64_t M;          // rows of A / output rows
+  int64_t N;          // output columns (SWIGLU: gate rows = n_packed / 2)
+  int64_t K;
+  int tiles_m, tiles_n, num_kb;
+  void* out;
+  int out_kind;
+  const float* row_scale;
+  const float* weight_scale;
+  int scalar_w;
+  const float* bias;
+  float enc_factor;
+  RowOut row;
+  int* err;
+};
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+H3_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+H3_DEV uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+H3_DEV void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+H3_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait.  Returns false (and raises the abort flag) on timeout, or when another
+// role has already aborted and honour_abort is set.
+H3_DEV bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
+                      bool honour_abort = true) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  uint32_t it = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++it & 63u) == 0) {
+      if (honour_abort && *abort_flag) return false;
+      if (globaltimer() - t0 > TIMEOUT_NS) {
+        *abort_flag = 1;
+        atomicExch(err, H3_ERR_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+H3_DEV void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+H3_DEV void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+H3_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, int32_t c0, int32_t c1,
+                        uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+
+H3_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+H3_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+H3_DEV void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+
+H3_DEV void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                      uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row core groups 1024 B
+// apart (SBO), descriptor version 1, base offset 0 (stage buffers are 1024-aligned).
+H3_DEV uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)1u << 16;             // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024u >> 4) << 32;   // stride byte offset
+  d |= (uint64_t)1u << 46;             // version
+  d |= (uint64_t)2u << 61;             // SWIZZLE_128B
+  return d;
+}
+
+H3_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, "
+      "[%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Tile order: groups of 16 M-blocks sweep all N-blocks, so concurrently running
+// CTAs share A rows and B columns in L2.
+H3_DEV void tile_coords(int tile, int tiles_m, int tiles_n, int& mb, int& nb) {
+  const int group = 16 * tiles_n;
+  const int g = tile / group;
+  const int first_m = g * 16;
+  const int gm = min(tiles_m - first_m, 16);
+  const int local = tile - g * group;
+  mb = first_m + local % gm;
+  nb = local / gm;
+}
+
+// ---------------------------------------------------------------------------
+// Epilogue helpers: one thread owns one output row and 32 consecutive columns.
+// ---------------------------------------------------------------------------
+H3_DEV void store_f16_chunk(__half* dst, int64_t n0, int64_t N, const float (&v)[32], bool vec) {
+  if (vec && n0 + 32 <= N) {
+    uint4* p = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __half2 h[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(v[8 * i + 2 * j], v[8 * i + 2 * j + 1]);
+      p[i] = *reinterpret_cast<uint4*>(h);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (n0 + j < N) dst[j] = __float2half_rn(v[j]);
+  }
+}
+
+H3_DEV void store_f32_chunk(float* dst, int64_t n0, int64_t N, const float (&v)[32], bool vec) {
+  if (vec && n0 + 32 <= N) {
+    float4* p = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) p[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (n0 + j < N) dst[j] = v[j];
+  }
+}
+
+H3_DEV void load_scales32(const float* w, int64_t n0, int64_t N, int scalar, float (&s)[32]) {
+  if (scalar) {
+    const float v = __ldg(w);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) s[j] = v;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) s[j] = (n0 + j < N) ? __ldg(w + n0 + j) : 0.0f;
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmB2, const Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(full + s), 1);
+      mbar_init(smem_u32(empty + s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(tfull + a), 1);
+      mbar_init(smem_u32(tempty + a), 128);
+    }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total_tiles = args.tiles_m * args.tiles_n;
+  const int num_kb = args.num_kb;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------ TMA producer ------------------------------
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, args.tiles_m, args.tiles_n, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(empty + stage), phase ^ 1u, abort_flag, args.err)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(full + stage);
+          mbar_expect_tx(fb, STAGE_BYTES);
+          tma_load_2d(smem_u32(sA + stage * A_STAGE), &tmA, kb * BK, mb * BM, fb);
+          if (EPI == EPI_SWIGLU) {
+            tma_load_2d(smem_u32(sB + stage * B_STAGE), &tmB, kb * BK, nb * (BN / 2), fb);
+            tma_load_2d(smem_u32(sB + stage * B_STAGE + (BN / 2) * BK), &tmB2, kb * BK,
+                        nb * (BN / 2), fb);
+          } else {
+            tma_load_2d(smem_u32(sB + stage * B_STAGE), &tmB, kb * BK, nb * BN, fb);
+          }
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Every TMA copy this thread issued must have landed before the CTA exits.
+      for (int s = 0; s < STAGES; ++s)
+        if (issued_mask & (1u << s))
+          mbar_wait(smem_u32(full + s), (issued_parity >> s) & 1u, abort_flag, args.err, false);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------ MMA issuer --------------------------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(smem_u32(tempty + acc), acc_phase ^ 1u, abort_flag, args.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(full + stage), phase, abort_flag, args.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * A_STAGE);
+          const uint32_t b0 = smem_u32(sB + stage * B_STAGE);
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k) {
+            tc_mma_i8(d_tmem, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), IDESC,
+                      (kb | k) != 0 ? 1u : 0u);
+          }
+          tc_commit(smem_u32(empty + stage));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(smem_u32(tfull + acc));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      // All MMAs issued by this thread complete before TMEM is released.
+      tc_commit(smem_u32(drain));
+      mbar_wait(smem_u32(drain), 0, abort_flag, args.err, false);
+    }
+  } else {
+    // ------------------------------ epilogue ------------------------------------
+    const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad + 32)
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+      int mb, nb;
+      tile_coords(tile, args.tiles_m, args.tiles_n, mb, nb);
+      if (!mbar_wait(smem_u32(tfull + acc), acc_phase, abort_flag, args.err)) break;
+      tc_fence_after();
+      const int64_t row = (int64_t)mb * BM + quad * 32 + lane;
+      const bool row_ok = row < args.M;
+      const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+      const int64_t N = args.N;
+
+      if (EPI == EPI_SWIGLU) {
+        const int64_t n_base = (int64_t)nb * (BN / 2);
+        const float a = row_ok ? __ldg(args.row_scale + row) : 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < (BN / 2) / 32; ++c) {
+          uint32_t rg[32], ru[32];
+          tmem_ld32(tbase + c * 32, rg);
+          tmem_ld32(tbase + BN / 2 + c * 32, ru);
+          const int64_t n0 = n_base + c * 32;
+          float wg[32], wu[32];
+          load_scales32(args.weight_scale, n0, N, 0, wg);
+          load_scales32(args.weight_scale + N, n0, N, 0, wu);
+          float y[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float vg = __fmul_rn(__int2float_rn((int32_t)rg[j]), __fmul_rn(a, wg[j]));
+            float vu = __fmul_rn(__int2float_rn((int32_t)ru[j]), __fmul_rn(a, wu[j]));
+            if (args.bias != nullptr && n0 + j < N) {
+              vg = __fadd_rn(vg, __ldg(args.bias + n0 + j));
+              vu = __fadd_rn(vu, __ldg(args.bias + N + n0 + j));
+            }
+            const float g = __half2float(__float2half_rn(vg));
+            const float u = __half2float(__float2half_rn(vu));
+            y[j] = swiglu_f32(g, u);
+          }
+          if (row_ok) {
+            if (args.out_kind == H3_OUT_F32)
+              store_f32_chunk(reinterpret_cast<float*>(args.out) + row * N + n0, n0, N, y,
+                              (N & 3) == 0);
+            else
+              store_f16_chunk(reinterpret_cast<__half*>(args.out) + row * N + n0, n0, N, y,
+                              (N & 7) == 0);
+          }
+        }
+      } else {
+        const int64_t n_base = (int64_t)nb * BN;
+        const float a = (row_ok && args.row_scale != nullptr) ? __ldg(args.row_scale + row) : 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          const int64_t n0 = n_base + c * 32;
+          if (n0 >= N) break;  // warp-uniform
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          if (!row_ok) continue;
+          if (EPI == EPI_I32) {
+            int32_t* dst = reinterpret_cast<int32_t*>(args.out) + row * N + n0;
+            if (n0 + 32 <= N && (N & 3) == 0) {
+              int4* p = reinterpret_cast<int4*>(dst);
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                p[i] = make_int4((int)r[4 * i], (int)r[4 * i + 1], (int)r[4 * i + 2], (int)r[4 * i + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n0 + j < N) dst[j] = (int32_t)r[j];
+            }
+          } else if (EPI == EPI_COLUMN) {
+            float w[32], y[32];
+            load_scales32(args.weight_scale, n0, N, args.scalar_w, w);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              y[j] = __fmul_rn(__int2float_rn((int32_t)r[j]), __fmul_rn(a, w[j]));
+              if (args.bias != nullptr && n0 + j < N) y[j] = __fadd_rn(y[j], __ldg(args.bias + n0 + j));
+            }
+            store_f16_chunk(reinterpret_cast<__half*>(args.out) + row * N + n0, n0, N, y,
+                            (N & 7) == 0);
+          } else if (EPI == EPI_ROW_ENCODE) {
+            float y[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) y[j] = __fmul_rn(__int2float_rn((int32_t)r[j]), args.enc_factor);
+            store_f16_chunk(reinterpret_cast<__half*>(args.out) + row * N + n0, n0, N, y,
+                            (N & 7) == 0);
+          } else {  // EPI_ROW_DEQUANT
+            float w[32], y[32];
+            load_scales32(args.weight_scale, n0, N, 0, w);
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              y[j] = __fmul_rn(__fmul_rn(__int2float_rn((int32_t)r[j]), a), w[j]);
+            if (args.row.kind == H3_OUT_F32) {
+              store_f32_chunk(reinterpret_cast<float*>(args.row.out) + row * N + n0, n0, N, y,
+                              (N & 3) == 0);
+            } else if (args.row.kind == H3_OUT_F16) {
+              store_f16_chunk(reinterpret_cast<__half*>(args.row.out) + row * N + n0, n0, N, y,
+                              (N & 7) == 0);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n0 + j < N) row_store(args.row, row, n0 + j, N, y[j]);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(tempty + acc));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// Row-major int8 [rows, k] with a (box_rows x 128-byte) box and 128-byte swizzle.
+static bool make_map(CUtensorMap* map, const int8_t* base, int64_t rows, int64_t k, int box_rows) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)k};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+static bool device_is_sm100(int dev) {
+  static int cache[64] = {0};  // 0 unknown, 1 yes, 2 no
+  if (dev < 0 || dev >= 64) return false;
+  if (cache[dev] == 0) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cache[dev] = (major == 10 && minor == 0) ? 1 : 2;
+  }
+  return cache[dev] == 1;
+}
+
+template <int EPI>
+static int launch(const int8_t* q, const int8_t* w, int64_t M, int64_t N, int64_t K, Args args,
+                  cudaStream_t stream) {
+  if (q == nullptr || w == nullptr || M < 0 || N <= 0 || K <= 0 || K % 16 != 0)
+    return H3_ERR_INVALID;
+  if (!h3host::aligned(q, 16) || !h3host::aligned(w, 16)) return H3_ERR_INVALID;
+  if (M > (int64_t)1 << 31 || N > (int64_t)1 << 24 || K > (int64_t)1 << 20) return H3_ERR_INVALID;
+  if (M == 0) return H3_OK;
+  int dev;
+  if (int s = h3host::bind_device_of(q, &dev)) return s;
+  if (!device_is_sm100(dev)) return H3_ERR_UNSUPPORTED;
+  CUtensorMap tA, tB, tB2;
+  if (!make_map(&tA, q, M, K, BM)) return H3_ERR_INVALID;
+  if (EPI == EPI_SWIGLU) {
+    if (!make_map(&tB, w, N, K, BN / 2)) return H3_ERR_INVALID;
+    if (!make_map(&tB2, w + N * K, N, K, BN / 2)) return H3_ERR_INVALID;
+  } else {
+    if (!make_map(&tB, w, N, K, BN)) return H3_ERR_INVALID;
+    tB2 = tB;
+  }
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.tiles_m = (int)((M + BM - 1) / BM);
+  args.tiles_n = (int)((N + (EPI == EPI_SWIGLU ? BN / 2 : BN) - 1) / (EPI == EPI_SWIGLU ? BN / 2 : BN));
+  args.num_kb = (int)((K + BK - 1) / BK);
+  args.err = h3host::error_word(dev);
+  if (args.err == nullptr) return H3_ERR_CUDA;
+  if (args.row.err == nullptr) args.row.err = args.err;
+  const int64_t tiles = (int64_t)args.tiles_m * args.tiles_n;
+  if (tiles > INT32_MAX) return H3_ERR_INVALID;
+  const int grid = (int)std::min<int64_t>(tiles, h3host::sm_count(dev));
+  static bool attr_set[64] = {false};
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(gemm_i8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             SMEM_BYTES) != cudaSuccess)
+      return H3_ERR_CUDA;
+    attr_set[dev] = true;
+  }
+  gemm_i8_kernel<EPI><<<grid, THREADS, SMEM_BYTES, stream>>>(tA, tB, tB2, args);
+  return h3host::check_launch();
+}
+
+static Args blank_args() {
+  Args a;
+  memset(&a, 0, sizeof(a));
+  a.row.kind = H3_OUT_F32;
+  return a;
+}
+
+}  // namespace gemm
+}  // namespace h3
+
+using namespace h3;
+using namespace h3::gemm;
+
+extern "C" int h3_int8_gemm_i32(const int8_t* q, const int8_t* w, int64_t m, int64_t n,
+                                int64_t k, int32_t* out, void* stream) {
+  if (out == nullptr || !h3host::aligned(out, 16)) return H3_ERR_INVALID;
+  Args a = blank_args();
+  a.out = out;
+  return launch<EPI_I32>(q, w, m, n, k, a, (cudaStream_t)stream);
+}
+
+extern "C" int h3_int8_gemm_column(const int8_t* q, const int8_t* w, int64_t m, int64_t n,
+                                   int64_t k, const float* row_scale, const float* weight_scale,
+                                   int64_t weight_scale_len, const float* bias, void* out_f16,
+                                   void* stream) {
+  if (out_f16 == nullptr || row_scale == nullptr || weight_scale == nullptr ||
+      (weight_scale_len != 1 && weight_scale_len != n) || !h3host::aligned(out_f16, 16))
+    return H3_ERR_INVALID;
+  Args a = blank_args();
+  a.out = out_f16;
+  a.row_scale = row_scale;
+  a.weight_scale = weight_scale;
+  a.scalar_w = weight_scale_len == 1;
+  a.bias = bias;
+  return launch<EPI_COLUMN>(q, w, m, n, k, a, (cudaStream_t)stream);
+}
+
+extern "C" int h3_int8_gemm_swiglu(const int8_t* q, const int8_t* w, int64_t m,
+                                   int64_t n_packed, int64_t k, const float* row_scale,
+                                   const float* weight_scale, const float* bias, int out_kind,
+                                   void* out, void* stream) {
+  if (out == nullptr || row_scale == nullptr || weight_scale == nullptr || n_packed <= 0 ||
+      n_packed % 2 != 0 || (out_kind != H3_OUT_F32 && out_kind != H3_OUT_F16) ||
+      !h3host::aligned(out, 16) || k % 16 != 0)
+    return H3_ERR_INVALID;
+  Args a = blank_args();
+  a.out = out;
+  a.out_kind = out_kind;
+  a.row_scale = row_scale;
+  a.weight_scale = weight_scale;
+  a.bias = bias;
+  return launch<EPI_SWIGLU>(q, w, m, n_packed / 2, k, a, (cudaStream_t)stream);
+}
+
+extern "C" int h3_int8_gemm_row_encode(const int8_t* q, const int8_t* w, int64_t m, int64_t n,
+                                       int64_t k, int shift, void* out_f16, void* stream) {
+  if (out_f16 == nullptr || shift < 0 || shift > 60 || !h3host::aligned(out_f16, 16))
+    return H3_ERR_INVALID;
+  Args a = blank_args();
+  a.out = out_f16;
+  a.enc_factor = ldexpf(1.0f, -shift);
+  return launch<EPI_ROW_ENCODE>(q, w, m, n, k, a, (cudaStream_t)stream);
+}
+
+extern "C" int h3_int8_gemm_row_dequant(const int8_t* q, const int8_t* w, int64_t m, int64_t n,
+                                        int64_t k, const float* row_scale,
+                                        const float* weight_scale, int out_kind, void* out,
+                                        void* residual_f16, const float* gate, int64_t gate_rows,
+                                        const int32_t* labels, void* stream) {
+  if (row_scale == nullptr || weight_scale == nullptr) return H3_ERR_INVALID;
+  if (out_kind == H3_OUT_RESIDUAL) {
+    if (residual_f16 == nullptr) return H3_ERR_INVALID;
+    if (gate != nullptr && (gate_rows < 1 || (labels == nullptr && gate_rows != 1)))
+      return H3_ERR_INVALID;
+  } else if (out_kind == H3_OUT_F32 || out_kind == H3_OUT_F16) {
+    if (out == nullptr || !h3host::aligned(out, 16)) return H3_ERR_INVALID;
+  } else {
+    return H3_ERR_INVALID;
+  }
+  Args a = blank_args();
+  a.row_scale = row_scale;
+  a.weight_scale = weight_scale;
+  a.row = RowOut{out_kind, out, reinterpret_cast<__half*>(residual_f16), gate, gate_rows, labels,
+                 nullptr};
+  return launch<EPI_ROW_DEQUANT>(q, w, m, n, k, a, (cudaStream_t)stream);
+}

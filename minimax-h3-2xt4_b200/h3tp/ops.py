@@ -1,0 +1,309 @@
+"""torch front end of the C ABI: validates tensors, allocates outputs on the input's
+device, and enqueues the sm_100a kernels on the current CUDA stream.
+
+Every function here launches native kernels; none has a CPU path.  Scales follow
+the reference's shapes: activation scales [M, 1] fp32, weight scales [N, 1] fp32.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native as N
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _need(t: torch.Tensor, dtype, name: str, ndim: int | None = None) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{name}: CUDA tensor required (the INT8 path has no CPU fallback)")
+    if t.dtype != dtype:
+        raise ValueError(f"{name}: {dtype} required, got {t.dtype}")
+    if ndim is not None and t.ndim != ndim:
+        raise ValueError(f"{name}: {ndim}-D tensor required")
+    return t.contiguous()
+
+
+def _vec(t: torch.Tensor, n: int, name: str) -> torch.Tensor:
+    t = _need(t, torch.float32, name)
+    if t.numel() != n:
+        raise ValueError(f"{name}: {n} values required, got {t.numel()}")
+    return t.reshape(-1)
+
+
+INPUT_KINDS = {"gateup_f16": N.IN_GATEUP_F16, "act_f32": N.IN_ACT_F32, "act_f16": N.IN_ACT_F16}
+DIVISIONS = {"rn": N.DIV_RN, "fast": N.DIV_FAST}
+
+
+def _producer_input(x: torch.Tensor, kind: str):
+    k = INPUT_KINDS[kind]
+    x = _need(x, torch.float32 if k == N.IN_ACT_F32 else torch.float16, "x", 2)
+    width = x.shape[1] // 2 if k == N.IN_GATEUP_F16 else x.shape[1]
+    return x, k, x.shape[0], width
+
+
+# ----------------------------------------------------------------------------
+# column path
+# ----------------------------------------------------------------------------
+def column_quantize(x: torch.Tensor, convrot: bool = True):
+    """Rotation (optional) + per-row INT8 quantisation of the column input.
+    Returns (q int8 [M, K], scale fp32 [M, 1])."""
+    x = _need(x, torch.float16, "x", 2)
+    M, K = x.shape
+    q = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    s = torch.empty((M, 1), dtype=torch.float32, device=x.device)
+    N.call("h3_column_quantize", x.data_ptr(), M, K, int(bool(convrot)), q.data_ptr(),
+           s.data_ptr(), _stream(x))
+    return q, s
+
+
+def int8_gemm_i32(q: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """Exact INT32 q @ w.T on the tensor cores (tcgen05 kind::i8)."""
+    q = _need(q, torch.int8, "q", 2)
+    w = _need(w, torch.int8, "weight", 2)
+    M, K = q.shape
+    if w.shape[1] != K:
+        raise ValueError("Input and weight inner dimensions must match")
+    out = torch.empty((M, w.shape[0]), dtype=torch.int32, device=q.device)
+    N.call("h3_int8_gemm_i32", q.data_ptr(), w.data_ptr(), M, w.shape[0], K, out.data_ptr(),
+           _stream(q))
+    return out
+
+
+def int8_gemm_column(q, w, row_scale, weight_scale, bias=None) -> torch.Tensor:
+    """INT8 GEMM + ordered column epilogue, fp16 [M, N]."""
+    q = _need(q, torch.int8, "q", 2)
+    w = _need(w, torch.int8, "weight", 2)
+    M, K = q.shape
+    Nn = w.shape[0]
+    if w.shape[1] != K:
+        raise ValueError("Input and weight inner dimensions must match")
+    a = _vec(row_scale, M, "row_scale")
+    ws = _need(weight_scale, torch.float32, "weight_scale").reshape(-1)
+    if ws.numel() not in (1, Nn):
+        raise ValueError("INT8 weight scale must be scalar or per-output-channel")
+    b = None if bias is None else _vec(bias, Nn, "bias")
+    out = torch.empty((M, Nn), dtype=torch.float16, device=q.device)
+    N.call("h3_int8_gemm_column", q.data_ptr(), w.data_ptr(), M, Nn, K, a.data_ptr(),
+           ws.data_ptr(), ws.numel(), _ptr(b), out.data_ptr(), _stream(q))
+    return out
+
+
+def int8_gemm_swiglu(q, w, row_scale, weight_scale, bias=None, out_dtype=torch.float32):
+    """FC1 GEMM with the FP32 SwiGLU epilogue; w is [gate_r | up_r]; output
+    [M, w.shape[0] // 2] in out_dtype (fp32 keeps the reference's bits)."""
+    q = _need(q, torch.int8, "q", 2)
+    w = _need(w, torch.int8, "weight", 2)
+    M, K = q.shape
+    Np = w.shape[0]
+    if w.shape[1] != K or Np % 2:
+        raise ValueError("SwiGLU weight must be [2*n, K] with matching K")
+    a = _vec(row_scale, M, "row_scale")
+    ws = _vec(weight_scale, Np, "weight_scale")
+    b = None if bias is None else _vec(bias, Np, "bias")
+    kind = {torch.float32: N.OUT_F32, torch.float16: N.OUT_F16}[out_dtype]
+    out = torch.empty((M, Np // 2), dtype=out_dtype, device=q.device)
+    N.call("h3_int8_gemm_swiglu", q.data_ptr(), w.data_ptr(), M, Np, K, a.data_ptr(),
+           ws.data_ptr(), _ptr(b), kind, out.data_ptr(), _stream(q))
+    return out
+
+
+def column_dequantize(acc, row_scale, weight_scale) -> torch.Tensor:
+    """tilelang_column_epilogue.dequantize: f16(C * (A * W))."""
+    acc = _need(acc, torch.int32, "accumulator", 2)
+    M, Nn = acc.shape
+    a = _vec(row_scale, M, "row_scale")
+    ws = _need(weight_scale, torch.float32, "weight_scale").reshape(-1)
+    if ws.numel() not in (1, Nn):
+        raise ValueError("Scalar or channel scale required")
+    out = torch.empty((M, Nn), dtype=torch.float16, device=acc.device)
+    N.call("h3_column_dequantize", acc.data_ptr(), M, Nn, a.data_ptr(), ws.data_ptr(),
+           ws.numel(), out.data_ptr(), _stream(acc))
+    return out
+
+
+# ----------------------------------------------------------------------------
+# FC2 producer
+# ----------------------------------------------------------------------------
+def swiglu_rotate_max(x, kind="gateup_f16", store=True):
+    """Phase 'stored' (store=True) or 'maximum'.  Returns (rotated fp32 or None,
+    row_max fp32 [M, 1])."""
+    x, k, M, W = _producer_input(x, kind)
+    rot = torch.empty((M, W), dtype=torch.float32, device=x.device) if store else None
+    m = torch.empty((M, 1), dtype=torch.float32, device=x.device)
+    N.call("h3_swiglu_rotate_max", x.data_ptr(), k, M, W, _ptr(rot), m.data_ptr(), _stream(x))
+    return rot, m
+
+
+def swiglu_rotate_quantize(x, row_max, kind="gateup_f16", division="rn"):
+    """Phase 'recompute': codes of the rotated activation under the reduced row max."""
+    x, k, M, W = _producer_input(x, kind)
+    m = _vec(row_max, M, "row_max")
+    q = torch.empty((M, W), dtype=torch.int8, device=x.device)
+    s = torch.empty((M, 1), dtype=torch.float32, device=x.device)
+    N.call("h3_swiglu_rotate_quantize", x.data_ptr(), k, M, W, m.data_ptr(),
+           DIVISIONS[division], q.data_ptr(), s.data_ptr(), _stream(x))
+    return q, s
+
+
+def swiglu_rotate_quantize_local(x, kind="gateup_f16", division="rn"):
+    """TP=1 single pass.  Returns (q, scale [M, 1], row_max [M, 1])."""
+    x, k, M, W = _producer_input(x, kind)
+    q = torch.empty((M, W), dtype=torch.int8, device=x.device)
+    s = torch.empty((M, 1), dtype=torch.float32, device=x.device)
+    m = torch.empty((M, 1), dtype=torch.float32, device=x.device)
+    N.call("h3_swiglu_rotate_quantize_local", x.data_ptr(), k, M, W, DIVISIONS[division],
+           q.data_ptr(), s.data_ptr(), m.data_ptr(), _stream(x))
+    return q, s, m
+
+
+def row_quantize(rotated, row_max, width=None, start=0, division="rn"):
+    """tilelang_row_quant.quantize: codes of rotated[:, start:start+width]."""
+    rotated = _need(rotated, torch.float32, "rotated", 2)
+    M, stride = rotated.shape
+    width = stride - start if width is None else int(width)
+    m = _vec(row_max, M, "row_max")
+    q = torch.empty((M, width), dtype=torch.int8, device=rotated.device)
+    s = torch.empty((M, 1), dtype=torch.float32, device=rotated.device)
+    N.call("h3_row_quantize", rotated.data_ptr(), M, width, stride, int(start), m.data_ptr(),
+           DIVISIONS[division], q.data_ptr(), s.data_ptr(), _stream(rotated))
+    return q, s
+
+
+# ----------------------------------------------------------------------------
+# row path
+# ----------------------------------------------------------------------------
+def transport_shift(full_k: int) -> int:
+    return int(N.load().h3_transport_shift(int(full_k)))
+
+
+def int8_gemm_row_encode(q, w, shift: int) -> torch.Tensor:
+    """INT8 GEMM + scaled-FP16 encode: f16(acc * 2^-shift), [M, N]."""
+    q = _need(q, torch.int8, "q", 2)
+    w = _need(w, torch.int8, "weight", 2)
+    M, K = q.shape
+    if w.shape[1] != K:
+        raise ValueError("Input and weight inner dimensions must match")
+    out = torch.empty((M, w.shape[0]), dtype=torch.float16, device=q.device)
+    N.call("h3_int8_gemm_row_encode", q.data_ptr(), w.data_ptr(), M, w.shape[0], K, int(shift),
+           out.data_ptr(), _stream(q))
+    return out
+
+
+def _gate_args(residual, gate, labels, M, Nn):
+    if residual is None:
+        return None, None, 0, None
+    residual = _need(residual, torch.float16, "residual", 2)
+    if residual.shape != (M, Nn):
+        raise ValueError("residual shape mismatch")
+    if gate is None:
+        return residual, None, 0, None
+    gate = _need(gate, torch.float32, "gate", 2)
+    if gate.shape[1] != Nn:
+        raise ValueError("gate table width mismatch")
+    lab = None
+    if labels is not None:
+        lab = _need(labels, torch.int32, "labels", 1)
+        if lab.numel() != M:
+            raise ValueError("one label per row required")
+    elif gate.shape[0] != 1:
+        raise ValueError("labels required for a multi-row gate table")
+    return residual, gate, gate.shape[0], lab
+
+
+def int8_gemm_row_dequant(q, w, row_scale, weight_scale, out_dtype=torch.float32,
+                          residual=None, gate=None, labels=None):
+    """TP=1 row GEMM, exact INT32 + fused dequant.  With `residual` the gated residual
+    is updated in place and returned; otherwise a new [M, N] tensor in out_dtype."""
+    q = _need(q, torch.int8, "q", 2)
+    w = _need(w, torch.int8, "weight", 2)
+    M, K = q.shape
+    Nn = w.shape[0]
+    if w.shape[1] != K:
+        raise ValueError("Input and weight inner dimensions must match")
+    a = _vec(row_scale, M, "row_scale")
+    ws = _vec(weight_scale, Nn, "weight_scale")
+    if residual is not None:
+        if not residual.is_contiguous():
+            raise ValueError("residual must be contiguous (updated in place)")
+        res, g, grows, lab = _gate_args(residual, gate, labels, M, Nn)
+        N.call("h3_int8_gemm_row_dequant", q.data_ptr(), w.data_ptr(), M, Nn, K, a.data_ptr(),
+               ws.data_ptr(), N.OUT_RESIDUAL, None, res.data_ptr(), _ptr(g), grows, _ptr(lab),
+               _stream(q))
+        return residual
+    kind = {torch.float32: N.OUT_F32, torch.float16: N.OUT_F16}[out_dtype]
+    out = torch.empty((M, Nn), dtype=out_dtype, device=q.device)
+    N.call("h3_int8_gemm_row_dequant", q.data_ptr(), w.data_ptr(), M, Nn, K, a.data_ptr(),
+           ws.data_ptr(), kind, out.data_ptr(), None, None, 0, None, _stream(q))
+    return out
+
+
+def fp16_encode(partial: torch.Tensor, shift: int) -> torch.Tensor:
+    p = _need(partial, torch.int32, "partial")
+    out = torch.empty(p.shape, dtype=torch.float16, device=p.device)
+    N.call("h3_fp16_encode", p.data_ptr(), p.numel(), int(shift), out.data_ptr(), _stream(p))
+    return out
+
+
+def fp16_decode(payload: torch.Tensor, shift: int) -> torch.Tensor:
+    y = _need(payload, torch.float16, "payload")
+    out = torch.empty(y.shape, dtype=torch.int32, device=y.device)
+    N.call("h3_fp16_decode", y.data_ptr(), y.numel(), int(shift), out.data_ptr(), _stream(y))
+    return out
+
+
+def row_reduce_finish(parts, shift, row_scale, weight_scale, out_dtype=torch.float32,
+                      residual=None, gate=None, labels=None):
+    """parts: fp16 [world, rows, N] (or [rows, N] for an already reduced payload).
+    Fixed-order fp32 sum + one fp16 rounding, decode, dequant, then store or gated
+    residual update (residual updated in place and returned)."""
+    parts = _need(parts, torch.float16, "parts")
+    if parts.ndim == 2:
+        parts = parts.unsqueeze(0)
+    world, M, Nn = parts.shape
+    a = _vec(row_scale, M, "row_scale")
+    ws = _vec(weight_scale, Nn, "weight_scale")
+    if residual is not None:
+        if not residual.is_contiguous():
+            raise ValueError("residual must be contiguous (updated in place)")
+        res, g, grows, lab = _gate_args(residual, gate, labels, M, Nn)
+        N.call("h3_row_reduce_finish", parts.data_ptr(), world, M * Nn, M, Nn, int(shift),
+               a.data_ptr(), ws.data_ptr(), N.OUT_RESIDUAL, None, res.data_ptr(), _ptr(g),
+               grows, _ptr(lab), _stream(parts))
+        return residual
+    kind = {torch.float32: N.OUT_F32, torch.float16: N.OUT_F16}[out_dtype]
+    out = torch.empty((M, Nn), dtype=out_dtype, device=parts.device)
+    N.call("h3_row_reduce_finish", parts.data_ptr(), world, M * Nn, M, Nn, int(shift),
+           a.data_ptr(), ws.data_ptr(), kind, out.data_ptr(), None, None, 0, None,
+           _stream(parts))
+    return out
+
+
+def dequantize_i32(acc, row_scale, weight_scale, out_dtype=torch.float32, bias=None):
+    """parallel_int8.dequantize order: ((acc * a) * w) + bias."""
+    acc = _need(acc, torch.int32, "accumulator", 2)
+    M, Nn = acc.shape
+    a = _vec(row_scale, M, "activation_scale")
+    ws = _need(weight_scale, torch.float32, "weight_scale").reshape(-1)
+    if ws.numel() not in (1, Nn):
+        raise ValueError("INT8 weight scale must be scalar or per-output-channel")
+    b = None if bias is None else _vec(bias, Nn, "bias")
+    kind = {torch.float32: N.OUT_F32, torch.float16: N.OUT_F16}[out_dtype]
+    out = torch.empty((M, Nn), dtype=out_dtype, device=acc.device)
+    N.call("h3_dequantize_i32", acc.data_ptr(), M, Nn, a.data_ptr(), ws.data_ptr(), ws.numel(),
+           _ptr(b), kind, out.data_ptr(), _stream(acc))
+    return out
+
+
+def expf_compare(x: torch.Tensor):
+    """(h3_expf(x), CUDA expf(x)) evaluated on the device."""
+    x = _need(x, torch.float32, "x")
+    ours = torch.empty_like(x)
+    ref = torch.empty_like(x)
+    N.call("h3_expf_compare", x.data_ptr(), x.numel(), ours.data_ptr(), ref.data_ptr(), _stream(x))
+    return ours, ref

@@ -1,0 +1,315 @@
+"""Kernel-level parity of libh3b200.so against the CPU oracle (bit-exact).
+
+Each test drives one C-ABI entry point through h3tp.ops on seeded inputs and compares
+every output bit with the oracle's restatement of the reference arithmetic:
+  - INT8 codes, INT32 accumulators and row scales: exact equality;
+  - fp16/fp32 epilogue outputs: exact equality too (the kernels follow the
+    reference's rounding order operation by operation).
+Shapes include ragged M/N tails, K at the 16-byte minimum and widths that are single
+or many ConvRot groups.
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _np(t):
+    return t.detach().cpu().numpy()
+
+
+def _gateup(rng, rows, width, heavy=True):
+    g = rng.standard_normal((rows, width)).astype(np.float32)
+    u = rng.standard_normal((rows, width)).astype(np.float32)
+    if heavy:
+        g[::7] *= rng.standard_t(3, size=(len(g[::7]), width)).astype(np.float32)
+        g[0, 0] = 1000.0  # reference outlier pattern (preview_fp32_swiglu_fusion.py:15)
+        u[0, min(512, width - 1)] = 1000.0
+    return np.concatenate([g, u], 1).astype(np.float16)
+
+
+def _bits_equal(a, b):
+    a = np.ascontiguousarray(a)
+    b = np.ascontiguousarray(b)
+    assert a.shape == b.shape and a.dtype == b.dtype, (a.shape, b.shape, a.dtype, b.dtype)
+    va = a.view(np.uint8 if a.itemsize == 1 else {2: np.uint16, 4: np.uint32}[a.itemsize])
+    vb = b.view(va.dtype)
+    bad = np.flatnonzero(va != vb)
+    assert bad.size == 0, f"{bad.size} of {a.size} differ; first at {np.unravel_index(bad[0], a.shape)}: {a.flat[bad[0]]} vs {b.flat[bad[0]]}"
+
+
+# ----------------------------------------------------------------------------
+# exponential
+# ----------------------------------------------------------------------------
+def test_expf_matches_oracle_on_all_fp16_inputs(cuda_device, oracle):
+    from h3tp import ops
+    h = np.arange(65536, dtype=np.uint32).astype(np.uint16).view(np.float16).astype(np.float32)
+    h = h[np.isfinite(h)]
+    rng = np.random.default_rng(0)
+    extra = np.concatenate([rng.uniform(-110, 95, 200000), rng.standard_normal(100000) * 4]).astype(np.float32)
+    x = np.concatenate([-h, extra]).astype(np.float32)
+    ours, cuda = ops.expf_compare(_t(x, cuda_device))
+    _bits_equal(_np(ours), oracle.expf(x))
+
+
+# ----------------------------------------------------------------------------
+# FC2 producer
+# ----------------------------------------------------------------------------
+@pytest.mark.parametrize("rows,width", [(1, 256), (17, 512), (33, 1024), (5, 7168), (3, 8192), (2, 24576)])
+@pytest.mark.parametrize("kind", ["gateup_f16", "act_f32", "act_f16"])
+def test_fc2_producer_bit_exact(cuda_device, oracle, rows, width, kind):
+    from h3tp import ops
+    rng = np.random.default_rng(rows * 131 + width)
+    if kind == "gateup_f16":
+        x = _gateup(rng, rows, width)
+    elif kind == "act_f32":
+        x = (rng.standard_normal((rows, width)) * 0.7).astype(np.float32)
+    else:
+        x = (rng.standard_normal((rows, width)) * 0.7).astype(np.float16)
+    R_ref, m_ref = oracle.fc2_rotate(x, kind)
+    xd = _t(x, cuda_device)
+    rot, m = ops.swiglu_rotate_max(xd, kind, store=True)
+    _bits_equal(_np(rot), R_ref)
+    _bits_equal(_np(m).ravel(), m_ref)
+    rot2, m2 = ops.swiglu_rotate_max(xd, kind, store=False)
+    assert rot2 is None
+    _bits_equal(_np(m2).ravel(), m_ref)
+    # global max across two emulated ranks: scale the maximum up for half the rows
+    gmax = m_ref.copy()
+    gmax[::2] *= 1.5
+    q_ref, s_ref = oracle.row_quantize(R_ref, gmax)
+    q, s = ops.swiglu_rotate_quantize(xd, _t(gmax, cuda_device), kind)
+    _bits_equal(_np(q), q_ref)
+    _bits_equal(_np(s).ravel(), s_ref)
+    q3, s3 = ops.row_quantize(rot, _t(gmax, cuda_device))
+    _bits_equal(_np(q3), q_ref)
+    _bits_equal(_np(s3).ravel(), s_ref)
+    ql_ref, sl_ref = oracle.row_quantize(R_ref, m_ref)
+    ql, sl, ml = ops.swiglu_rotate_quantize_local(xd, kind)
+    _bits_equal(_np(ql), ql_ref)
+    _bits_equal(_np(sl).ravel(), sl_ref)
+    _bits_equal(_np(ml).ravel(), m_ref)
+
+
+def test_row_quantize_owned_slice(cuda_device, oracle):
+    from h3tp import ops
+    rng = np.random.default_rng(5)
+    X = rng.standard_normal((9, 1024)).astype(np.float32)
+    m = np.abs(X).max(1).astype(np.float32) * 1.25
+    q_ref, s_ref = oracle.row_quantize(X, m, start=256, width=512)
+    q, s = ops.row_quantize(_t(X, cuda_device), _t(m, cuda_device), width=512, start=256)
+    _bits_equal(_np(q), q_ref)
+    _bits_equal(_np(s).ravel(), s_ref)
+
+
+def test_fast_division_disagreement_is_small(cuda_device, oracle):
+    """The reference's production quantizer divides with __fdividef; the path uses
+    IEEE division (bit-exact with the oracle).  The fast variant must disagree on a
+    tiny fraction of codes, by one step at most."""
+    from h3tp import ops
+    rng = np.random.default_rng(11)
+    x = _gateup(rng, 64, 4096)
+    xd = _t(x, cuda_device)
+    q_rn, _, m = ops.swiglu_rotate_quantize_local(xd, "gateup_f16", "rn")
+    q_fast, _ = ops.swiglu_rotate_quantize(xd, m, "gateup_f16", "fast")
+    d = (_np(q_rn).astype(np.int32) - _np(q_fast).astype(np.int32))
+    assert np.abs(d).max() <= 1
+    assert np.count_nonzero(d) / d.size < 1e-3
+
+
+# ----------------------------------------------------------------------------
+# column activation quantizer
+# ----------------------------------------------------------------------------
+@pytest.mark.parametrize("rows,k,convrot", [(1, 256, True), (19, 3072, True), (7, 5120, True),
+                                            (4, 16384, True), (19, 3072, False), (3, 48, False)])
+def test_column_quantize_bit_exact(cuda_device, oracle, rows, k, convrot):
+    from h3tp import ops
+    rng = np.random.default_rng(rows + k)
+    x = rng.standard_normal((rows, k)).astype(np.float32)
+    cols = rng.permutation(k)[: max(1, k // 100)]
+    x[:, cols] *= 20.0  # 1% outlier columns
+    x = x.astype(np.float16)
+    q_ref, s_ref = oracle.column_quantize(x, convrot)
+    q, s = ops.column_quantize(_t(x, cuda_device), convrot)
+    _bits_equal(_np(q), q_ref)
+    _bits_equal(_np(s).ravel(), s_ref)
+
+
+# ----------------------------------------------------------------------------
+# tcgen05 INT8 GEMM + fused epilogues
+# ----------------------------------------------------------------------------
+GEMM_SHAPES = [(1, 256, 128), (17, 200, 16), (128, 256, 256), (300, 512, 3072),
+               (129, 384, 1040), (256, 1024, 8192), (64, 3072, 1024)]
+
+
+def _operands(rng, M, N, K):
+    A = rng.integers(-128, 128, size=(M, K), dtype=np.int8)
+    W = rng.integers(-127, 128, size=(N, K), dtype=np.int8)
+    return A, W
+
+
+@pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
+def test_gemm_i32_exact(cuda_device, oracle, M, N, K):
+    from h3tp import ops
+    rng = np.random.default_rng(M * 7 + N * 3 + K)
+    A, W = _operands(rng, M, N, K)
+    C = ops.int8_gemm_i32(_t(A, cuda_device), _t(W, cuda_device))
+    _bits_equal(_np(C), oracle.int8_gemm(A, W))
+
+
+def test_gemm_i32_extremes(cuda_device, oracle):
+    """Saturating operands: every product -128*-127 or 127*127 (largest sums)."""
+    from h3tp import ops
+    M, N, K = 130, 260, 8192
+    A = np.full((M, K), -128, np.int8)
+    A[1::2] = 127
+    W = np.full((N, K), -127, np.int8)
+    W[::3] = 127
+    C = ops.int8_gemm_i32(_t(A, cuda_device), _t(W, cuda_device))
+    _bits_equal(_np(C), oracle.int8_gemm(A, W))
+
+
+@pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
+@pytest.mark.parametrize("bias", [False, True])
+def test_gemm_column_bit_exact(cuda_device, oracle, M, N, K, bias):
+    from h3tp import ops
+    rng = np.random.default_rng(M + N + K + bias)
+    A, W = _operands(rng, M, N, K)
+    a = rng.uniform(1e-3, 5e-2, M).astype(np.float32)
+    w = rng.uniform(1e-3, 1e-2, N).astype(np.float32)
+    b = (rng.standard_normal(N) * 0.02).astype(np.float32) if bias else None
+    y = ops.int8_gemm_column(_t(A, cuda_device), _t(W, cuda_device), _t(a, cuda_device),
+                             _t(w, cuda_device), None if b is None else _t(b, cuda_device))
+    _bits_equal(_np(y), oracle.column_epilogue(oracle.int8_gemm(A, W), a, w, b))
+
+
+def test_gemm_column_scalar_weight_scale(cuda_device, oracle):
+    from h3tp import ops
+    rng = np.random.default_rng(3)
+    A, W = _operands(rng, 40, 96, 64)
+    a = rng.uniform(1e-3, 5e-2, 40).astype(np.float32)
+    w = np.array([0.004], np.float32)
+    y = ops.int8_gemm_column(_t(A, cuda_device), _t(W, cuda_device), _t(a, cuda_device), _t(w, cuda_device))
+    _bits_equal(_np(y), oracle.column_epilogue(oracle.int8_gemm(A, W), a, w))
+
+
+@pytest.mark.parametrize("M,Nh,K", [(1, 128, 128), (33, 96, 256), (300, 256, 3072), (129, 384, 1024)])
+@pytest.mark.parametrize("out", ["f32", "f16"])
+@pytest.mark.parametrize("bias", [False, True])
+def test_gemm_swiglu_bit_exact(cuda_device, oracle, M, Nh, K, out, bias):
+    from h3tp import ops
+    rng = np.random.default_rng(M + Nh + K)
+    A, W = _operands(rng, M, 2 * Nh, K)
+    a = rng.uniform(1e-3, 5e-2, M).astype(np.float32)
+    w = rng.uniform(1e-3, 1e-2, 2 * Nh).astype(np.float32)
+    b = (rng.standard_normal(2 * Nh) * 0.02).astype(np.float32) if bias else None
+    y = ops.int8_gemm_swiglu(_t(A, cuda_device), _t(W, cuda_device), _t(a, cuda_device),
+                             _t(w, cuda_device), None if b is None else _t(b, cuda_device),
+                             torch.float32 if out == "f32" else torch.float16)
+    _bits_equal(_np(y), oracle.swiglu_epilogue(oracle.int8_gemm(A, W), a, w, b, out))
+
+
+@pytest.mark.parametrize("M,N,K", [(17, 256, 7168), (300, 512, 1024), (5, 200, 2048)])
+def test_gemm_row_encode_bit_exact(cuda_device, oracle, M, N, K):
+    from h3tp import ops
+    rng = np.random.default_rng(M + N)
+    A, W = _operands(rng, M, N, K)
+    shift = oracle.transport_shift(2 * K)
+    y = ops.int8_gemm_row_encode(_t(A, cuda_device), _t(W, cuda_device), shift)
+    _bits_equal(_np(y), oracle.fp16_encode(oracle.int8_gemm(A, W), shift))
+
+
+@pytest.mark.parametrize("out", ["f32", "f16", "residual", "residual_nogate"])
+def test_gemm_row_dequant_bit_exact(cuda_device, oracle, out):
+    from h3tp import ops
+    M, N, K = 150, 384, 2048
+    rng = np.random.default_rng(21)
+    A, W = _operands(rng, M, N, K)
+    a = rng.uniform(1e-3, 5e-2, M).astype(np.float32)
+    w = (rng.uniform(1e-3, 1e-2, N) / 512).astype(np.float32)
+    C = oracle.int8_gemm(A, W)
+    Ad, Wd, ad, wd = (_t(v, cuda_device) for v in (A, W, a, w))
+    if out in ("f32", "f16"):
+        y = ops.int8_gemm_row_dequant(Ad, Wd, ad, wd, torch.float32 if out == "f32" else torch.float16)
+        _bits_equal(_np(y), oracle.dequantize_i32(C, a, w, out=out))
+        return
+    X = rng.standard_normal((M, N)).astype(np.float16)
+    gate = labels = None
+    if out == "residual":
+        gate = rng.standard_normal((9, N)).astype(np.float32)
+        labels = rng.integers(0, 9, M).astype(np.int32)
+    Xd = _t(X, cuda_device)
+    ops.int8_gemm_row_dequant(Ad, Wd, ad, wd, residual=Xd,
+                              gate=None if gate is None else _t(gate, cuda_device),
+                              labels=None if labels is None else _t(labels, cuda_device))
+    ref = X.copy()
+    oracle.dequantize_i32(C, a, w, out="residual", residual=ref, gate=gate, labels=labels)
+    _bits_equal(_np(Xd), ref)
+
+
+# ----------------------------------------------------------------------------
+# transport codec and reduction epilogue
+# ----------------------------------------------------------------------------
+def test_fp16_codec_bit_exact(cuda_device, oracle):
+    from h3tp import ops
+    rng = np.random.default_rng(744)
+    P = rng.integers(-10_000_000, 10_000_000, size=(17, 256), dtype=np.int32)
+    P[0, :8] = [16777217, -8388609, 1, -1, 65535, -65535, 127, 0]
+    for shift in (0, 10, 11, 12):
+        y = ops.fp16_encode(_t(P, cuda_device), shift)
+        _bits_equal(_np(y), oracle.fp16_encode(P, shift))
+        back = ops.fp16_decode(y, shift)
+        _bits_equal(_np(back), oracle.fp16_decode(_np(y), shift))
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("out", ["f32", "f16", "residual"])
+def test_row_reduce_finish_bit_exact(cuda_device, oracle, world, out):
+    from h3tp import ops
+    rng = np.random.default_rng(world * 10 + len(out))
+    rows, width = 37, 264
+    shift = oracle.transport_shift(world * 1024)
+    parts = rng.standard_normal((world, rows, width)).astype(np.float16) * np.float16(100)
+    a = rng.uniform(1e-3, 5e-2, rows).astype(np.float32)
+    w = rng.uniform(1e-6, 1e-5, width).astype(np.float32)
+    pd = _t(parts, cuda_device)
+    if out != "residual":
+        y = ops.row_reduce_finish(pd, shift, _t(a, cuda_device), _t(w, cuda_device),
+                                  torch.float32 if out == "f32" else torch.float16)
+        _bits_equal(_np(y), oracle.row_reduce_finish(parts, shift, a, w, out=out))
+        return
+    X = rng.standard_normal((rows, width)).astype(np.float16)
+    gate = rng.standard_normal((3, width)).astype(np.float32)
+    labels = (np.arange(rows) % 3).astype(np.int32)
+    Xd = _t(X, cuda_device)
+    ops.row_reduce_finish(pd, shift, _t(a, cuda_device), _t(w, cuda_device), residual=Xd,
+                          gate=_t(gate, cuda_device), labels=_t(labels, cuda_device))
+    ref = X.copy()
+    oracle.row_reduce_finish(parts, shift, a, w, out="residual", residual=ref, gate=gate, labels=labels)
+    _bits_equal(_np(Xd), ref)
+
+
+def test_column_and_int32_dequantize(cuda_device, oracle):
+    from h3tp import ops
+    rng = np.random.default_rng(9)
+    C = rng.integers(-2**26, 2**26, size=(23, 129), dtype=np.int32)
+    a = rng.uniform(1e-3, 5e-2, 23).astype(np.float32)
+    w = rng.uniform(1e-3, 1e-2, 129).astype(np.float32)
+    b = rng.standard_normal(129).astype(np.float32)
+    Cd, ad, wd, bd = (_t(v, cuda_device) for v in (C, a, w, b))
+    _bits_equal(_np(ops.column_dequantize(Cd, ad, wd)), oracle.column_epilogue(C, a, w))
+    _bits_equal(_np(ops.dequantize_i32(Cd, ad, wd, torch.float32, bd)),
+                oracle.dequantize_i32(C, a, w, bias=b, out="f32"))
+    _bits_equal(_np(ops.dequantize_i32(Cd, ad, wd, torch.float16)),
+                oracle.dequantize_i32(C, a, w, out="f16"))
+
+
+def test_no_device_error_after_suite(cuda_device):
+    from h3tp import _native
+    torch.cuda.synchronize()
+    assert _native.device_error(0) == 0
