@@ -1,0 +1,406 @@
+"""Benchmark of the B200 tensor-parallel INT8 linear path: the DiT MLP block.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (TP = N)
+
+Workload (MLP part, M = 32768 tokens, hidden 3072, MLP 8192):
+one step is FC1 (ColumnParallel, [gate|up]) -> FP32 SwiGLU -> ConvRot256 -> global
+per-row INT8 quant -> FC2 (RowParallel) -> partial-sum reduction -> fp16 residual add,
+i.e. TPDiTMLPINT8.forward, on seeded synthetic inputs and random-init INT8 weights of
+that shape (no checkpoint or dataset is involved).
+
+value: whole-job INT8 TOPS = 2*M*(2*ffn*hidden + hidden*ffn) / device time per block
+       (max over ranks, CUDA events, inputs resident in HBM; h alone is 201 MB, larger
+       than the 126 MB L2, so no flush is needed between steps).
+e2e:   the same through the public module API with the step's inputs (h, residual)
+       copied host->device from pinned memory and the updated residual copied back,
+       inside the timed region.
+roofline: the dominant kernel (the FC1 tcgen05 GEMM with the SwiGLU epilogue) timed
+       with CUDA events inside the timed steps, against the INT8 tensor peak.
+cpu_baseline / --impl reference: the reference's CPU path (torch._int_mm, the CPU
+       INT32 GEMM of patches/parallel_int8.int_mm, plus the oracle's C restatement of
+       the rotation / quantisation / epilogues) on a bounded row sample, host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "minimax-h3-2xt4_b200"))
+
+METRIC = "INT8 TOPS/GPU and µs per DiT MLP block at M=32k, TP 1/2/4/8; % of INT8 TC peak"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=32768)
+    ap.add_argument("--hidden", type=int, default=3072)
+    ap.add_argument("--ffn", type=int, default=8192)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def block_ops(M, hidden, ffn):
+    return 2 * M * (2 * ffn) * hidden + 2 * M * hidden * ffn
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d.get("hbm_gbs", 6650.0), "bf16": d.get("bf16_tflops", 1590.0),
+                "bf16_sustained": d.get("bf16_tflops_sustained", 1400.0), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+# ----------------------------------------------------------------------------
+# synthetic workload (identical bytes on every rank: generated on the CPU)
+# ----------------------------------------------------------------------------
+def make_weights(hidden, ffn, seed=0):
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    w1 = torch.randint(-127, 128, (2 * ffn, hidden), generator=g, dtype=torch.int8)
+    s1 = (torch.rand((2 * ffn, 1), generator=g) * 9e-3 + 1e-3).float()
+    w2 = torch.randint(-127, 128, (hidden, ffn), generator=g, dtype=torch.int8)
+    s2 = ((torch.rand((hidden, 1), generator=g) * 9e-3 + 1e-3) / 512).float()  # /512 fold
+    return w1, s1, w2, s2
+
+
+def make_inputs(M, hidden, seed=1):
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    h = torch.randn((M, hidden), generator=g)
+    cols = torch.randperm(hidden, generator=g)[: max(1, hidden // 100)]
+    h[:, cols] *= 20.0  # 1% outlier columns
+    x = torch.randn((M, hidden), generator=g) * 0.25
+    return h.half(), x.half()
+
+
+# ----------------------------------------------------------------------------
+# clocks
+# ----------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.QUERY,
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            f = [v.strip() for v in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------
+# CPU baseline (the reference's CPU path on host cores; oracle = checker code)
+# ----------------------------------------------------------------------------
+def cpu_block_sample(rows, w1, s1, w2, s2, h, x, threads):
+    """One MLP block over `rows` rows on the CPU in the reference's order; returns
+    (seconds, ops)."""
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+    torch.set_num_threads(threads)
+    hs = h[:rows].numpy()
+    t0 = time.perf_counter()
+    q, a = O.column_quantize(hs, True)
+    C1 = torch._int_mm(torch.from_numpy(q), w1.t().contiguous()).numpy()  # parallel_int8.int_mm
+    act = O.swiglu_epilogue(C1, a, s1.numpy().ravel())
+    R, m = O.fc2_rotate(act, "act_f32")
+    q2, a2 = O.row_quantize(R, m)
+    C2 = torch._int_mm(torch.from_numpy(q2), w2.t().contiguous()).numpy()
+    res = x[:rows].numpy().copy()
+    O.dequantize_i32(C2, a2, s2.numpy().ravel(), out="residual", residual=res)
+    dt = time.perf_counter() - t0
+    return dt, block_ops(rows, w2.shape[0], w2.shape[1])
+
+
+def cpu_baseline(w1, s1, w2, s2, h, x, budget_s=12.0, rows=512):
+    threads = os.cpu_count() or 1
+    cpu_block_sample(64, w1, s1, w2, s2, h, x, threads)  # warm-up
+    total_t = total_ops = 0.0
+    n = 0
+    while total_t < budget_s and n < 200:
+        dt, ops = cpu_block_sample(rows, w1, s1, w2, s2, h, x, threads)
+        total_t += dt
+        total_ops += ops
+        n += 1
+    return {"value": round(total_ops / total_t / 1e12, 4), "unit": "TOPS", "cores": threads,
+            "kind": "port",
+            "sample": f"{n} x {rows}-row slices of the M=32768 MLP block "
+                      f"(oracle C rotation/quant/epilogues + torch._int_mm), {total_t:.1f} s"}
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path, one bounded row sample per step."""
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    w1, s1, w2, s2 = make_weights(args.hidden, args.ffn)
+    h, x = make_inputs(args.tokens, args.hidden)
+    rows = 512
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_block_sample(rows, w1, s1, w2, s2, h, x, threads)
+    times = []
+    for _ in range(args.steps):
+        dt, ops = cpu_block_sample(rows, w1, s1, w2, s2, h, x, threads)
+        times.append(dt)
+    total = sum(times)
+    ops_per_step = block_ops(rows, args.hidden, args.ffn)
+    value = ops_per_step * args.steps / total / 1e12
+    ms_full = total / args.steps * (args.tokens / rows) * 1e3
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": "TOPS", "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_full, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "dit_mlp_block", "M": args.tokens, "hidden": args.hidden,
+                   "ffn": args.ffn, "parallelism": "cpu", "sample_rows": rows},
+        "cpu_baseline": {"value": round(value, 4), "unit": "TOPS", "cores": threads, "kind": "port",
+                         "sample": f"{rows}-row slice of the M={args.tokens} MLP block per step"},
+        "e2e": {"value": round(value, 4), "unit": "TOPS", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------
+# GPU arm
+# ----------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    comm = None
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        comm = dist
+
+    from h3tp import _native, ops
+    from h3tp.tp_dit import TPDiTMLPINT8
+    from h3tp import dit_column_linear as col, swiglu_quant as sq
+
+    M, hidden, ffn = args.tokens, args.hidden, args.ffn
+    w1, s1, w2, s2 = make_weights(hidden, ffn)
+    h_cpu, x_cpu = make_inputs(M, hidden)
+    mlp = TPDiTMLPINT8(hidden, ffn, rank, world, device=dev, comm=comm)
+    mlp.fc1.load_shard_from_full(w1, s1)
+    mlp.fc2.load_shard_from_full(w2, s2)
+    h = h_cpu.to(dev)
+    x = x_cpu.to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    fc1_events = []
+
+    def step(record=False):
+        # TPDiTMLPINT8.forward, unrolled so the FC1 GEMM can be bracketed by events.
+        codes, row_scale = col._prepare_activation(h, True, 256)
+        if record:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        act = ops.int8_gemm_swiglu(codes, mlp.fc1.weight, row_scale,
+                                   mlp.fc1.weight_scale.reshape(-1), None, torch.float32)
+        if record:
+            e1.record(stream)
+            fc1_events.append((e0, e1))
+        sq.row_linear(act, mlp.fc2.weight, mlp.fc2.weight_scale, comm,
+                      mode=mlp.fc2.operator_policy.fc2_quantizer, scaled_transport=True,
+                      residual=x, transport=mlp.fc2.operator_policy.row_transport)
+
+    with torch.no_grad():
+        for _ in range(max(3, args.warmup)):
+            step()
+        torch.cuda.synchronize()
+        if comm:
+            dist.barrier()
+        calls0 = ops.launch_count()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clocks:
+            if comm:
+                dist.barrier()
+            torch.cuda.synchronize()
+            start.record(stream)
+            for _ in range(args.steps):
+                step(record=True)
+            end.record(stream)
+            torch.cuda.synchronize()
+            if comm:
+                dist.barrier()
+        launches = ops.launch_count() - calls0
+        elapsed_ms = start.elapsed_time(end)
+        fc1_ms = statistics.mean(a.elapsed_time(b) for a, b in fc1_events)
+        t = torch.tensor([elapsed_ms, fc1_ms], device=dev, dtype=torch.float64)
+        if comm:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms, fc1_ms = float(t[0]), float(t[1])
+        ms_per_step = elapsed_ms / args.steps
+
+        # e2e through the public module API with host buffers
+        e2e = None
+        if not args.no_e2e:
+            h_pin = h_cpu.pin_memory()
+            x_pin = x_cpu.pin_memory()
+            out_pin = torch.empty_like(x_cpu).pin_memory()
+            hd = torch.empty_like(h)
+            xd = torch.empty_like(x)
+
+            def e2e_step():
+                hd.copy_(h_pin, non_blocking=True)
+                xd.copy_(x_pin, non_blocking=True)
+                y = mlp(xd, hd)
+                out_pin.copy_(y, non_blocking=True)
+
+            for _ in range(2):
+                e2e_step()
+            torch.cuda.synchronize()
+            if comm:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            n_e2e = max(3, args.steps // 4)
+            for _ in range(n_e2e):
+                e2e_step()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            te = torch.tensor([e0.elapsed_time(e1) / n_e2e], device=dev, dtype=torch.float64)
+            if comm:
+                dist.all_reduce(te, op=dist.ReduceOp.MAX)
+            e2e_ms = float(te[0])
+            e2e = {"value": round(block_ops(M, hidden, ffn) / (e2e_ms * 1e-3) / 1e12, 3),
+                   "unit": "TOPS", "ms_per_step": round(e2e_ms, 4),
+                   "h2d_bytes_per_step": h_cpu.numel() * 2 + x_cpu.numel() * 2,
+                   "d2h_bytes_per_step": x_cpu.numel() * 2,
+                   "api": "TPDiTMLPINT8.forward (h3tp.tp_dit), pinned host buffers"}
+
+        err = _native.device_error(local)
+        if comm:
+            e = torch.tensor([err], device=dev)
+            dist.all_reduce(e, op=dist.ReduceOp.MAX)
+            err = int(e.item())
+
+    if comm:
+        dist.barrier()
+    total_ops = block_ops(M, hidden, ffn)
+    value = total_ops / (ms_per_step * 1e-3) / 1e12
+    pk = peaks()
+    int8_peak = 2.0 * pk["bf16"]
+    fc1_ops = 2 * M * (2 * ffn // world) * hidden
+    achieved = fc1_ops / (fc1_ms * 1e-3) / 1e12
+    traffic = None
+    tfile = ROOT / "profiles" / "roofline_traffic.json"
+    if tfile.exists():
+        try:
+            traffic = json.loads(tfile.read_text()).get(f"fc1_swiglu_gemm_tp{world}")
+        except ValueError:
+            traffic = None
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "TOPS", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "us_per_block": round(ms_per_step * 1e3, 1), "tops_per_gpu": round(value / world, 3),
+        "frac_of_int8_peak_per_gpu": round(value / world / int8_peak, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded N(0,1) input with 1% x20 outlier columns, random int8 weights)",
+        "config": {"workload": "dit_mlp_block", "M": M, "hidden": hidden, "ffn": ffn,
+                   "tp": world, "parallelism": f"tp{world}",
+                   "fc2_quantizer": mlp.fc2.operator_policy.fc2_quantizer,
+                   "row_transport": mlp.fc2.operator_policy.row_transport,
+                   "l2": "inputs larger than L2 (h = 201 MB per step), no flush"},
+        "roofline": {"kernel": "gemm_i8_kernel<EPI_SWIGLU> (FC1)", "bound": "tensor",
+                     "achieved": round(achieved, 2), "peak": round(int8_peak, 1), "unit": "TOPS",
+                     "frac": round(achieved / int8_peak, 4), "traffic": traffic,
+                     "ms_per_launch": round(fc1_ms, 4), "ops_per_launch": fc1_ops,
+                     "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({pk['source']}); "
+                                    "INT8 dense peak estimate"},
+        "gpu_launches": int(launches),
+        "device_error": err,
+    }
+    clk = clocks.summary()
+    line["clocks"] = {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
+                      "reasons": clk["reasons"]}
+    if e2e is not None:
+        line["e2e"] = e2e
+    if rank == 0 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(w1, s1, w2, s2, h_cpu, x_cpu)
+    if comm:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -192,6 +192,15 @@ int h3_dequantize_i32(const int32_t* acc, int64_t rows, int64_t width,
                       int64_t weight_scale_len, const float* bias, int out_kind, void* out,
                       void* stream);
 
+/* Gated residual add (tilelang_dit_fusion.py:39-53, the gate_kernel of gated_add):
+ *   X[m, n] = f16( fma(f32(f16(branch[m, n])), G[labels[m], n], f32(X[m, n])) )
+ * branch is fp32 (branch_kind H3_OUT_F32, rounded to fp16 first, as the row output's
+ * .to(fp16) does) or fp16 (H3_OUT_F16).  gate == NULL means G = 1 (plain fp16
+ * residual add); labels may be NULL when gate_rows == 1. */
+int h3_gated_add(const void* branch, int branch_kind, int64_t rows, int64_t width,
+                 void* residual_f16, const float* gate, int64_t gate_rows,
+                 const int32_t* labels, void* stream);
+
 /* ----------------------------------------------------------------------------
  * Diagnostics
  * ------------------------------------------------------------------------- */

@@ -7,8 +7,6 @@
 
 namespace h3 {
 
-H3_DEV float pow2f(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
-
 // ---------------------------------------------------------------------------
 // Scaled-FP16 codec (tilelang_transport_tradeoffs.py:26-39)
 // ---------------------------------------------------------------------------
@@ -108,6 +106,19 @@ __global__ void dequantize_i32_kernel(const int32_t* __restrict__ acc, int64_t r
       reinterpret_cast<float*>(out)[i] = v;
     else
       reinterpret_cast<__half*>(out)[i] = __float2half_rn(v);
+  }
+}
+
+// gate_kernel of tilelang_dit_fusion.py:39-53 with an fp32 or fp16 branch.
+__global__ void gated_add_kernel(const void* __restrict__ branch, int branch_kind, int64_t rows,
+                                 int64_t width, RowOut o) {
+  const int64_t total = rows * width;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / width, c = i - r * width;
+    const float y = branch_kind == H3_OUT_F32 ? reinterpret_cast<const float*>(branch)[i]
+                                              : __half2float(reinterpret_cast<const __half*>(branch)[i]);
+    row_store(o, r, c, width, y);
   }
 }
 
@@ -224,5 +235,24 @@ extern "C" int h3_dequantize_i32(const int32_t* acc, int64_t rows, int64_t width
   if (int s = h3host::bind_device_of(acc, &dev)) return s;
   dequantize_i32_kernel<<<elementwise_grid(rows * width, dev), 256, 0, (cudaStream_t)stream>>>(
       acc, rows, width, row_scale, weight_scale, weight_scale_len == 1, bias, out_kind, out);
+  return h3host::check_launch();
+}
+
+extern "C" int h3_gated_add(const void* branch, int branch_kind, int64_t rows, int64_t width,
+                            void* residual_f16, const float* gate, int64_t gate_rows,
+                            const int32_t* labels, void* stream) {
+  if (branch == nullptr || residual_f16 == nullptr || rows < 0 || width <= 0 ||
+      (branch_kind != H3_OUT_F32 && branch_kind != H3_OUT_F16))
+    return H3_ERR_INVALID;
+  if (gate != nullptr && (gate_rows < 1 || (labels == nullptr && gate_rows != 1)))
+    return H3_ERR_INVALID;
+  if (rows == 0) return H3_OK;
+  int dev;
+  if (int s = h3host::bind_device_of(branch, &dev)) return s;
+  RowOut o{H3_OUT_RESIDUAL, nullptr, reinterpret_cast<__half*>(residual_f16), gate, gate_rows,
+           labels, h3host::error_word(dev)};
+  if (o.err == nullptr) return H3_ERR_CUDA;
+  gated_add_kernel<<<elementwise_grid(rows * width, dev), 256, 0, (cudaStream_t)stream>>>(
+      branch, branch_kind, rows, width, o);
   return h3host::check_launch();
 }

@@ -52,6 +52,7 @@ SIGNATURES = {
     "h3_fp16_decode": [_P, _I64, _I, _P, _P],
     "h3_row_reduce_finish": [_P, _I, _I64, _I64, _I64, _I, _P, _P, _I, _P, _P, _P, _I64, _P, _P],
     "h3_dequantize_i32": [_P, _I64, _I64, _P, _P, _I64, _P, _I, _P, _P],
+    "h3_gated_add": [_P, _I, _I64, _I64, _P, _P, _I64, _P, _P],
     "h3_expf_compare": [_P, _I64, _P, _P, _P],
 }
 _RESTYPES = {"h3_status_string": ctypes.c_char_p}
@@ -94,8 +95,22 @@ def check(status: int, name: str) -> None:
     raise H3Error(f"{name}: {msg}")
 
 
+# Entry points that enqueue exactly one kernel per successful call.
+_LAUNCHING = {n for n in SIGNATURES if n not in (
+    "h3_abi_version", "h3_status_string", "h3_device_error", "h3_transport_shift")}
+_launches = 0
+
+
 def call(name: str, *args) -> None:
+    global _launches
     check(getattr(load(), name)(*args), name)
+    if name in _LAUNCHING:
+        _launches += 1
+
+
+def launch_count() -> int:
+    """Number of native kernels this process has enqueued through call()."""
+    return _launches
 
 
 def device_error(device: int) -> int:

@@ -1,0 +1,127 @@
+"""Per-session operator selection (mirror of the linear-path parts of
+patches/h3_operator_policy.py).
+
+The reference's fields are kept with their names and value sets, and a `b200` value
+is added to each backend field.  The T4-only values map onto the B200 kernels:
+  row_linear_backend   'tilelang_scaled_fp16' / 'b200_scaled_fp16' -> scaled-FP16 transport
+                       'tilelang_packed' / 'native' / 'b200_int32'  -> exact INT32 SUM
+  fc2_quantizer        'fused_stored' / 'fused_recompute' -> B200 FC2 producer
+                       'native' / 'owned_fp32' -> FP32 cast + full-gather exact route
+  column_linear_backend 'preallocated' / 'cuda_int8_tilelang' / 'b200' -> B200 column GEMM
+New B200 fields:
+  row_transport   'rowblock' (deterministic reduce-scatter + all-gather) or 'allreduce'
+  quant_division  'rn' (IEEE, bit-exact with the CPU oracle) or 'fast' (__fdividef)
+  fc1_swiglu_epilogue  FC1 stores the FP32 SwiGLU activation instead of fp16 [gate|up]
+"""
+from __future__ import annotations
+
+import logging
+from dataclasses import dataclass
+from functools import lru_cache
+
+import torch
+
+ROW_BACKENDS = ("tilelang_packed", "tilelang_scaled_fp16", "native", "b200_scaled_fp16", "b200_int32")
+FC2_QUANTIZERS = ("native", "owned_fp32", "fused_stored", "fused_recompute")
+COLUMN_BACKENDS = ("preallocated", "cuda_int8_tilelang", "b200")
+
+
+@dataclass(frozen=True)
+class H3OperatorPolicy:
+    row_linear_backend: str = "b200_scaled_fp16"
+    fc2_quantizer: str = "fused_recompute"
+    column_linear_backend: str = "b200"
+    dit_fused_gate: bool = True
+    dit_fused_row_gate: bool = True
+    dit_p0_2_lifetime: bool = True
+    dit_p0_3_lifetime: bool = True
+    dit_p0_b_inplace: bool = True
+    dit_p0_a1_turing: bool = True
+    dit_p0_c_local_rotation: bool = True
+    row_transport: str = "rowblock"
+    quant_division: str = "rn"
+    fc1_swiglu_epilogue: bool = True
+
+    def __post_init__(self):
+        for name in ("dit_fused_gate", "dit_fused_row_gate", "dit_p0_2_lifetime",
+                     "dit_p0_3_lifetime", "dit_p0_b_inplace", "dit_p0_a1_turing",
+                     "dit_p0_c_local_rotation", "fc1_swiglu_epilogue"):
+            if type(getattr(self, name)) is not bool:
+                raise ValueError(name + " must be boolean")
+        if self.row_linear_backend not in ROW_BACKENDS:
+            raise ValueError("Unknown row-linear backend")
+        if self.fc2_quantizer not in FC2_QUANTIZERS:
+            raise ValueError("Unknown FC2 quantizer")
+        if self.column_linear_backend not in COLUMN_BACKENDS:
+            raise ValueError("Unknown column linear backend")
+        if self.row_transport not in ("rowblock", "allreduce"):
+            raise ValueError("Unknown row transport")
+        if self.quant_division not in ("rn", "fast"):
+            raise ValueError("Unknown quantizer division")
+
+    @property
+    def scaled_transport(self) -> bool:
+        return self.row_linear_backend in ("tilelang_scaled_fp16", "b200_scaled_fp16")
+
+
+@lru_cache(maxsize=32)
+def _fallback(name, device, capability):
+    logging.warning("H3 %s: B200 path unavailable on %s (%s)", name, device, capability)
+
+
+def configure_block(block, kind, policy):
+    """Carries the policy onto a TP block's projections (h3_operator_policy.py:56-75)."""
+    block.operator_policy = policy
+    for name in (("o_proj", "down_proj") if kind == "te" else ("out_proj", "fc2")):
+        if getattr(block, name, None) is not None:
+            getattr(block, name).operator_policy = policy
+    if kind == "dit":
+        for name in ("qkv_proj", "fc1"):
+            column = getattr(block, name, None)
+            if column is not None:
+                column.operator_policy = policy
+                column._vram_p0_a1 = policy.dit_p0_a1_turing
+        if getattr(block, "out_proj", None) is not None:
+            block.out_proj._vram_p0_2 = policy.dit_p0_2_lifetime
+            block.out_proj._vram_p0_c = policy.dit_p0_c_local_rotation
+        if getattr(block, "fc2", None) is not None:
+            block.fc2._vram_p0_3 = policy.dit_p0_3_lifetime
+            block.fc2._vram_p0_b = policy.dit_p0_b_inplace
+        if getattr(block, "fc1", None) is not None:
+            block.fc1._vram_p0_3_producer = policy.dit_p0_3_lifetime
+            block.fc1._swiglu_epilogue = policy.fc1_swiglu_epilogue
+    return block
+
+
+def row_linear(module, x, fallback, comm, input_act=None):
+    """RowParallel dispatch (h3_operator_policy.py:213-237).  Returns FP32 [..., N]."""
+    policy = getattr(module, "operator_policy", None) or H3OperatorPolicy()
+    from . import swiglu_quant as quant
+    division = policy.quant_division
+    if (input_act == "swiglu" and policy.fc2_quantizer in ("fused_stored", "fused_recompute")
+            and policy.row_linear_backend != "native"):
+        if quant.supported(x, module.weight, module.weight_scale, module.world_size,
+                           module.convrot_groupsize):
+            return quant.row_linear(x, module.weight, module.weight_scale, comm,
+                                    mode=policy.fc2_quantizer,
+                                    scaled_transport=policy.scaled_transport,
+                                    transport=policy.row_transport, division=division)
+        _fallback("FC2 fused quantizer", str(x.device), None)
+    if input_act is None and x.shape[-1] % 256 == 0 and module.convrot_groupsize == 256:
+        # O projection: local ConvRot of owned groups, global row max, quantise.
+        from .row_quant import global_row_quantize
+        q, scale = global_row_quantize(x, comm, module.world_size, 256, None, division=division)
+        out = quant._finish_quantized(q, scale, module.weight, module.weight_scale.reshape(-1),
+                                      comm, policy.scaled_transport, policy.row_transport)
+        return out.reshape(*x.shape[:-1], module.weight.shape[0])
+    args = (x, module.weight, module.weight_scale, comm, module.world_size,
+            module.convrot_groupsize, input_act)
+    return fallback(*args)
+
+
+def row_linear_parts(module, gate, up, fallback, comm):
+    """Separate gate/up inputs (h3_operator_policy.py:240-255): packed into the
+    [gate | up] layout of the fused FC2 route."""
+    if gate.shape != up.shape or gate.dtype != up.dtype or gate.device != up.device:
+        raise ValueError("Matching gate/up required")
+    return row_linear(module, torch.cat((gate, up), -1), fallback, comm, "swiglu")

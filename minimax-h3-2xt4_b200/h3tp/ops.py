@@ -11,6 +11,11 @@ import torch
 from . import _native as N
 
 
+def launch_count() -> int:
+    """Kernels enqueued so far by this process (one per native call)."""
+    return N.launch_count()
+
+
 def _ptr(t: torch.Tensor | None):
     return None if t is None else t.data_ptr()
 
@@ -298,6 +303,22 @@ def dequantize_i32(acc, row_scale, weight_scale, out_dtype=torch.float32, bias=N
     N.call("h3_dequantize_i32", acc.data_ptr(), M, Nn, a.data_ptr(), ws.data_ptr(), ws.numel(),
            _ptr(b), kind, out.data_ptr(), _stream(acc))
     return out
+
+
+def gated_add(residual, branch, gate=None, labels=None):
+    """X = f16(fma(f16(branch), G[label], X)) in place (gate_kernel,
+    tilelang_dit_fusion.py:39-53); branch fp32 or fp16 [M, N]; returns residual."""
+    if not residual.is_contiguous():
+        raise ValueError("residual must be contiguous (updated in place)")
+    if branch.dtype not in (torch.float32, torch.float16):
+        raise ValueError("branch must be fp32 or fp16")
+    b = _need(branch, branch.dtype, "branch", 2)
+    M, Nn = b.shape
+    res, g, grows, lab = _gate_args(residual, gate, labels, M, Nn)
+    kind = N.OUT_F32 if b.dtype == torch.float32 else N.OUT_F16
+    N.call("h3_gated_add", b.data_ptr(), kind, M, Nn, res.data_ptr(), _ptr(g), grows, _ptr(lab),
+           _stream(b))
+    return residual
 
 
 def expf_compare(x: torch.Tensor):
