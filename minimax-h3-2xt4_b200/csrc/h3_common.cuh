@@ -42,15 +42,14 @@ H3_DEV float f32_bits(uint32_t b) { return __uint_as_float(b); }
 // 99.3% of the fp16 inputs the SwiGLU sees.  The disagreement against CUDA expf is
 // measured on the GPU by tests/test_gpu_kernels.py.
 // ---------------------------------------------------------------------------
-H3_DEV float h3_expf(float x) {
-  if (x != x) return __fadd_rn(x, x);           // NaN in, NaN out
-  if (x > 89.0f) return __uint_as_float(0x7f800000u);
-  if (x < -104.0f) return 0.0f;
+// Shared core: for xc in [-104, 89], n = rint(xc / ln2) and y = exp(xc - n ln2) in
+// [0.7, 1.42], such that exp(xc) = y * 2^n.
+H3_DEV void exp_core(float xc, float& y, int& ni) {
   const float l2e = f32_bits(0x3fb8aa3bu);       // float32(1/ln 2)
   const float ln2_hi = f32_bits(0x3f317200u);    // 16 significant bits
   const float ln2_lo = f32_bits(0x35bfbe8eu);    // float32(ln2 - ln2_hi)
-  const float n = rintf(__fmul_rn(x, l2e));
-  const float r1 = __fmaf_rn(-n, ln2_hi, x);                 // exact
+  const float n = rintf(__fmul_rn(xc, l2e));
+  const float r1 = __fmaf_rn(-n, ln2_hi, xc);                // exact
   const float r = __fmaf_rn(-n, ln2_lo, r1);                 // rounded reduced argument
   const float corr = __fmaf_rn(-n, ln2_lo, __fadd_rn(r1, -r));  // its rounding error
   float t = __fmaf_rn(r, f32_bits(0x37d00d01u), f32_bits(0x39500d01u));  // 1/40320, 1/5040
@@ -62,21 +61,70 @@ H3_DEV float h3_expf(float x) {
   const float s = __fmaf_rn(t, __fmul_rn(r, r), corr);
   const float hi = __fadd_rn(1.0f, r);
   const float lo = __fadd_rn(r, -__fadd_rn(hi, -1.0f));      // exact error of 1 + r
-  const float y = __fadd_rn(hi, __fadd_rn(lo, s));
-  const int ni = (int)n;
+  y = __fadd_rn(hi, __fadd_rn(lo, s));
+  ni = (int)n;
+}
+
+H3_DEV float h3_expf(float x) {
+  // Branch-free: the reduction runs on x clamped to [-104, 89] and the special
+  // results (overflow to +inf, underflow to 0, NaN) are selected at the end, which is
+  // the same value the early-return form gives for every input.
+  const float xc = fminf(fmaxf(x, -104.0f), 89.0f);
+  float y;
+  int ni;
+  exp_core(xc, y, ni);
   const int h = ni >> 1;                         // floor(ni / 2)
   const float s1 = __uint_as_float((uint32_t)(h + 127) << 23);
   const float s2 = __uint_as_float((uint32_t)(ni - h + 127) << 23);
-  return __fmul_rn(__fmul_rn(y, s1), s2);
+  float res = __fmul_rn(__fmul_rn(y, s1), s2);
+  res = (x > 89.0f) ? __uint_as_float(0x7f800000u) : res;
+  res = (x < -104.0f) ? 0.0f : res;
+  return (x != x) ? __fadd_rn(x, x) : res;
+}
+
+// 1 +rn h3_expf(-g), for every non-NaN float g, at lower cost.  Outside
+// -g in [-17, 88.9] the sum is already decided: for -g < -17, exp(-g) < 2^-24 and
+// 1 + exp(-g) rounds to 1, which exp(-17) gives too; for -g > 88.9 both overflow to
+// +inf.  Inside, n >= -25, so y * 2^(n-1) is an exact normal product and the final
+// doubling is exact or overflows exactly where (y * 2^h) * 2^(n-h) does.  A NaN g
+// yields 1 here (instead of NaN), which still makes g / den NaN.
+H3_DEV float silu_den(float g) {
+  const float x = fminf(fmaxf(-g, -17.0f), 88.9f);
+  float y;
+  int ni;
+  exp_core(x, y, ni);
+  const float s = __uint_as_float((uint32_t)(ni - 1 + 127) << 23);
+  return __fadd_rn(1.0f, __fmul_rn(__fmul_rn(y, s), 2.0f));
+}
+
+// silu(g) = g /rn (1 +rn exp(-g)), the activation half of the reference's SwiGLU
+// (tilelang_swiglu_quant.py:22-23), reference form.
+H3_DEV float silu_ieee(float g) {
+  return __fdiv_rn(g, __fadd_rn(1.0f, h3_expf(-g)));
+}
+
+// The same value for every float g, without operands that make the IEEE division
+// leave its common path.  A denominator above 2^64 only occurs for g < -44; there
+// both operands are multiplied by 2^-32, which is exact (|g| * 2^-32 >= 2^-27 and
+// den * 2^-32 < 2^96 stay normal), so the quotient - itself >= 44 / FLT_MAX, a normal
+// float - and its rounding are unchanged.  An infinite denominator with a finite g
+// (g < -88.7) gives g / inf = -0, produced as -0 / 1.  Verified bit-identical to
+// silu_ieee on all 65536 fp16 gate values (tests/test_gpu_kernels.py).
+H3_DEV float silu_fast(float g) {
+  float den = silu_den(g);
+  float num = g;
+  const bool big = den > 18446744073709551616.0f;  // 2^64
+  const bool inf_den = (den == __uint_as_float(0x7f800000u)) && (fabsf(g) < __uint_as_float(0x7f800000u));
+  num = big ? __fmul_rn(num, 2.3283064365386963e-10f) : num;  // 2^-32
+  den = big ? __fmul_rn(den, 2.3283064365386963e-10f) : den;
+  num = inf_den ? -0.0f : num;
+  den = inf_den ? 1.0f : den;
+  return __fdiv_rn(num, den);
 }
 
 // FP32 SwiGLU of one (gate, up) pair, in the order of tilelang_swiglu_quant.py:21-24:
 //   a = (gate /rn (1 +rn exp(-gate))) *rn up
-H3_DEV float swiglu_f32(float gate, float up) {
-  const float den = __fadd_rn(1.0f, h3_expf(-gate));
-  const float act = __fdiv_rn(gate, den);
-  return __fmul_rn(act, up);
-}
+H3_DEV float swiglu_f32(float gate, float up) { return __fmul_rn(silu_fast(gate), up); }
 
 // Row scale of the production row quantizer (tilelang_row_quant.py:166-167):
 //   scale = fmaxf(fminf(max, FLT_MAX) *rn float32(1/127), 1e-30)

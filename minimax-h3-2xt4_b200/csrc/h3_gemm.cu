@@ -11,8 +11,9 @@
 //     (cta_group::1, kind::i8, M=128, N=256, K=32 per instruction) into an INT32
 //     accumulator in tensor memory (TMEM); two 256-column accumulators are
 //     double-buffered so the epilogue of tile i overlaps the MMAs of tile i+1;
-//   - warps 2-5 (one per 32-lane TMEM quadrant) read the accumulator with
-//     tcgen05.ld, apply the fused epilogue and store to global memory.
+//   - warps 2-17 (four per 32-lane TMEM quadrant, each owning a quarter of the
+//     tile's columns) read the accumulator with tcgen05.ld, apply the fused epilogue and
+//     store to global memory with 128-bit accesses.
 //
 // Every mbarrier wait is bounded (2 s of %globaltimer); a wait that gives up sets the
 // library's device error word (H3_ERR_TIMEOUT), raises a CTA-wide abort flag, and
@@ -34,15 +35,29 @@ constexpr int STAGES = 4;
 constexpr int A_STAGE = BM * BK;  // 16 KiB
 constexpr int B_STAGE = BN * BK;  // 32 KiB
 constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
-constexpr int THREADS = 192;
+constexpr int EPI_WARPS = 16;                // four warps per 32-lane TMEM quadrant
+constexpr int EPI_PARTS = EPI_WARPS / 4;     // column slices of a tile, one per warp
+constexpr int THREADS = 64 + 32 * EPI_WARPS;  // warp 0 TMA, warp 1 MMA, warps 2.. epilogue
 constexpr int TMEM_COLS = 512;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr unsigned long long TIMEOUT_NS = 2000000000ull;
+
+// 2-SM (cta_group::2) variant: a CTA pair computes a 256 x 256 tile; each CTA stages
+// its 128 rows of A and 128 rows (one N half) of B, and holds 128 x 256 of the INT32
+// accumulator in its own TMEM.
+constexpr int BM2 = 256;
+constexpr int B_HALF = (BN / 2) * BK;          // 16 KiB
+constexpr int STAGES2 = 6;
+constexpr int STAGE2_BYTES = A_STAGE + B_HALF;  // 32 KiB per CTA
+constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 256;
 
 // Instruction descriptor, kind::i8: D = S32 (bits 4-5 = 2), A = B = signed 8-bit
 // (bits 7-9 and 10-12 = 1), both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
 constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
                            ((uint32_t)(BM >> 4) << 24);
+
+constexpr uint32_t IDESC2 = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                            ((uint32_t)(BM2 >> 4) << 24);
 
 enum Epi { EPI_I32 = 0, EPI_COLUMN = 1, EPI_SWIGLU = 2, EPI_ROW_ENCODE = 3, EPI_ROW_DEQUANT = 4 };
 
@@ -59,6 +74,8 @@ struct Args {
   const float* bias;
   float enc_factor;
   RowOut row;
+  int res_vec;    // residual / gate rows may use 128-bit accesses
+  int scale_vec;  // weight scales / bias may use 128-bit loads
   int* err;
 };
 
@@ -146,6 +163,54 @@ H3_DEV void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t 
       : "memory");
 }
 
+H3_DEV uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of `saddr` (a shared::cta address) in CTA `rank` of the cluster
+H3_DEV uint32_t cluster_addr(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+H3_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+}
+
+H3_DEV void mbar_arrive_remote(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+// TMA load into this CTA's shared memory that completes its bytes on the pair
+// leader's mbarrier (no multicast).
+H3_DEV void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int32_t c0, int32_t c1,
+                             uint32_t cluster_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(cluster_bar)
+      : "memory");
+}
+
+H3_DEV void tc_commit_pair(uint32_t cluster_bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   cluster_bar)
+               : "memory");
+}
+
+H3_DEV void tc_mma_i8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row core groups 1024 B
 // apart (SBO), descriptor version 1, base offset 0 (stage buffers are 1024-aligned).
 H3_DEV uint64_t sw128_desc(uint32_t saddr) {
@@ -158,7 +223,7 @@ H3_DEV uint64_t sw128_desc(uint32_t saddr) {
   return d;
 }
 
-H3_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+H3_DEV void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
@@ -171,8 +236,26 @@ H3_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
         "=r"(r[31])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+
+H3_DEV void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+H3_DEV void tmem_ld8_nowait(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
+H3_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Tile order: groups of 16 M-blocks sweep all N-blocks, so concurrently running
 // CTAs share A rows and B columns in L2.
@@ -189,11 +272,12 @@ H3_DEV void tile_coords(int tile, int tiles_m, int tiles_n, int& mb, int& nb) {
 // ---------------------------------------------------------------------------
 // Epilogue helpers: one thread owns one output row and 32 consecutive columns.
 // ---------------------------------------------------------------------------
-H3_DEV void store_f16_chunk(__half* dst, int64_t n0, int64_t N, const float (&v)[32], bool vec) {
-  if (vec && n0 + 32 <= N) {
+template <int C>
+H3_DEV void store_f16_chunk(__half* dst, int64_t n0, int64_t N, const float (&v)[C], bool vec) {
+  if (vec && n0 + C <= N) {
     uint4* p = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < C / 8; ++i) {
       __half2 h[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(v[8 * i + 2 * j], v[8 * i + 2 * j + 1]);
@@ -201,31 +285,202 @@ H3_DEV void store_f16_chunk(__half* dst, int64_t n0, int64_t N, const float (&v)
     }
   } else {
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
+    for (int j = 0; j < C; ++j)
       if (n0 + j < N) dst[j] = __float2half_rn(v[j]);
   }
 }
 
-H3_DEV void store_f32_chunk(float* dst, int64_t n0, int64_t N, const float (&v)[32], bool vec) {
-  if (vec && n0 + 32 <= N) {
+template <int C>
+H3_DEV void store_f32_chunk(float* dst, int64_t n0, int64_t N, const float (&v)[C], bool vec) {
+  if (vec && n0 + C <= N) {
     float4* p = reinterpret_cast<float4*>(dst);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) p[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    for (int i = 0; i < C / 4; ++i) p[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
   } else {
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
+    for (int j = 0; j < C; ++j)
       if (n0 + j < N) dst[j] = v[j];
   }
 }
 
-H3_DEV void load_scales32(const float* w, int64_t n0, int64_t N, int scalar, float (&s)[32]) {
-  if (scalar) {
-    const float v = __ldg(w);
+// Gated residual update of C consecutive columns of one row
+// (tilelang_dit_fusion.py:68-75): X = f16(fma(f32(f16(y)), G[lab], f32(X))).
+template <int C>
+H3_DEV void residual_chunk(const RowOut& o, int64_t row, int64_t n0, int64_t N, int64_t lab,
+                           const float (&y)[C], bool vec) {
+  if (vec && n0 + C <= N) {
+    uint4* p = reinterpret_cast<uint4*>(o.residual + row * N + n0);
+    const float4* g4 = o.gate ? reinterpret_cast<const float4*>(o.gate + lab * N + n0) : nullptr;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) s[j] = v;
+    for (int i = 0; i < C / 8; ++i) {
+      uint4 u = p[i];
+      __half2* h = reinterpret_cast<__half2*>(&u);
+      float g[8];
+      if (g4 != nullptr) {
+        const float4 ga = __ldg(g4 + 2 * i), gb = __ldg(g4 + 2 * i + 1);
+        g[0] = ga.x; g[1] = ga.y; g[2] = ga.z; g[3] = ga.w;
+        g[4] = gb.x; g[5] = gb.y; g[6] = gb.z; g[7] = gb.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) g[j] = 1.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 x = __half22float2(h[j]);
+        const float b0 = __half2float(__float2half_rn(y[8 * i + 2 * j]));
+        const float b1 = __half2float(__float2half_rn(y[8 * i + 2 * j + 1]));
+        h[j] = __floats2half2_rn(__fmaf_rn(b0, g[2 * j], x.x), __fmaf_rn(b1, g[2 * j + 1], x.y));
+      }
+      p[i] = u;
+    }
   } else {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) s[j] = (n0 + j < N) ? __ldg(w + n0 + j) : 0.0f;
+    for (int j = 0; j < C; ++j)
+      if (n0 + j < N) row_store(o, row, n0 + j, N, y[j]);
+  }
+}
+
+template <int C>
+H3_DEV void load_scales(const float* w, int64_t n0, int64_t N, int scalar, float (&s)[C],
+                        bool vec = false) {
+  if (vec && !scalar && n0 + C <= N) {
+    const float4* p = reinterpret_cast<const float4*>(w + n0);
+#pragma unroll
+    for (int i = 0; i < C / 4; ++i) {
+      const float4 f = __ldg(p + i);
+      s[4 * i] = f.x; s[4 * i + 1] = f.y; s[4 * i + 2] = f.z; s[4 * i + 3] = f.w;
+    }
+  } else if (scalar) {
+    const float v = __ldg(w);
+#pragma unroll
+    for (int j = 0; j < C; ++j) s[j] = v;
+  } else {
+#pragma unroll
+    for (int j = 0; j < C; ++j) s[j] = (n0 + j < N) ? __ldg(w + n0 + j) : 0.0f;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Epilogue of one output tile: this warp's 32 TMEM lanes (`row` is the lane's output
+// row) and one EPI_PARTS-th of the tile's 256 accumulator columns.
+// ---------------------------------------------------------------------------
+template <int EPI>
+H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool row_ok, int nb,
+                          int part) {
+  const int64_t N = args.N;
+  if (EPI == EPI_SWIGLU) {
+    // accumulator columns [0,128) = gate rows, [128,256) = up rows of this tile
+    constexpr int GCOLS = (BN / 2) / EPI_PARTS;  // gate columns of this warp
+    const int64_t n_base = (int64_t)nb * (BN / 2) + part * GCOLS;
+    const float a = row_ok ? __ldg(args.row_scale + row) : 0.0f;
+    const bool vec4 = args.scale_vec != 0;
+    constexpr int SW = 8;  // columns per step: keeps the SwiGLU epilogue within 96 registers
+#pragma unroll 1
+    for (int c = 0; c < GCOLS / SW; ++c) {
+      const int64_t n0 = n_base + c * SW;
+      if (n0 >= N) break;  // warp-uniform
+      uint32_t rg[SW], ru[SW];
+      tmem_ld8_nowait(tbase + part * GCOLS + c * SW, rg);
+      tmem_ld8_nowait(tbase + BN / 2 + part * GCOLS + c * SW, ru);
+      float wg[SW], wu[SW];
+      load_scales<SW>(args.weight_scale, n0, N, 0, wg, vec4);
+      load_scales<SW>(args.weight_scale + N, n0, N, 0, wu, vec4);
+      float bg[SW], bu[SW];
+      if (args.bias != nullptr) {
+        load_scales<SW>(args.bias, n0, N, 0, bg, vec4);
+        load_scales<SW>(args.bias + N, n0, N, 0, bu, vec4);
+      }
+      tmem_wait_ld();
+      float y[SW];
+#pragma unroll
+      for (int j = 0; j < SW; ++j) {
+        float vg = __fmul_rn(__int2float_rn((int32_t)rg[j]), __fmul_rn(a, wg[j]));
+        float vu = __fmul_rn(__int2float_rn((int32_t)ru[j]), __fmul_rn(a, wu[j]));
+        if (args.bias != nullptr) {
+          vg = __fadd_rn(vg, bg[j]);
+          vu = __fadd_rn(vu, bu[j]);
+        }
+        const float g = __half2float(__float2half_rn(vg));
+        const float u = __half2float(__float2half_rn(vu));
+        y[j] = swiglu_f32(g, u);
+      }
+      if (row_ok) {
+        if (args.out_kind == H3_OUT_F32)
+          store_f32_chunk<SW>(reinterpret_cast<float*>(args.out) + row * N + n0, n0, N, y,
+                              (N & 3) == 0);
+        else
+          store_f16_chunk<SW>(reinterpret_cast<__half*>(args.out) + row * N + n0, n0, N, y,
+                              (N & 7) == 0);
+      }
+    }
+  } else {
+    constexpr int COLS = BN / EPI_PARTS;  // accumulator columns of this warp
+    const int64_t n_base = (int64_t)nb * BN + part * COLS;
+    const float a = (row_ok && args.row_scale != nullptr) ? __ldg(args.row_scale + row) : 0.0f;
+    int64_t lab = 0;
+    if (EPI == EPI_ROW_DEQUANT && args.row.kind == H3_OUT_RESIDUAL && row_ok &&
+        args.row.gate != nullptr && args.row.labels != nullptr) {
+      lab = __ldg(args.row.labels + row);
+      if (lab < 0 || lab >= args.row.gate_rows) {
+        atomicExch(args.row.err, H3_ERR_INVALID);
+        lab = 0;
+      }
+    }
+#pragma unroll 1
+    for (int c = 0; c < COLS / 16; ++c) {
+      const int64_t n0 = n_base + c * 16;
+      if (n0 >= N) break;  // warp-uniform
+      uint32_t r[16];
+      tmem_ld16_nowait(tbase + part * COLS + c * 16, r);
+      float w[16];
+      if (EPI == EPI_COLUMN || EPI == EPI_ROW_DEQUANT)
+        load_scales<16>(args.weight_scale, n0, N, EPI == EPI_COLUMN ? args.scalar_w : 0, w,
+                        args.scale_vec != 0);
+      tmem_wait_ld();
+      if (!row_ok) continue;
+      if (EPI == EPI_I32) {
+        int32_t* dst = reinterpret_cast<int32_t*>(args.out) + row * N + n0;
+        if (n0 + 16 <= N && (N & 3) == 0) {
+          int4* p = reinterpret_cast<int4*>(dst);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            p[i] = make_int4((int)r[4 * i], (int)r[4 * i + 1], (int)r[4 * i + 2], (int)r[4 * i + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (n0 + j < N) dst[j] = (int32_t)r[j];
+        }
+      } else if (EPI == EPI_COLUMN) {
+        float y[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          y[j] = __fmul_rn(__int2float_rn((int32_t)r[j]), __fmul_rn(a, w[j]));
+          if (args.bias != nullptr && n0 + j < N) y[j] = __fadd_rn(y[j], __ldg(args.bias + n0 + j));
+        }
+        store_f16_chunk<16>(reinterpret_cast<__half*>(args.out) + row * N + n0, n0, N, y,
+                            (N & 7) == 0);
+      } else if (EPI == EPI_ROW_ENCODE) {
+        float y[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) y[j] = __fmul_rn(__int2float_rn((int32_t)r[j]), args.enc_factor);
+        store_f16_chunk<16>(reinterpret_cast<__half*>(args.out) + row * N + n0, n0, N, y,
+                            (N & 7) == 0);
+      } else {  // EPI_ROW_DEQUANT
+        float y[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          y[j] = __fmul_rn(__fmul_rn(__int2float_rn((int32_t)r[j]), a), w[j]);
+        if (args.row.kind == H3_OUT_F32) {
+          store_f32_chunk<16>(reinterpret_cast<float*>(args.row.out) + row * N + n0, n0, N, y,
+                              (N & 3) == 0);
+        } else if (args.row.kind == H3_OUT_F16) {
+          store_f16_chunk<16>(reinterpret_cast<__half*>(args.row.out) + row * N + n0, n0, N, y,
+                              (N & 7) == 0);
+        } else {
+          residual_chunk<16>(args.row, row, n0, N, lab, y, args.res_vec != 0);
+        }
+      }
+    }
   }
 }
 
@@ -257,7 +512,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(tfull + a), 1);
-      mbar_init(smem_u32(tempty + a), 128);
+      mbar_init(smem_u32(tempty + a), 32 * EPI_WARPS);
     }
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
@@ -359,7 +614,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ------------------------------ epilogue ------------------------------------
-    const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad + 32)
+    const int quad = warp & 3;          // TMEM lanes [32*quad, 32*quad + 32)
+    const int part = (warp - 2) >> 2;   // which column slice of the tile
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
@@ -368,102 +624,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!mbar_wait(smem_u32(tfull + acc), acc_phase, abort_flag, args.err)) break;
       tc_fence_after();
       const int64_t row = (int64_t)mb * BM + quad * 32 + lane;
-      const bool row_ok = row < args.M;
       const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-      const int64_t N = args.N;
-
-      if (EPI == EPI_SWIGLU) {
-        const int64_t n_base = (int64_t)nb * (BN / 2);
-        const float a = row_ok ? __ldg(args.row_scale + row) : 0.0f;
-#pragma unroll 1
-        for (int c = 0; c < (BN / 2) / 32; ++c) {
-          uint32_t rg[32], ru[32];
-          tmem_ld32(tbase + c * 32, rg);
-          tmem_ld32(tbase + BN / 2 + c * 32, ru);
-          const int64_t n0 = n_base + c * 32;
-          float wg[32], wu[32];
-          load_scales32(args.weight_scale, n0, N, 0, wg);
-          load_scales32(args.weight_scale + N, n0, N, 0, wu);
-          float y[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float vg = __fmul_rn(__int2float_rn((int32_t)rg[j]), __fmul_rn(a, wg[j]));
-            float vu = __fmul_rn(__int2float_rn((int32_t)ru[j]), __fmul_rn(a, wu[j]));
-            if (args.bias != nullptr && n0 + j < N) {
-              vg = __fadd_rn(vg, __ldg(args.bias + n0 + j));
-              vu = __fadd_rn(vu, __ldg(args.bias + N + n0 + j));
-            }
-            const float g = __half2float(__float2half_rn(vg));
-            const float u = __half2float(__float2half_rn(vu));
-            y[j] = swiglu_f32(g, u);
-          }
-          if (row_ok) {
-            if (args.out_kind == H3_OUT_F32)
-              store_f32_chunk(reinterpret_cast<float*>(args.out) + row * N + n0, n0, N, y,
-                              (N & 3) == 0);
-            else
-              store_f16_chunk(reinterpret_cast<__half*>(args.out) + row * N + n0, n0, N, y,
-                              (N & 7) == 0);
-          }
-        }
-      } else {
-        const int64_t n_base = (int64_t)nb * BN;
-        const float a = (row_ok && args.row_scale != nullptr) ? __ldg(args.row_scale + row) : 0.0f;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          const int64_t n0 = n_base + c * 32;
-          if (n0 >= N) break;  // warp-uniform
-          uint32_t r[32];
-          tmem_ld32(tbase + c * 32, r);
-          if (!row_ok) continue;
-          if (EPI == EPI_I32) {
-            int32_t* dst = reinterpret_cast<int32_t*>(args.out) + row * N + n0;
-            if (n0 + 32 <= N && (N & 3) == 0) {
-              int4* p = reinterpret_cast<int4*>(dst);
-#pragma unroll
-              for (int i = 0; i < 8; ++i)
-                p[i] = make_int4((int)r[4 * i], (int)r[4 * i + 1], (int)r[4 * i + 2], (int)r[4 * i + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (n0 + j < N) dst[j] = (int32_t)r[j];
-            }
-          } else if (EPI == EPI_COLUMN) {
-            float w[32], y[32];
-            load_scales32(args.weight_scale, n0, N, args.scalar_w, w);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              y[j] = __fmul_rn(__int2float_rn((int32_t)r[j]), __fmul_rn(a, w[j]));
-              if (args.bias != nullptr && n0 + j < N) y[j] = __fadd_rn(y[j], __ldg(args.bias + n0 + j));
-            }
-            store_f16_chunk(reinterpret_cast<__half*>(args.out) + row * N + n0, n0, N, y,
-                            (N & 7) == 0);
-          } else if (EPI == EPI_ROW_ENCODE) {
-            float y[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) y[j] = __fmul_rn(__int2float_rn((int32_t)r[j]), args.enc_factor);
-            store_f16_chunk(reinterpret_cast<__half*>(args.out) + row * N + n0, n0, N, y,
-                            (N & 7) == 0);
-          } else {  // EPI_ROW_DEQUANT
-            float w[32], y[32];
-            load_scales32(args.weight_scale, n0, N, 0, w);
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              y[j] = __fmul_rn(__fmul_rn(__int2float_rn((int32_t)r[j]), a), w[j]);
-            if (args.row.kind == H3_OUT_F32) {
-              store_f32_chunk(reinterpret_cast<float*>(args.row.out) + row * N + n0, n0, N, y,
-                              (N & 3) == 0);
-            } else if (args.row.kind == H3_OUT_F16) {
-              store_f16_chunk(reinterpret_cast<__half*>(args.row.out) + row * N + n0, n0, N, y,
-                              (N & 7) == 0);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (n0 + j < N) row_store(args.row, row, n0 + j, N, y[j]);
-            }
-          }
-        }
-      }
+      epilogue_tile<EPI>(args, tbase, row, row < args.M, nb, part);
       tc_fence_before();
       mbar_arrive(smem_u32(tempty + acc));
       acc ^= 1;
@@ -476,6 +638,190 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// 2-SM kernel: clusters of two CTAs; CTA rank 0 (the leader) issues the M=256 MMAs.
+//   full[s]   leader only: one arrive.expect_tx (both CTAs' bytes) + the TMA bytes of
+//             both CTAs (each CTA's loads complete on the leader's barrier)
+//   empty[s]  each CTA: released by the leader's commit after the MMAs read stage s
+//   tfull[a]  each CTA: released by the leader's commit when accumulator a is final
+//   tempty[a] leader only: one arrive per epilogue warp of both CTAs
+// ---------------------------------------------------------------------------
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmB2, const Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES2 * A_STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES2 * STAGE2_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES2;
+  uint64_t* tfull = bars + 2 * STAGES2;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES2; ++s) {
+      mbar_init(smem_u32(full + s), 1);
+      mbar_init(smem_u32(empty + s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(tfull + a), 1);
+      mbar_init(smem_u32(tempty + a), 2 * EPI_WARPS);
+    }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the peer's barriers are initialised before any remote signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total_tiles = args.tiles_m * args.tiles_n;
+  const int num_kb = args.num_kb;
+  const int cluster_id = blockIdx.x >> 1;
+  const int clusters = gridDim.x >> 1;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------- TMA producer (both CTAs) ----------------------
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int tile = cluster_id; tile < total_tiles && ok; tile += clusters) {
+        int mb, nb;
+        tile_coords(tile, args.tiles_m, args.tiles_n, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(empty + stage), phase ^ 1u, abort_flag, args.err)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(full + stage);
+          if (leader) mbar_expect_tx(fb, 2 * STAGE2_BYTES);
+          const uint32_t fb_leader = cluster_addr(fb, 0);
+          tma_load_2d_pair(smem_u32(sA + stage * A_STAGE), &tmA, kb * BK,
+                           mb * BM2 + (int)rank * BM, fb_leader);
+          if (EPI == EPI_SWIGLU) {
+            // rank 0 stages the 128 gate rows, rank 1 the 128 up rows of this tile
+            tma_load_2d_pair(smem_u32(sB + stage * B_HALF), rank == 0 ? &tmB : &tmB2, kb * BK,
+                             nb * (BN / 2), fb_leader);
+          } else {
+            tma_load_2d_pair(smem_u32(sB + stage * B_HALF), &tmB, kb * BK,
+                             nb * BN + (int)rank * (BN / 2), fb_leader);
+          }
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES2) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // The leader's full barriers complete only when both CTAs' copies landed.
+      if (leader)
+        for (int s = 0; s < STAGES2; ++s)
+          if (issued_mask & (1u << s))
+            mbar_wait(smem_u32(full + s), (issued_parity >> s) & 1u, abort_flag, args.err, false);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------------------- MMA issuer (leader) ---------------------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = cluster_id; tile < total_tiles && ok; tile += clusters) {
+        if (!mbar_wait(smem_u32(tempty + acc), acc_phase ^ 1u, abort_flag, args.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(full + stage), phase, abort_flag, args.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * A_STAGE);
+          const uint32_t b0 = smem_u32(sB + stage * B_HALF);
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k) {
+            tc_mma_i8_pair(d_tmem, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), IDESC2,
+                           (kb | k) != 0 ? 1u : 0u);
+          }
+          const uint32_t eb = smem_u32(empty + stage);
+          tc_commit_pair(cluster_addr(eb, 0));
+          tc_commit_pair(cluster_addr(eb, 1));
+          if (++stage == STAGES2) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        const uint32_t tb = smem_u32(tfull + acc);
+        tc_commit_pair(cluster_addr(tb, 0));
+        tc_commit_pair(cluster_addr(tb, 1));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      // All MMAs complete before either CTA releases its TMEM.
+      tc_commit_pair(cluster_addr(smem_u32(drain), 0));
+      mbar_wait(smem_u32(drain), 0, abort_flag, args.err, false);
+    }
+  } else {
+    // ---------------------------- epilogue (both CTAs) ----------------------------
+    const int quad = warp & 3;
+    const int part = (warp - 2) >> 2;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = cluster_id; tile < total_tiles; tile += clusters) {
+      int mb, nb;
+      tile_coords(tile, args.tiles_m, args.tiles_n, mb, nb);
+      if (!mbar_wait(smem_u32(tfull + acc), acc_phase, abort_flag, args.err)) break;
+      tc_fence_after();
+      const int64_t row = (int64_t)mb * BM2 + (int64_t)rank * BM + quad * 32 + lane;
+      const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+      epilogue_tile<EPI>(args, tbase, row, row < args.M, nb, part);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(cluster_addr(smem_u32(tempty + acc), 0));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the pair still reads its smem or TMEM
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                  "r"(TMEM_COLS)
                  : "memory");
   }
@@ -534,35 +880,52 @@ static int launch(const int8_t* q, const int8_t* w, int64_t M, int64_t N, int64_
   int dev;
   if (int s = h3host::bind_device_of(q, &dev)) return s;
   if (!device_is_sm100(dev)) return H3_ERR_UNSUPPORTED;
+  // CTA pairs (256-row tiles) once there is more than one 128-row block; a single
+  // CTA per tile below that.
+  const bool pair = M > BM;
+  const int bn_rows = EPI == EPI_SWIGLU ? BN / 2 : (pair ? BN / 2 : BN);
   CUtensorMap tA, tB, tB2;
   if (!make_map(&tA, q, M, K, BM)) return H3_ERR_INVALID;
   if (EPI == EPI_SWIGLU) {
-    if (!make_map(&tB, w, N, K, BN / 2)) return H3_ERR_INVALID;
-    if (!make_map(&tB2, w + N * K, N, K, BN / 2)) return H3_ERR_INVALID;
+    if (!make_map(&tB, w, N, K, bn_rows)) return H3_ERR_INVALID;
+    if (!make_map(&tB2, w + N * K, N, K, bn_rows)) return H3_ERR_INVALID;
   } else {
-    if (!make_map(&tB, w, N, K, BN)) return H3_ERR_INVALID;
+    if (!make_map(&tB, w, N, K, bn_rows)) return H3_ERR_INVALID;
     tB2 = tB;
   }
+  const int tile_n = EPI == EPI_SWIGLU ? BN / 2 : BN;
   args.M = M;
   args.N = N;
   args.K = K;
-  args.tiles_m = (int)((M + BM - 1) / BM);
-  args.tiles_n = (int)((N + (EPI == EPI_SWIGLU ? BN / 2 : BN) - 1) / (EPI == EPI_SWIGLU ? BN / 2 : BN));
+  args.tiles_m = (int)((M + (pair ? BM2 : BM) - 1) / (pair ? BM2 : BM));
+  args.tiles_n = (int)((N + tile_n - 1) / tile_n);
   args.num_kb = (int)((K + BK - 1) / BK);
   args.err = h3host::error_word(dev);
   if (args.err == nullptr) return H3_ERR_CUDA;
   if (args.row.err == nullptr) args.row.err = args.err;
   const int64_t tiles = (int64_t)args.tiles_m * args.tiles_n;
   if (tiles > INT32_MAX) return H3_ERR_INVALID;
-  const int grid = (int)std::min<int64_t>(tiles, h3host::sm_count(dev));
-  static bool attr_set[64] = {false};
-  if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(gemm_i8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             SMEM_BYTES) != cudaSuccess)
-      return H3_ERR_CUDA;
-    attr_set[dev] = true;
+  const int sms = h3host::sm_count(dev);
+  static bool attr_set[64][2] = {{false}};
+  if (pair) {
+    if (!attr_set[dev][1]) {
+      if (cudaFuncSetAttribute(gemm_i8_pair_kernel<EPI>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES) != cudaSuccess)
+        return H3_ERR_CUDA;
+      attr_set[dev][1] = true;
+    }
+    const int grid = 2 * (int)std::min<int64_t>(tiles, sms / 2);
+    gemm_i8_pair_kernel<EPI><<<grid, THREADS, SMEM2_BYTES, stream>>>(tA, tB, tB2, args);
+  } else {
+    if (!attr_set[dev][0]) {
+      if (cudaFuncSetAttribute(gemm_i8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               SMEM_BYTES) != cudaSuccess)
+        return H3_ERR_CUDA;
+      attr_set[dev][0] = true;
+    }
+    const int grid = (int)std::min<int64_t>(tiles, sms);
+    gemm_i8_kernel<EPI><<<grid, THREADS, SMEM_BYTES, stream>>>(tA, tB, tB2, args);
   }
-  gemm_i8_kernel<EPI><<<grid, THREADS, SMEM_BYTES, stream>>>(tA, tB, tB2, args);
   return h3host::check_launch();
 }
 
@@ -600,6 +963,7 @@ extern "C" int h3_int8_gemm_column(const int8_t* q, const int8_t* w, int64_t m, 
   a.weight_scale = weight_scale;
   a.scalar_w = weight_scale_len == 1;
   a.bias = bias;
+  a.scale_vec = n % 4 == 0 && h3host::aligned(weight_scale, 16);
   return launch<EPI_COLUMN>(q, w, m, n, k, a, (cudaStream_t)stream);
 }
 
@@ -617,6 +981,8 @@ extern "C" int h3_int8_gemm_swiglu(const int8_t* q, const int8_t* w, int64_t m,
   a.row_scale = row_scale;
   a.weight_scale = weight_scale;
   a.bias = bias;
+  a.scale_vec = (n_packed / 2) % 4 == 0 && h3host::aligned(weight_scale, 16) &&
+                (bias == nullptr || h3host::aligned(bias, 16));
   return launch<EPI_SWIGLU>(q, w, m, n_packed / 2, k, a, (cudaStream_t)stream);
 }
 
@@ -650,5 +1016,8 @@ extern "C" int h3_int8_gemm_row_dequant(const int8_t* q, const int8_t* w, int64_
   a.weight_scale = weight_scale;
   a.row = RowOut{out_kind, out, reinterpret_cast<__half*>(residual_f16), gate, gate_rows, labels,
                  nullptr};
+  a.scale_vec = n % 4 == 0 && h3host::aligned(weight_scale, 16);
+  a.res_vec = (n % 8 == 0) && h3host::aligned(residual_f16, 16) &&
+              (gate == nullptr || h3host::aligned(gate, 16));
   return launch<EPI_ROW_DEQUANT>(q, w, m, n, k, a, (cudaStream_t)stream);
 }

@@ -194,6 +194,17 @@ __global__ void expf_compare_kernel(const float* __restrict__ x, int64_t n,
   }
 }
 
+__global__ void silu_compare_kernel(const float* __restrict__ g, int64_t n,
+                                    float* __restrict__ fast, float* __restrict__ ieee,
+                                    float* __restrict__ cuda) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    fast[i] = silu_fast(g[i]);
+    ieee[i] = silu_ieee(g[i]);
+    if (cuda != nullptr) cuda[i] = __fdiv_rn(g[i], __fadd_rn(1.0f, expf(-g[i])));
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Launch helpers
 // ---------------------------------------------------------------------------
@@ -350,5 +361,16 @@ extern "C" int h3_expf_compare(const float* x, int64_t n, float* ours, float* cu
   if (int s = h3host::bind_device_of(x, &dev)) return s;
   const int grid = (int)std::min<int64_t>((n + 255) / 256, 4096);
   expf_compare_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(x, n, ours, cuda);
+  return h3host::check_launch();
+}
+
+extern "C" int h3_silu_compare(const float* g, int64_t n, float* fast, float* ieee,
+                               float* cuda, void* stream) {
+  if (g == nullptr || fast == nullptr || ieee == nullptr || n < 0) return H3_ERR_INVALID;
+  if (n == 0) return H3_OK;
+  int dev;
+  if (int s = h3host::bind_device_of(g, &dev)) return s;
+  const int grid = (int)std::min<int64_t>((n + 255) / 256, 4096);
+  silu_compare_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(g, n, fast, ieee, cuda);
   return h3host::check_launch();
 }

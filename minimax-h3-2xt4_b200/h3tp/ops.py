@@ -328,3 +328,14 @@ def expf_compare(x: torch.Tensor):
     ref = torch.empty_like(x)
     N.call("h3_expf_compare", x.data_ptr(), x.numel(), ours.data_ptr(), ref.data_ptr(), _stream(x))
     return ours, ref
+
+
+def silu_compare(g: torch.Tensor):
+    """(fast, ieee, cuda_expf) evaluations of g / (1 + exp(-g)) on the device."""
+    g = _need(g, torch.float32, "g")
+    fast = torch.empty_like(g)
+    ieee = torch.empty_like(g)
+    cuda = torch.empty_like(g)
+    N.call("h3_silu_compare", g.data_ptr(), g.numel(), fast.data_ptr(), ieee.data_ptr(),
+           cuda.data_ptr(), _stream(g))
+    return fast, ieee, cuda

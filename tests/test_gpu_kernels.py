@@ -57,6 +57,54 @@ def test_expf_matches_oracle_on_all_fp16_inputs(cuda_device, oracle):
     _bits_equal(_np(ours), oracle.expf(x))
 
 
+def test_expf_disagreement_with_cuda_expf_is_reported(cuda_device, oracle):
+    """The path's exponential differs from CUDA's expf (which the reference calls) on
+    a small fraction of inputs; measured here over every finite fp16 gate value."""
+    from h3tp import ops
+    h = np.arange(65536, dtype=np.uint32).astype(np.uint16).view(np.float16).astype(np.float32)
+    x = -h[np.isfinite(h)]
+    ours, cuda = ops.expf_compare(_t(x, cuda_device))
+    ours, cuda = _np(ours), _np(cuda)
+    differ = np.count_nonzero(ours.view(np.uint32) != cuda.view(np.uint32))
+    frac = differ / x.size
+    print(f"h3_expf vs CUDA expf on {x.size} fp16 inputs: {differ} differ ({frac:.4%})")
+    ulp = np.abs(ours.view(np.int32).astype(np.int64) - cuda.view(np.int32).astype(np.int64))
+    fin = np.isfinite(ours) & np.isfinite(cuda) & (ours > 1e-37)
+    assert ulp[fin].max() <= 4, "CUDA expf is documented within a few ulp"
+
+
+def test_code_disagreement_vs_cuda_expf_swiglu(cuda_device, oracle):
+    """Effect of the exponential on the INT8 codes: the reference's SwiGLU with CUDA
+    expf, rotated and quantised by the oracle, against the path's codes."""
+    from h3tp import ops
+    rng = np.random.default_rng(31)
+    x = _gateup(rng, 256, 4096)
+    g = x[:, :4096].astype(np.float32)
+    u = x[:, 4096:].astype(np.float32)
+    _, _, silu_cuda = ops.silu_compare(_t(g.ravel(), cuda_device))
+    act_cuda = (_np(silu_cuda).reshape(g.shape) * u).astype(np.float32)  # RN product, as the kernel
+    R_c, m_c = oracle.fc2_rotate(act_cuda, "act_f32")
+    q_c, _ = oracle.row_quantize(R_c, m_c)
+    q, _, _ = ops.swiglu_rotate_quantize_local(_t(x, cuda_device), "gateup_f16")
+    d = _np(q).astype(np.int32) - q_c.astype(np.int32)
+    rate = np.count_nonzero(d) / d.size
+    print(f"INT8 code disagreement vs CUDA-expf SwiGLU: {np.count_nonzero(d)} of {d.size} ({rate:.6%})")
+    assert np.abs(d).max() <= 1 and rate < 1e-3
+
+
+def test_silu_fast_path_is_bit_identical_on_all_fp16_gates(cuda_device, oracle):
+    from h3tp import ops
+    g = np.arange(65536, dtype=np.uint32).astype(np.uint16).view(np.float16).astype(np.float32)
+    fast, ieee, _ = ops.silu_compare(_t(g, cuda_device))
+    fast, ieee = _np(fast), _np(ieee)
+    nan = np.isnan(g)
+    assert np.isnan(fast[nan]).all() and np.isnan(ieee[nan]).all()
+    _bits_equal(fast[~nan], ieee[~nan])
+    fin = np.isfinite(g)
+    ref = np.array([oracle.lib().h3o_swiglu(float(v), 1.0) for v in g[fin]], np.float32)
+    _bits_equal(fast[fin], ref)
+
+
 # ----------------------------------------------------------------------------
 # FC2 producer
 # ----------------------------------------------------------------------------
