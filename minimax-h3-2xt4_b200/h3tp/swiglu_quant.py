@@ -51,6 +51,9 @@ def prepare(x: torch.Tensor, comm, mode: str = "fused_stored", *, consume_input:
     if mode not in MODES:
         raise ValueError(mode)
     kind, kl = input_kind(x, local_k)
+    if kl % 256 or kl == 0:
+        # checked on every rank before the MAX collective (tilelang_swiglu_quant.py:16)
+        raise ValueError("Whole regular ConvRot256 groups required")
     flat = x.reshape(-1, x.shape[-1]).contiguous()
     if C.world_of(comm) == 1:
         q, s, _ = ops.swiglu_rotate_quantize_local(flat, kind, division)

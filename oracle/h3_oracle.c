@@ -348,6 +348,16 @@ EXPORT void h3o_dequantize_i32(const int32_t* acc, int64_t rows, int64_t width, 
     }
 }
 
+/* gated_add of h3_tensor_flow.py:145-152 (gate_kernel, tilelang_dit_fusion.py:39-53)
+ * with an fp32 branch rounded to fp16 first: X = f16(fma(f16(y), G[label], X)). */
+EXPORT void h3o_gated_add(const float* y, int64_t rows, int64_t width, uint16_t* residual,
+                          const float* gate, const int32_t* labels) {
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t c = 0; c < width; ++c)
+      row_out(2, NULL, residual, gate, labels, r, c, width, y[r * width + c]);
+}
+
 /* shift_for of tilelang_transport_tradeoffs.py:20-22 on the full reduction length. */
 EXPORT int h3o_transport_shift(int64_t full_k) {
   if (full_k <= 0) return 0;

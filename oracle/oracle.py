@@ -48,6 +48,7 @@ def lib() -> ctypes.CDLL:
         L.h3o_fp16_decode.argtypes = [P, I64, I, P]
         L.h3o_row_reduce_finish.argtypes = [P, I, I64, I64, I64, I, P, P, I, P, P, P, P]
         L.h3o_dequantize_i32.argtypes = [P, I64, I64, P, P, I64, P, I, P, P, P, P]
+        L.h3o_gated_add.argtypes = [P, I64, I64, P, P, P]
         L.h3o_transport_shift.argtypes = [I64]
         L.h3o_transport_shift.restype = I
         _LIB = L
@@ -227,6 +228,17 @@ def dequantize_i32(acc, row_scale, weight_scale, bias=None, out="f32", residual=
         _p(None if gate is None else _c(gate, np.float32)),
         _p(None if labels is None else _c(labels, np.int32)))
     return residual if o == 2 else Y
+
+
+def gated_add(y, residual, gate=None, labels=None):
+    """X = f16(fma(f16(y), G[label], X)) in place on `residual` (fp16, contiguous)."""
+    y = _c(y, np.float32)
+    rows, width = y.shape
+    assert residual.dtype == np.float16 and residual.flags.c_contiguous and residual.shape == y.shape
+    lib().h3o_gated_add(_p(y), rows, width, _p(residual),
+                        _p(None if gate is None else _c(gate, np.float32)),
+                        _p(None if labels is None else _c(labels, np.int32)))
+    return residual
 
 
 # ----------------------------------------------------------------------------

@@ -1,0 +1,100 @@
+"""Host-side API contracts that need no GPU: operator policy values and validation,
+module constructors and parameter layouts (tp_dit.py:25-162), dispatch guards, and the
+absence of any CPU fallback in the kernel wrappers."""
+import dataclasses
+
+import pytest
+import torch
+
+
+def test_policy_defaults_and_validation():
+    from h3tp.h3_operator_policy import H3OperatorPolicy
+    p = H3OperatorPolicy()
+    assert p.row_linear_backend == "b200_scaled_fp16" and p.scaled_transport
+    assert p.fc2_quantizer in ("fused_stored", "fused_recompute")
+    assert p.column_linear_backend == "b200"
+    # the reference's own values stay accepted (h3_operator_policy.py:9-41)
+    ref = H3OperatorPolicy(row_linear_backend="tilelang_scaled_fp16", fc2_quantizer="fused_stored",
+                           column_linear_backend="cuda_int8_tilelang")
+    assert ref.scaled_transport
+    assert not H3OperatorPolicy(row_linear_backend="native").scaled_transport
+    for bad in (dict(row_linear_backend="x"), dict(fc2_quantizer="x"), dict(column_linear_backend="x"),
+                dict(row_transport="ring"), dict(quant_division="approx"), dict(dit_fused_row_gate=1)):
+        with pytest.raises(ValueError):
+            H3OperatorPolicy(**bad)
+    with pytest.raises(dataclasses.FrozenInstanceError):
+        p.fc2_quantizer = "native"
+
+
+def test_tensor_flow_policy():
+    from h3tp.h3_tensor_flow import TensorFlowPolicy
+    assert TensorFlowPolicy().divisor == 512.0
+    with pytest.raises(ValueError):
+        TensorFlowPolicy(residual_exponent=13)
+    with pytest.raises(ValueError):
+        TensorFlowPolicy(mode="fp8")
+
+
+def test_module_parameter_layouts():
+    from h3tp.tp_dit import ColumnParallelLinearINT8, RowParallelLinearINT8
+    c = ColumnParallelLinearINT8(512, 3 * 1024, rank=1, world_size=4, components=3, device="cpu")
+    assert c.weight.shape == (768, 512) and c.weight.dtype == torch.int8
+    assert c.weight_scale.shape == (768, 1) and c.weight_scale.dtype == torch.float32
+    assert not c.weight.requires_grad
+    r = RowParallelLinearINT8(8192, 3072, rank=3, world_size=8, device="cpu")
+    assert r.weight.shape == (3072, 1024) and r.weight_scale.shape == (3072, 1)
+    full = torch.arange(3072 * 8192, dtype=torch.int64).remainder(251).sub(125).to(torch.int8).reshape(3072, 8192)
+    r.load_shard_from_full(full, torch.ones(3072, 1))
+    assert torch.equal(r.weight, full[:, 3 * 1024:4 * 1024])
+    with pytest.raises(AssertionError):
+        RowParallelLinearINT8(1000, 64, world_size=3, device="cpu")
+
+
+def test_row_parallel_requires_reduction_and_group():
+    from h3tp.tp_dit import RowParallelLinearINT8
+    r = RowParallelLinearINT8(512, 64, rank=0, world_size=2, device="cpu")
+    with pytest.raises(ValueError):
+        r(torch.zeros(3, 256, dtype=torch.float16), reduce_sum=False)
+    with pytest.raises(RuntimeError):
+        r(torch.zeros(3, 256, dtype=torch.float16))  # no initialised TP group of 2
+
+
+def test_kernel_wrappers_have_no_cpu_fallback():
+    from h3tp import ops
+    q = torch.zeros((4, 64), dtype=torch.int8)
+    with pytest.raises(ValueError, match="no CPU fallback"):
+        ops.int8_gemm_i32(q, q)
+    with pytest.raises(ValueError, match="no CPU fallback"):
+        ops.column_quantize(torch.zeros((4, 256), dtype=torch.float16))
+    with pytest.raises(ValueError, match="no CPU fallback"):
+        ops.swiglu_rotate_quantize_local(torch.zeros((4, 512), dtype=torch.float16))
+
+
+def test_fc2_input_classification():
+    from h3tp.swiglu_quant import input_kind, supported
+    assert input_kind(torch.zeros(2, 1024, dtype=torch.float16), 512) == ("gateup_f16", 512)
+    assert input_kind(torch.zeros(2, 512, dtype=torch.float32), 512) == ("act_f32", 512)
+    assert input_kind(torch.zeros(2, 512, dtype=torch.float16), 512) == ("act_f16", 512)
+    with pytest.raises(ValueError):
+        input_kind(torch.zeros(2, 1024, dtype=torch.float32), 512)
+    with pytest.raises(ValueError):
+        input_kind(torch.zeros(2, 512, dtype=torch.bfloat16), 512)
+    w = torch.zeros(128, 512, dtype=torch.int8)
+    assert not supported(torch.zeros(2, 1024, dtype=torch.float16), w, torch.ones(128), 2, 256)  # CPU
+
+
+def test_row_blocks_cover_rows_once():
+    from h3tp.comm import row_blocks
+    for rows in (0, 1, 7, 37, 32768):
+        for world in (1, 2, 3, 4, 8):
+            blocks = row_blocks(rows, world)
+            assert len(blocks) == world
+            cover = [i for a, b in blocks for i in range(a, b)]
+            assert cover == list(range(rows))
+
+
+def test_transport_shift_generalisation():
+    from h3tp import ops, transport
+    assert transport.shift_for(7168) == 12 and transport.shift_for(3584) == 11
+    assert transport.shift_for(8192 // 8, 8) == transport.shift_for(8192 // 2, 2) == 12
+    assert ops.transport_shift(3072) == 10
