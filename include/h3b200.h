@@ -217,6 +217,13 @@ int h3_expf_compare(const float* x, int64_t n, float* ours, float* cuda, void* s
 int h3_silu_compare(const float* g, int64_t n, float* fast, float* ieee, float* cuda,
                     void* stream);
 
+/* INT8 codes of x[i] / scale[i] two ways: fast[i] as the kernels compute them
+ * (one correctly rounded reciprocal per scale, a Markstein quotient correction and
+ * magic-number rounding), ieee[i] with IEEE division, rintf and a float-to-int
+ * conversion (tilelang_row_quant.py:169-173, division 'rn').  They must agree. */
+int h3_quant_compare(const float* x, const float* scale, int64_t n, int8_t* fast,
+                     int8_t* ieee, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

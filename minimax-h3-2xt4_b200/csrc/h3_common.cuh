@@ -48,7 +48,10 @@ H3_DEV void exp_core(float xc, float& y, int& ni) {
   const float l2e = f32_bits(0x3fb8aa3bu);       // float32(1/ln 2)
   const float ln2_hi = f32_bits(0x3f317200u);    // 16 significant bits
   const float ln2_lo = f32_bits(0x35bfbe8eu);    // float32(ln2 - ln2_hi)
-  const float n = rintf(__fmul_rn(xc, l2e));
+  // n = rint(xc / ln2) by the 1.5 * 2^23 addition (|xc / ln2| < 2^22), integer from
+  // the low mantissa bits
+  const float big = __fadd_rn(__fmul_rn(xc, l2e), 12582912.0f);
+  const float n = __fadd_rn(big, -12582912.0f);
   const float r1 = __fmaf_rn(-n, ln2_hi, xc);                // exact
   const float r = __fmaf_rn(-n, ln2_lo, r1);                 // rounded reduced argument
   const float corr = __fmaf_rn(-n, ln2_lo, __fadd_rn(r1, -r));  // its rounding error
@@ -62,7 +65,7 @@ H3_DEV void exp_core(float xc, float& y, int& ni) {
   const float hi = __fadd_rn(1.0f, r);
   const float lo = __fadd_rn(r, -__fadd_rn(hi, -1.0f));      // exact error of 1 + r
   y = __fadd_rn(hi, __fadd_rn(lo, s));
-  ni = (int)n;
+  ni = __float_as_int(big) - 0x4B400000;
 }
 
 H3_DEV float h3_expf(float x) {
@@ -140,6 +143,32 @@ H3_DEV int8_t quantize_code(float x, float scale, int division) {
   const float rounded = rintf(scaled);
   const float clipped = fminf(127.0f, fmaxf(-128.0f, rounded));
   return (int8_t)(int)clipped;
+}
+
+// x / scale, correctly rounded, from inv = RN(1 / scale) (computed once per row): the
+// quotient correction step of P. Markstein, "Computation of elementary functions on the
+// IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990 - with a correctly
+// rounded reciprocal and a first quotient within one ulp, RN(q0 + (x - q0*scale)*inv)
+// is RN(x / scale); the remainder is exact in one FMA.  Infinite and NaN quotients
+// take q0, which is then the IEEE result (scale is finite and >= 1e-30).
+H3_DEV float div_by_scale(float x, float scale, float inv) {
+  const float q0 = __fmul_rn(x, inv);
+  const float r = __fmaf_rn(-q0, scale, x);
+  const float q1 = __fmaf_rn(r, inv, q0);
+  return fabsf(q0) < __uint_as_float(0x7f800000u) ? q1 : q0;
+}
+
+// The same code as quantize_code(x, scale, 0) without conversion-unit work: clamping
+// before rounding gives the same integer (rint is monotone and the bounds are
+// integers), and adding 1.5 * 2^23 rounds |t| <= 128 to the nearest integer, ties to
+// even, leaving it in the low mantissa bits.
+H3_DEV int8_t quantize_code_rn(float x, float scale, float inv) {
+  const float t = fminf(127.0f, fmaxf(-128.0f, div_by_scale(x, scale, inv)));
+  return (int8_t)(__float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000);
+}
+
+H3_DEV int8_t quantize_code_mode(float x, float scale, float inv, int division) {
+  return division ? quantize_code(x, scale, 1) : quantize_code_rn(x, scale, inv);
 }
 
 // ---------------------------------------------------------------------------

@@ -104,13 +104,14 @@ __global__ void __launch_bounds__(512) swiglu_rotate_kernel(
       scale = row_scale_from_max(__ldg(row_max_in + row));
     }
     if (MODE == MODE_QUANT || MODE == MODE_LOCAL) {
+      const float inv = __fdiv_rn(1.0f, scale);
 #pragma unroll
       for (int j = 0; j < NB; ++j) {
         const int64_t blk = tid + (int64_t)j * blockDim.x;
         if (blk < blocks) {
           int8_t c[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) c[i] = quantize_code(v[j][i], scale, division);
+          for (int i = 0; i < 16; ++i) c[i] = quantize_code_mode(v[j][i], scale, inv, division);
           store_int8x16(q + row * width + blk * 16, c);
         }
       }
@@ -156,13 +157,14 @@ __global__ void __launch_bounds__(512) column_quantize_kernel(
     }
     const float m = block_reduce_max(local_max, red);
     const float scale = row_scale_from_max(m);
+    const float inv = __fdiv_rn(1.0f, scale);
 #pragma unroll
     for (int j = 0; j < NB; ++j) {
       const int64_t blk = tid + (int64_t)j * blockDim.x;
       if (blk < blocks) {
         int8_t c[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) c[i] = quantize_code(v[j][i], scale, H3_DIV_RN);
+        for (int i = 0; i < 16; ++i) c[i] = quantize_code_rn(v[j][i], scale, inv);
         store_int8x16(q + row * k + blk * 16, c);
       }
     }
@@ -180,7 +182,8 @@ __global__ void row_quantize_kernel(const float* __restrict__ x, int64_t rows, i
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / width, c = i - r * width;
     const float scale = row_scale_from_max(__ldg(row_max + r));
-    q[i] = quantize_code(__ldg(x + r * stride + start + c), scale, division);
+    const float inv = __fdiv_rn(1.0f, scale);
+    q[i] = quantize_code_mode(__ldg(x + r * stride + start + c), scale, inv, division);
     if (c == 0) scale_out[r] = scale;
   }
 }
@@ -202,6 +205,16 @@ __global__ void silu_compare_kernel(const float* __restrict__ g, int64_t n,
     fast[i] = silu_fast(g[i]);
     ieee[i] = silu_ieee(g[i]);
     if (cuda != nullptr) cuda[i] = __fdiv_rn(g[i], __fadd_rn(1.0f, expf(-g[i])));
+  }
+}
+
+__global__ void quant_compare_kernel(const float* __restrict__ x, const float* __restrict__ scale,
+                                     int64_t n, int8_t* __restrict__ fast, int8_t* __restrict__ ieee) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float s = scale[i];
+    fast[i] = quantize_code_rn(x[i], s, __fdiv_rn(1.0f, s));
+    ieee[i] = quantize_code(x[i], s, H3_DIV_RN);
   }
 }
 
@@ -372,5 +385,17 @@ extern "C" int h3_silu_compare(const float* g, int64_t n, float* fast, float* ie
   if (int s = h3host::bind_device_of(g, &dev)) return s;
   const int grid = (int)std::min<int64_t>((n + 255) / 256, 4096);
   silu_compare_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(g, n, fast, ieee, cuda);
+  return h3host::check_launch();
+}
+
+extern "C" int h3_quant_compare(const float* x, const float* scale, int64_t n, int8_t* fast,
+                                int8_t* ieee, void* stream) {
+  if (x == nullptr || scale == nullptr || fast == nullptr || ieee == nullptr || n < 0)
+    return H3_ERR_INVALID;
+  if (n == 0) return H3_OK;
+  int dev;
+  if (int s = h3host::bind_device_of(x, &dev)) return s;
+  const int grid = (int)std::min<int64_t>((n + 255) / 256, (int64_t)h3host::sm_count(dev) * 16);
+  quant_compare_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(x, scale, n, fast, ieee);
   return h3host::check_launch();
 }

@@ -55,6 +55,7 @@ SIGNATURES = {
     "h3_gated_add": [_P, _I, _I64, _I64, _P, _P, _I64, _P, _P],
     "h3_expf_compare": [_P, _I64, _P, _P, _P],
     "h3_silu_compare": [_P, _I64, _P, _P, _P, _P],
+    "h3_quant_compare": [_P, _P, _I64, _P, _P, _P],
 }
 _RESTYPES = {"h3_status_string": ctypes.c_char_p}
 

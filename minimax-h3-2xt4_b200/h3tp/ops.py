@@ -339,3 +339,16 @@ def silu_compare(g: torch.Tensor):
     N.call("h3_silu_compare", g.data_ptr(), g.numel(), fast.data_ptr(), ieee.data_ptr(),
            cuda.data_ptr(), _stream(g))
     return fast, ieee, cuda
+
+
+def quant_compare(x: torch.Tensor, scale: torch.Tensor):
+    """(kernel codes, IEEE-division codes) of x / scale, elementwise."""
+    x = _need(x, torch.float32, "x")
+    scale = _need(scale, torch.float32, "scale")
+    if scale.numel() != x.numel():
+        raise ValueError("one scale per value")
+    fast = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+    ieee = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+    N.call("h3_quant_compare", x.data_ptr(), scale.data_ptr(), x.numel(), fast.data_ptr(),
+           ieee.data_ptr(), _stream(x))
+    return fast, ieee

@@ -105,6 +105,35 @@ def test_silu_fast_path_is_bit_identical_on_all_fp16_gates(cuda_device, oracle):
     _bits_equal(fast[fin], ref)
 
 
+def test_quantizer_division_identity(cuda_device):
+    """The kernels' code path (Markstein-corrected quotient from a per-row reciprocal,
+    magic-number rounding) equals IEEE division + rintf + clamp on tens of millions of
+    (x, scale) pairs, including exact half-way quotients and non-finite inputs."""
+    from h3tp import ops
+    g = torch.Generator(device=cuda_device).manual_seed(5)
+    n = 1 << 24
+    for trial in range(4):
+        e = torch.rand(n, device=cuda_device, generator=g) * 200 - 100
+        scale = torch.exp2(e).float()
+        x = (torch.rand(n, device=cuda_device, generator=g) * 262 - 131) * scale
+        fast, ieee = ops.quant_compare(x.float(), scale)
+        assert torch.equal(fast, ieee), int((fast != ieee).sum())
+    # exact ties (k + 1/2) * 2^e and their neighbours, scale a power of two
+    k = torch.arange(-130, 131, device=cuda_device, dtype=torch.float32)
+    es = torch.arange(-60, 61, device=cuda_device, dtype=torch.float32)
+    scale = torch.exp2(es)[:, None].expand(-1, k.numel()).reshape(-1).contiguous()
+    x = ((k + 0.5)[None, :] * torch.exp2(es)[:, None]).reshape(-1).contiguous()
+    for xx in (x, torch.nextafter(x, torch.full_like(x, float("inf"))),
+               torch.nextafter(x, torch.full_like(x, -float("inf")))):
+        fast, ieee = ops.quant_compare(xx, scale)
+        assert torch.equal(fast, ieee)
+    special = torch.tensor([0.0, -0.0, float("inf"), -float("inf"), float("nan"), 1e-45, -3e38, 3e38],
+                           device=cuda_device)
+    for s_ in (1e-30, 1.0, 3e38 / 127):
+        fast, ieee = ops.quant_compare(special, torch.full_like(special, s_))
+        assert torch.equal(fast, ieee), (s_, fast.tolist(), ieee.tolist())
+
+
 # ----------------------------------------------------------------------------
 # FC2 producer
 # ----------------------------------------------------------------------------
