@@ -202,6 +202,33 @@ int h3_gated_add(const void* branch, int branch_kind, int64_t rows, int64_t widt
                  const int32_t* labels, void* stream);
 
 /* ----------------------------------------------------------------------------
+ * Column linear without allocation.  No counterpart in the reference: added for
+ * callers that may not allocate device memory (code running during CUDA graph
+ * capture, runtimes that budget all device memory through their own pool, paths that
+ * cannot afford cudaMalloc's synchronisation).
+ * ------------------------------------------------------------------------- */
+
+/* Bytes of the file-scope static __device__ scratch array that every GPU loading
+ * this library holds until the process exits. */
+#define H3_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* The column path of h3_column_quantize followed by h3_int8_gemm_column in one call
+ * that allocates nothing: the INT8 codes, the row scales and the error word live in
+ * the static scratch array.  Requires 256 + roundup256(4*m) + m*k <=
+ * H3_NOALLOC_SCRATCH_BYTES (e.g. m*k up to ~32 MiB) and returns H3_ERR_INVALID,
+ * launching nothing, beyond that.  The first call on a device looks the array's
+ * device address up (cudaGetSymbolAddress); make that first call before any stream
+ * capture.  All calls on a device share the array: calls whose GPU work overlaps race
+ * and must be serialised by the caller (one stream, or events).
+ * h3_column_linear_noalloc_error reads (without clearing) the error word of the last
+ * call; the next call clears it. */
+int h3_column_linear_noalloc(const void* x_f16, int64_t m, int64_t k, int convrot,
+                             const int8_t* w, int64_t n, const float* weight_scale,
+                             int64_t weight_scale_len, const float* bias, void* out_f16,
+                             void* stream);
+int h3_column_linear_noalloc_error(int device, int* code);
+
+/* ----------------------------------------------------------------------------
  * Diagnostics
  * ------------------------------------------------------------------------- */
 

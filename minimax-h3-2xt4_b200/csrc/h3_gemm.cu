@@ -23,6 +23,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <mutex>
+
 #include "h3_common.cuh"
 
 namespace h3 {
@@ -1020,4 +1022,129 @@ extern "C" int h3_int8_gemm_row_dequant(const int8_t* q, const int8_t* w, int64_
   a.res_vec = (n % 8 == 0) && h3host::aligned(residual_f16, 16) &&
               (gate == nullptr || h3host::aligned(gate, 16));
   return launch<EPI_ROW_DEQUANT>(q, w, m, n, k, a, (cudaStream_t)stream);
+}
+
+// ---------------------------------------------------------------------------
+// Column linear that allocates nothing.
+//
+// For callers that must not allocate device memory: code running while a CUDA
+// stream is being captured into a graph (an allocation there is illegal or breaks
+// the capture), runtimes that account for every byte of device memory through their
+// own pool (the ComfyUI rank worker budgets weights and activations; an allocation
+// behind its back defeats that budget), and latency-critical paths where
+// cudaMalloc's implicit synchronisation is unacceptable.  The activation codes, the
+// row scales and the device error word live in one file-scope static __device__
+// array of H3_NOALLOC_SCRATCH_BYTES, held by every GPU that loads this library until
+// the process exits.  Every call on a device shares that array and leaves its
+// contents behind, so calls whose GPU work overlaps (different streams, or several
+// host threads) race with each other.
+// ---------------------------------------------------------------------------
+namespace h3 {
+namespace noalloc {
+
+static __device__ __align__(256) uint8_t g_scratch[H3_NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_scratch for each device, looked up once with that device
+// current.  In host code g_scratch names a host-side shadow, not device memory, so
+// only the address returned by cudaGetSymbolAddress may be handed to a kernel.
+static uint8_t* scratch_ptr(int dev) {
+  static uint8_t* cache[64] = {nullptr};
+  static std::mutex mu;
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_scratch) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    cache[dev] = static_cast<uint8_t*>(p);
+  }
+  return cache[dev];
+}
+
+static int64_t align256(int64_t b) { return (b + 255) / 256 * 256; }
+
+}  // namespace noalloc
+}  // namespace h3
+
+extern "C" int h3_column_linear_noalloc(const void* x_f16, int64_t m, int64_t k, int convrot,
+                                        const int8_t* w, int64_t n, const float* weight_scale,
+                                        int64_t weight_scale_len, const float* bias,
+                                        void* out_f16, void* stream) {
+  using namespace h3::noalloc;
+  if (x_f16 == nullptr || w == nullptr || weight_scale == nullptr || out_f16 == nullptr ||
+      m < 0 || k <= 0 || n <= 0 || k % 16 != 0 ||
+      (weight_scale_len != 1 && weight_scale_len != n) || !h3host::aligned(out_f16, 16) ||
+      !h3host::aligned(w, 16))
+    return H3_ERR_INVALID;
+  // layout: [error word | row scales | codes], each 256-byte aligned
+  const int64_t scale_off = 256;
+  const int64_t code_off = scale_off + align256(m * 4);
+  if (m > ((int64_t)1 << 31) || code_off + m * k > (int64_t)H3_NOALLOC_SCRATCH_BYTES)
+    return H3_ERR_INVALID;  // beyond the static scratch: use h3_column_quantize + h3_int8_gemm_column
+  if (m == 0) return H3_OK;
+  int dev;
+  if (int s = h3host::bind_device_of(x_f16, &dev)) return s;
+  if (!device_is_sm100(dev)) return H3_ERR_UNSUPPORTED;
+  uint8_t* base = scratch_ptr(dev);
+  if (base == nullptr) return H3_ERR_CUDA;
+  int* err = reinterpret_cast<int*>(base);
+  float* row_scale = reinterpret_cast<float*>(base + scale_off);
+  int8_t* q = reinterpret_cast<int8_t*>(base + code_off);
+  cudaStream_t st = (cudaStream_t)stream;
+  // the error word is the only scratch that must start at zero; codes and scales are
+  // rewritten in full below
+  if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess) return H3_ERR_CUDA;
+  if (int s = h3_column_quantize(x_f16, m, k, convrot, q, row_scale, stream)) return s;
+
+  // GEMM + ordered column epilogue, as h3_int8_gemm_column with the static error word
+  Args args = blank_args();
+  args.out = out_f16;
+  args.row_scale = row_scale;
+  args.weight_scale = weight_scale;
+  args.scalar_w = weight_scale_len == 1;
+  args.bias = bias;
+  args.scale_vec = n % 4 == 0 && h3host::aligned(weight_scale, 16);
+  const bool pair = m > BM;
+  CUtensorMap tA, tB;
+  if (!make_map(&tA, q, m, k, BM)) return H3_ERR_INVALID;
+  if (!make_map(&tB, w, n, k, pair ? BN / 2 : BN)) return H3_ERR_INVALID;
+  args.M = m;
+  args.N = n;
+  args.K = k;
+  args.tiles_m = (int)((m + (pair ? BM2 : BM) - 1) / (pair ? BM2 : BM));
+  args.tiles_n = (int)((n + BN - 1) / BN);
+  args.num_kb = (int)((k + BK - 1) / BK);
+  args.err = err;
+  args.row.err = err;
+  const int64_t tiles = (int64_t)args.tiles_m * args.tiles_n;
+  const int sms = h3host::sm_count(dev);
+  if (pair) {
+    if (cudaFuncSetAttribute(gemm_i8_pair_kernel<EPI_COLUMN>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES) != cudaSuccess)
+      return H3_ERR_CUDA;
+    const int grid = 2 * (int)std::min<int64_t>(tiles, sms / 2);
+    gemm_i8_pair_kernel<EPI_COLUMN><<<grid, THREADS, SMEM2_BYTES, st>>>(tA, tB, tB, args);
+  } else {
+    if (cudaFuncSetAttribute(gemm_i8_kernel<EPI_COLUMN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             SMEM_BYTES) != cudaSuccess)
+      return H3_ERR_CUDA;
+    const int grid = (int)std::min<int64_t>(tiles, sms);
+    gemm_i8_kernel<EPI_COLUMN><<<grid, THREADS, SMEM_BYTES, st>>>(tA, tB, tB, args);
+  }
+  return h3host::check_launch();
+}
+
+extern "C" int h3_column_linear_noalloc_error(int device, int* code) {
+  if (code == nullptr) return H3_ERR_INVALID;
+  *code = 0;
+  int cur = -1;
+  cudaGetDevice(&cur);
+  if (cur != device && cudaSetDevice(device) != cudaSuccess) return H3_ERR_CUDA;
+  uint8_t* base = h3::noalloc::scratch_ptr(device);
+  if (base == nullptr) return H3_ERR_CUDA;
+  if (cudaDeviceSynchronize() != cudaSuccess) return H3_ERR_CUDA;
+  return cudaMemcpy(code, base, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess ? H3_OK
+                                                                                    : H3_ERR_CUDA;
 }

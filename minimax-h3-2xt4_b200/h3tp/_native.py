@@ -56,6 +56,8 @@ SIGNATURES = {
     "h3_expf_compare": [_P, _I64, _P, _P, _P],
     "h3_silu_compare": [_P, _I64, _P, _P, _P, _P],
     "h3_quant_compare": [_P, _P, _I64, _P, _P, _P],
+    "h3_column_linear_noalloc": [_P, _I64, _I64, _I, _P, _I64, _P, _I64, _P, _P, _P],
+    "h3_column_linear_noalloc_error": [_I, _P],
 }
 _RESTYPES = {"h3_status_string": ctypes.c_char_p}
 
@@ -99,7 +101,8 @@ def check(status: int, name: str) -> None:
 
 # Entry points that enqueue exactly one kernel per successful call.
 _LAUNCHING = {n for n in SIGNATURES if n not in (
-    "h3_abi_version", "h3_status_string", "h3_device_error", "h3_transport_shift")}
+    "h3_abi_version", "h3_status_string", "h3_device_error", "h3_transport_shift",
+    "h3_column_linear_noalloc_error")}
 _launches = 0
 
 
