@@ -385,9 +385,11 @@ def run_ours(args):
                       "reasons": clk["reasons"]}
     if e2e is not None:
         line["e2e"] = e2e
-    if rank == 0 and not args.no_cpu:
+    if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(w1, s1, w2, s2, h_cpu, x_cpu)
     if comm:
+        from h3tp import peer
+        peer.release()
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:

@@ -202,6 +202,36 @@ int h3_gated_add(const void* branch, int branch_kind, int64_t rows, int64_t widt
                  const int32_t* labels, void* stream);
 
 /* ----------------------------------------------------------------------------
+ * Row transport over NVLink peer memory.  Replaces, for the residual form of the
+ * row output, the reference's NCCL fp16 SUM of the encoded partials
+ * (tilelang_transport_p2.py:57-58, tilelang_swiglu_quant.py:116-127) and the fused
+ * row-gate epilogue that follows it (tilelang_dit_fusion.py:57-77, 146-151), with the
+ * same arithmetic as h3_row_reduce_finish(out_kind = H3_OUT_RESIDUAL).
+ *
+ * bases[w] (w < world, world in {2, 4, 8}) is rank w's workspace buffer mapped into
+ * this process (every rank's buffer has the same layout; the caller maps them, e.g.
+ * with torch symmetric memory):
+ *   flags_off    1024 bytes of u32 flags, zeroed on every rank before the first call
+ *   partial_off  fp16 [rows, width] partial of that rank (h3_int8_gemm_row_encode)
+ *   block_off    fp16 [rows, width] finished rows of that rank's row block
+ * Rank r owns rows [r*per, min(rows, (r+1)*per)), per = ceil(rows / world).
+ * h3_peer_reduce: fixed rank-order reduction of the owned rows from every rank's
+ * partial, decode, dequant and gated residual update of those rows of residual_f16
+ * (also copied into this rank's block); h3_peer_gather: copies the peers' finished
+ * rows into residual_f16.  Every rank calls both, in that order, on one stream, with
+ * the same `epoch` (1, 2, 3, ... per call).  Waits for peers are bounded (2 s); a
+ * wait that gives up leaves H3_ERR_TIMEOUT in h3_device_error and the workspace must
+ * be re-created.  width % 8 == 0; pointers 16-byte aligned. */
+int h3_peer_reduce(const void* const* bases, int world, int rank, int64_t flags_off,
+                   int64_t partial_off, int64_t block_off, int64_t rows, int64_t width,
+                   int shift, const float* row_scale, const float* weight_scale,
+                   void* residual_f16, const float* gate, int64_t gate_rows,
+                   const int32_t* labels, uint32_t epoch, void* stream);
+int h3_peer_gather(const void* const* bases, int world, int rank, int64_t flags_off,
+                   int64_t block_off, int64_t rows, int64_t width, void* residual_f16,
+                   uint32_t epoch, void* stream);
+
+/* ----------------------------------------------------------------------------
  * Column linear without allocation.  No counterpart in the reference: added for
  * callers that may not allocate device memory (code running during CUDA graph
  * capture, runtimes that budget all device memory through their own pool, paths that

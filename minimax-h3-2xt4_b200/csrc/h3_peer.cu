@@ -1,0 +1,314 @@
+// Row transport over NVLink peer memory: the scaled-FP16 partial SUM of the row
+// parallel linear (tilelang_transport_p2.py:57-58, NCCL fp16 SUM) fused with its
+// epilogue (decode, FP32 dequant, gated residual; tilelang_dit_fusion.py:57-77).
+//
+// Every rank owns one buffer of the same layout, mapped into every other rank's
+// address space (torch symmetric memory); `bases[w]` is rank w's buffer as seen from
+// this process:
+//
+//   [flags_off]    ready[64] u32 | done[64] u32 | counter u32   (zeroed once at set-up)
+//   [partial_off]  fp16 [rows, width]   this rank's encoded partial (written by the
+//                                       row GEMM's encode epilogue)
+//   [block_off]    fp16 [rows, width]   finished residual rows of this rank's block
+//
+// One call with epoch e (the same on every rank, increasing by one per call):
+//   reduce kernel  each CTA stores e into ready[rank] of every rank (release, system
+//                  scope), waits until its own ready[w] >= e for every w, then sums the
+//                  partials of this rank's row block [row_begin, row_end) in rank
+//                  order 0..world-1 (fp32, one fp16 rounding at the end, the bits of an
+//                  NCCL fp16 SUM at world 2), decodes, dequantises and applies the
+//                  gated residual to those rows of the local residual, and copies the
+//                  finished rows into its block buffer.  The last CTA to finish stores
+//                  e into done[rank] of every rank.
+//   gather kernel  waits until done[w] >= e for every peer w and copies the peers'
+//                  finished rows from their block buffers into the local residual.
+//
+// Reuse across calls is ordered by the flags: a rank rewrites its partial only after
+// its gather of the previous call, which waited for every peer's done (so every peer
+// has finished reading it), and a rank rewrites its block buffer only after every peer
+// signalled ready for the new call (so every peer's previous gather has finished).
+// All waits are bounded (2 s of %globaltimer); a wait that gives up records
+// H3_ERR_TIMEOUT in the library's device error word, and a reduce that timed out
+// publishes no done flag, so the peers' gathers time out too rather than read
+// unfinished rows.
+
+#include "h3_common.cuh"
+
+namespace h3 {
+namespace peer {
+
+constexpr int MAX_WORLD = 8;
+constexpr int64_t READY = 0, DONE = 256, COUNTER = 512;
+constexpr unsigned long long TIMEOUT_NS = 2000000000ull;
+constexpr int THREADS = 256;
+
+struct Args {
+  uint64_t bases[MAX_WORLD];
+  int64_t flags_off, partial_off, block_off;
+  int world, rank;
+  int64_t rows, width, row_begin, row_end, per;
+  float up;
+  const float* row_scale;
+  const float* weight_scale;
+  __half* residual;
+  const float* gate;
+  int64_t gate_rows;
+  const int32_t* labels;
+  uint32_t epoch;
+  int* err;
+};
+
+H3_DEV uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+H3_DEV uint32_t* flag(const Args& a, int owner, int64_t region, int slot) {
+  return reinterpret_cast<uint32_t*>(a.bases[owner] + a.flags_off + region) + slot;
+}
+
+H3_DEV void store_release(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+H3_DEV uint32_t load_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Threads 0..world-1 each wait for one rank's flag in `region` of this rank's buffer;
+// returns (to every thread of the CTA) whether all of them arrived in time.
+H3_DEV bool wait_all(const Args& a, int64_t region, bool skip_self) {
+  bool ok = true;
+  if ((int)threadIdx.x < a.world && !(skip_self && (int)threadIdx.x == a.rank)) {
+    const uint32_t* f = flag(a, a.rank, region, threadIdx.x);
+    const uint64_t t0 = globaltimer();
+    while ((int32_t)(load_acquire(f) - a.epoch) < 0) {
+      if (globaltimer() - t0 > TIMEOUT_NS) {
+        ok = false;
+        break;
+      }
+      __nanosleep(32);
+    }
+  }
+  ok = __syncthreads_and(ok);
+  if (ok) asm volatile("fence.acq_rel.sys;" ::: "memory");
+  return ok;
+}
+
+H3_DEV uint4 load_peer(uint64_t base, int64_t off) {
+  return __ldcv(reinterpret_cast<const uint4*>(base + off));
+}
+
+// One 8-column chunk: rank-order fp32 sum of the partials, one fp16 rounding, decode,
+// dequant, then X = f16(fma(f32(f16(y)), G[lab], f32(X))).
+template <int W>
+H3_DEV uint4 finish_chunk(const Args& a, const uint4 (&u)[W], int64_t r, int64_t c0, uint4 x) {
+  float t[8];
+#pragma unroll
+  for (int w = 0; w < W; ++w) {
+    const __half2* h = reinterpret_cast<const __half2*>(&u[w]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(h[j]);
+      if (w == 0) {
+        t[2 * j] = f.x;
+        t[2 * j + 1] = f.y;
+      } else {
+        t[2 * j] = __fadd_rn(t[2 * j], f.x);
+        t[2 * j + 1] = __fadd_rn(t[2 * j + 1], f.y);
+      }
+    }
+  }
+  const float s = __ldg(a.row_scale + r);
+  const float4 w0 = __ldg(reinterpret_cast<const float4*>(a.weight_scale + c0));
+  const float4 w1 = __ldg(reinterpret_cast<const float4*>(a.weight_scale + c0) + 1);
+  const float ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  float g[8];
+  if (a.gate != nullptr) {
+    int64_t lab = a.labels ? (int64_t)__ldg(a.labels + r) : 0;
+    if (lab < 0 || lab >= a.gate_rows) {
+      atomicExch(a.err, H3_ERR_INVALID);
+      lab = 0;
+    }
+    const float4* gp = reinterpret_cast<const float4*>(a.gate + lab * a.width + c0);
+    const float4 g0 = __ldg(gp), g1 = __ldg(gp + 1);
+    g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w;
+    g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) g[j] = 1.0f;
+  }
+  __half2* xh = reinterpret_cast<__half2*>(&x);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float b[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int k = 2 * j + e;
+      const float reduced = __half2float(__float2half_rn(t[k]));
+      const int32_t restored = __float2int_rz(__fmul_rn(reduced, a.up));
+      const float y = __fmul_rn(__fmul_rn(__int2float_rn(restored), s), ws[k]);
+      b[e] = __half2float(__float2half_rn(y));
+    }
+    const float2 xf = __half22float2(xh[j]);
+    xh[j] = __floats2half2_rn(__fmaf_rn(b[0], g[2 * j], xf.x), __fmaf_rn(b[1], g[2 * j + 1], xf.y));
+  }
+  return x;
+}
+
+template <int W>
+__global__ void __launch_bounds__(THREADS) reduce_kernel(const Args a) {
+  // Phase 0: this rank's partial is complete (stream order); announce it to every rank.
+  if ((int)threadIdx.x < W) {
+    __threadfence_system();
+    store_release(flag(a, threadIdx.x, READY, a.rank), a.epoch);
+  }
+  const bool ok = wait_all(a, READY, false);
+  if (ok) {
+    const int64_t chunks = a.width >> 3;
+    const int64_t total = (a.row_end - a.row_begin) * chunks;
+    uint4* block = reinterpret_cast<uint4*>(a.bases[a.rank] + a.block_off);
+    uint4* res = reinterpret_cast<uint4*>(a.residual);
+    for (int64_t i = blockIdx.x * (int64_t)THREADS + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * THREADS) {
+      const int64_t r = a.row_begin + i / chunks;
+      const int64_t c0 = (i % chunks) << 3;
+      const int64_t e = r * chunks + (c0 >> 3);  // uint4 index of the chunk
+      uint4 u[W];
+#pragma unroll
+      for (int w = 0; w < W; ++w) u[w] = load_peer(a.bases[w], a.partial_off + e * 16);
+      const uint4 y = finish_chunk<W>(a, u, r, c0, res[e]);
+      res[e] = y;
+      block[e] = y;
+    }
+  } else if (threadIdx.x == 0) {
+    atomicExch(a.err, H3_ERR_TIMEOUT);
+  }
+  // Count this CTA (failures in the high half-word); the last one resets the counter
+  // and, when every CTA succeeded, publishes done to every rank.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    unsigned int* counter =
+        reinterpret_cast<unsigned int*>(a.bases[a.rank] + a.flags_off + COUNTER);
+    const unsigned int old = atomicAdd(counter, ok ? 1u : 0x10000u);
+    const unsigned int seen = (old & 0xffffu) + (old >> 16);
+    if (seen == gridDim.x - 1) {
+      const bool all_ok = ok && (old >> 16) == 0;
+      *reinterpret_cast<volatile unsigned int*>(counter) = 0;
+      __threadfence_system();
+      if (all_ok)
+        for (int w = 0; w < W; ++w) store_release(flag(a, w, DONE, a.rank), a.epoch);
+    }
+  }
+}
+
+template <int W>
+__global__ void __launch_bounds__(THREADS) gather_kernel(const Args a) {
+  if (!wait_all(a, DONE, true)) {
+    if (threadIdx.x == 0) atomicExch(a.err, H3_ERR_TIMEOUT);
+    return;
+  }
+  const int64_t chunks = a.width >> 3;
+  const int64_t own = a.row_end - a.row_begin;
+  const int64_t total = (a.rows - own) * chunks;
+  uint4* res = reinterpret_cast<uint4*>(a.residual);
+  for (int64_t i = blockIdx.x * (int64_t)THREADS + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * THREADS) {
+    int64_t r = i / chunks;
+    if (r >= a.row_begin) r += own;
+    const int owner = (int)(r / a.per);
+    const int64_t e = r * chunks + i % chunks;
+    res[e] = load_peer(a.bases[owner], a.block_off + e * 16);
+  }
+}
+
+template <int W>
+cudaError_t launch(const Args& a, int blocks, bool gather, cudaStream_t st) {
+  if (gather)
+    gather_kernel<W><<<blocks, THREADS, 0, st>>>(a);
+  else
+    reduce_kernel<W><<<blocks, THREADS, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+int run(const void* const* bases, int world, int rank, int64_t flags_off, int64_t partial_off,
+        int64_t block_off, int64_t rows, int64_t width, int shift, const float* row_scale,
+        const float* weight_scale, void* residual_f16, const float* gate, int64_t gate_rows,
+        const int32_t* labels, uint32_t epoch, bool gather, void* stream) {
+  if (bases == nullptr || residual_f16 == nullptr || (world != 2 && world != 4 && world != 8) ||
+      rank < 0 || rank >= world || rows < 0 || width <= 0 || width % 8 || epoch == 0 ||
+      flags_off < 0 || partial_off < 0 || block_off < 0 || flags_off % 16 ||
+      partial_off % 16 || block_off % 16 || !h3host::aligned(residual_f16, 16))
+    return H3_ERR_INVALID;
+  if (!gather) {
+    if (row_scale == nullptr || weight_scale == nullptr || shift < 0 || shift > 60 ||
+        !h3host::aligned(weight_scale, 16))
+      return H3_ERR_INVALID;
+    if (gate != nullptr &&
+        (gate_rows < 1 || (labels == nullptr && gate_rows != 1) || !h3host::aligned(gate, 16)))
+      return H3_ERR_INVALID;
+  }
+  Args a{};
+  for (int w = 0; w < world; ++w) {
+    if (bases[w] == nullptr || !h3host::aligned(bases[w], 16)) return H3_ERR_INVALID;
+    a.bases[w] = reinterpret_cast<uint64_t>(bases[w]);
+  }
+  int dev;
+  if (int s = h3host::bind_device_of(residual_f16, &dev)) return s;
+  a.flags_off = flags_off;
+  a.partial_off = partial_off;
+  a.block_off = block_off;
+  a.world = world;
+  a.rank = rank;
+  a.rows = rows;
+  a.width = width;
+  a.per = rows ? (rows + world - 1) / world : 1;
+  a.row_begin = std::min<int64_t>(rows, rank * a.per);
+  a.row_end = std::min<int64_t>(rows, (rank + 1) * a.per);
+  a.up = ldexpf(1.0f, shift);
+  a.row_scale = row_scale;
+  a.weight_scale = weight_scale;
+  a.residual = reinterpret_cast<__half*>(residual_f16);
+  a.gate = gate;
+  a.gate_rows = gate_rows;
+  a.labels = labels;
+  a.epoch = epoch;
+  a.err = h3host::error_word(dev);
+  if (a.err == nullptr) return H3_ERR_CUDA;
+  // Enough CTAs to keep every SM's load slots busy; the flags make any grid size safe
+  // (no CTA waits for another CTA of the same launch).
+  const int64_t items = (gather ? rows - (a.row_end - a.row_begin) : a.row_end - a.row_begin) *
+                        (width / 8);
+  const int blocks = (int)std::max<int64_t>(
+      1, std::min<int64_t>((items + THREADS - 1) / THREADS, (int64_t)h3host::sm_count(dev) * 8));
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e = world == 2 ? launch<2>(a, blocks, gather, st)
+                  : world == 4 ? launch<4>(a, blocks, gather, st)
+                               : launch<8>(a, blocks, gather, st);
+  return e == cudaSuccess ? H3_OK : H3_ERR_CUDA;
+}
+
+}  // namespace peer
+}  // namespace h3
+
+extern "C" int h3_peer_reduce(const void* const* bases, int world, int rank, int64_t flags_off,
+                              int64_t partial_off, int64_t block_off, int64_t rows,
+                              int64_t width, int shift, const float* row_scale,
+                              const float* weight_scale, void* residual_f16, const float* gate,
+                              int64_t gate_rows, const int32_t* labels, uint32_t epoch,
+                              void* stream) {
+  return h3::peer::run(bases, world, rank, flags_off, partial_off, block_off, rows, width, shift,
+                       row_scale, weight_scale, residual_f16, gate, gate_rows, labels, epoch,
+                       false, stream);
+}
+
+extern "C" int h3_peer_gather(const void* const* bases, int world, int rank, int64_t flags_off,
+                              int64_t block_off, int64_t rows, int64_t width, void* residual_f16,
+                              uint32_t epoch, void* stream) {
+  return h3::peer::run(bases, world, rank, flags_off, 0, block_off, rows, width, 0, nullptr,
+                       nullptr, residual_f16, nullptr, 0, nullptr, epoch, true, stream);
+}

@@ -30,6 +30,8 @@ OUT_RESIDUAL = 2
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _I = ctypes.c_int
+_U32 = ctypes.c_uint32
+_PP = ctypes.POINTER(ctypes.c_void_p)
 
 # name -> argtypes (all return int status unless listed in _RESTYPES)
 SIGNATURES = {
@@ -53,6 +55,9 @@ SIGNATURES = {
     "h3_row_reduce_finish": [_P, _I, _I64, _I64, _I64, _I, _P, _P, _I, _P, _P, _P, _I64, _P, _P],
     "h3_dequantize_i32": [_P, _I64, _I64, _P, _P, _I64, _P, _I, _P, _P],
     "h3_gated_add": [_P, _I, _I64, _I64, _P, _P, _I64, _P, _P],
+    "h3_peer_reduce": [_PP, _I, _I, _I64, _I64, _I64, _I64, _I64, _I, _P, _P, _P, _P, _I64, _P,
+                       _U32, _P],
+    "h3_peer_gather": [_PP, _I, _I, _I64, _I64, _I64, _I64, _P, _U32, _P],
     "h3_expf_compare": [_P, _I64, _P, _P, _P],
     "h3_silu_compare": [_P, _I64, _P, _P, _P, _P],
     "h3_quant_compare": [_P, _P, _I64, _P, _P, _P],

@@ -9,7 +9,11 @@ is added to each backend field.  The T4-only values map onto the B200 kernels:
                        'native' / 'owned_fp32' -> FP32 cast + full-gather exact route
   column_linear_backend 'preallocated' / 'cuda_int8_tilelang' / 'b200' -> B200 column GEMM
 New B200 fields:
-  row_transport   'rowblock' (deterministic reduce-scatter + all-gather) or 'allreduce'
+  row_transport   'p2p' (reduce + gather over NVLink peer memory, own kernels; the
+                  default), 'rowblock' (NCCL all_to_all + fixed-order reduce + all_gather)
+                  or 'allreduce' (NCCL fp16 SUM, the reference's form).  All three give
+                  the same bits; 'p2p' needs a torch.distributed NCCL group and the
+                  residual form of the row output, and uses 'rowblock' otherwise.
   quant_division  'rn' (IEEE, bit-exact with the CPU oracle) or 'fast' (__fdividef)
   fc1_swiglu_epilogue  FC1 stores the FP32 SwiGLU activation instead of fp16 [gate|up]
 """
@@ -38,7 +42,7 @@ class H3OperatorPolicy:
     dit_p0_b_inplace: bool = True
     dit_p0_a1_turing: bool = True
     dit_p0_c_local_rotation: bool = True
-    row_transport: str = "rowblock"
+    row_transport: str = "p2p"
     quant_division: str = "rn"
     fc1_swiglu_epilogue: bool = True
 
@@ -54,7 +58,7 @@ class H3OperatorPolicy:
             raise ValueError("Unknown FC2 quantizer")
         if self.column_linear_backend not in COLUMN_BACKENDS:
             raise ValueError("Unknown column linear backend")
-        if self.row_transport not in ("rowblock", "allreduce"):
+        if self.row_transport not in ("p2p", "rowblock", "allreduce"):
             raise ValueError("Unknown row transport")
         if self.quant_division not in ("rn", "fast"):
             raise ValueError("Unknown quantizer division")

@@ -6,6 +6,8 @@ the reference's shapes: activation scales [M, 1] fp32, weight scales [N, 1] fp32
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _native as N
@@ -187,14 +189,19 @@ def transport_shift(full_k: int) -> int:
     return int(N.load().h3_transport_shift(int(full_k)))
 
 
-def int8_gemm_row_encode(q, w, shift: int) -> torch.Tensor:
-    """INT8 GEMM + scaled-FP16 encode: f16(acc * 2^-shift), [M, N]."""
+def int8_gemm_row_encode(q, w, shift: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """INT8 GEMM + scaled-FP16 encode: f16(acc * 2^-shift), [M, N].  `out` (contiguous
+    fp16 [M, N], e.g. a peer-mapped transport buffer) receives the payload if given."""
     q = _need(q, torch.int8, "q", 2)
     w = _need(w, torch.int8, "weight", 2)
     M, K = q.shape
     if w.shape[1] != K:
         raise ValueError("Input and weight inner dimensions must match")
-    out = torch.empty((M, w.shape[0]), dtype=torch.float16, device=q.device)
+    if out is None:
+        out = torch.empty((M, w.shape[0]), dtype=torch.float16, device=q.device)
+    elif (out.dtype != torch.float16 or tuple(out.shape) != (M, w.shape[0])
+          or not out.is_contiguous() or out.device != q.device):
+        raise ValueError("out must be a contiguous fp16 [M, N] tensor on the input's device")
     N.call("h3_int8_gemm_row_encode", q.data_ptr(), w.data_ptr(), M, w.shape[0], K, int(shift),
            out.data_ptr(), _stream(q))
     return out
@@ -318,6 +325,35 @@ def gated_add(residual, branch, gate=None, labels=None):
     kind = N.OUT_F32 if b.dtype == torch.float32 else N.OUT_F16
     N.call("h3_gated_add", b.data_ptr(), kind, M, Nn, res.data_ptr(), _ptr(g), grows, _ptr(lab),
            _stream(b))
+    return residual
+
+
+def peer_reduce(bases, world: int, rank: int, flags_off: int, partial_off: int, block_off: int,
+                rows: int, width: int, shift: int, row_scale, weight_scale, residual,
+                gate=None, labels=None, epoch: int = 1):
+    """Reduce + fused gated-residual epilogue of this rank's row block over peer
+    memory (h3_peer_reduce); `bases` are the world buffer addresses (ints)."""
+    a = _vec(row_scale, rows, "row_scale")
+    ws = _vec(weight_scale, width, "weight_scale")
+    if not residual.is_contiguous():
+        raise ValueError("residual must be contiguous (updated in place)")
+    res, g, grows, lab = _gate_args(residual, gate, labels, rows, width)
+    arr = (ctypes.c_void_p * world)(*bases)
+    N.call("h3_peer_reduce", arr, world, rank, flags_off, partial_off, block_off, rows, width,
+           int(shift), a.data_ptr(), ws.data_ptr(), res.data_ptr(), _ptr(g), grows, _ptr(lab),
+           int(epoch), _stream(res))
+    return residual
+
+
+def peer_gather(bases, world: int, rank: int, flags_off: int, block_off: int, rows: int,
+                width: int, residual, epoch: int = 1):
+    """Copies the peers' finished row blocks into `residual` (h3_peer_gather)."""
+    res = _need(residual, torch.float16, "residual", 2)
+    if res.data_ptr() != residual.data_ptr() or tuple(res.shape) != (rows, width):
+        raise ValueError("residual must be a contiguous fp16 [rows, width] tensor")
+    arr = (ctypes.c_void_p * world)(*bases)
+    N.call("h3_peer_gather", arr, world, rank, flags_off, block_off, rows, width, res.data_ptr(),
+           int(epoch), _stream(res))
     return residual
 
 

@@ -1,0 +1,116 @@
+"""Peer-memory row transport: the B200 form of the FC2 / O-projection partial SUM.
+
+The reference sums the per-rank scaled-FP16 partials with NCCL's fp16 all-reduce and
+then runs the fused row-gate epilogue (tilelang_swiglu_quant.py:119-124,
+tilelang_dit_fusion.py:146-151).  Over NVSwitch every GPU can load from every peer's
+HBM directly, so here the exchange is two kernels of our own (csrc/h3_peer.cu):
+
+  1. the row GEMM's encode epilogue writes the partial straight into this rank's
+     peer-mapped buffer (no staging copy);
+  2. h3_peer_reduce: each rank loads its row block of every rank's partial from peer
+     memory, sums in rank order, decodes, dequantises and updates its rows of the
+     gated residual (the same bits as h3_row_reduce_finish);
+  3. h3_peer_gather: each rank copies the peers' finished rows into its residual.
+
+The buffers are torch symmetric memory (one allocation per rank, mapped into every
+rank); synchronisation is by epoch flags in the same buffers, with bounded waits.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+
+FLAGS_BYTES = 1024
+_ALIGN = 256
+
+
+def _group_name(group) -> str:
+    if isinstance(group, dist.ProcessGroup):
+        return group.group_name
+    return dist.group.WORLD.group_name
+
+
+def available(comm) -> bool:
+    """True when `comm` is a torch.distributed NCCL process group (or the default group
+    through the torch.distributed module) whose ranks can map each other's memory."""
+    try:
+        group = comm if isinstance(comm, dist.ProcessGroup) else None
+        if comm is not dist and group is None:
+            return False
+        if not dist.is_initialized():
+            return False
+        return dist.get_backend(group) == "nccl"
+    except Exception:
+        return False
+
+
+class PeerWorkspace:
+    """One symmetric buffer per rank: flags | partial fp16 [rows, width] | block fp16."""
+
+    def __init__(self, group, device: torch.device, width: int, rows: int):
+        import torch.distributed._symmetric_memory as symm
+
+        self.group = group
+        self.device = torch.device(device)
+        self.width = int(width)
+        self.capacity = int(rows)
+        part = -(-self.capacity * self.width * 2 // _ALIGN) * _ALIGN
+        self.partial_off = FLAGS_BYTES
+        self.block_off = FLAGS_BYTES + part
+        nbytes = FLAGS_BYTES + 2 * part
+        with torch.cuda.device(self.device):
+            self.buf = symm.empty(nbytes, dtype=torch.uint8, device=self.device)
+            self.buf[:FLAGS_BYTES].zero_()
+            self.handle = symm.rendezvous(self.buf, _group_name(group))
+            torch.cuda.synchronize(self.device)
+        self.world = int(self.handle.world_size)
+        self.rank = int(self.handle.rank)
+        self.bases = [int(p) for p in self.handle.buffer_ptrs]
+        self.epoch = 0
+        # every rank's flags are zero before any rank signals
+        dist.barrier(group=group if isinstance(group, dist.ProcessGroup) else None)
+
+    def partial(self, rows: int) -> torch.Tensor:
+        """This rank's fp16 [rows, width] partial, the row GEMM's encode output."""
+        n = rows * self.width
+        return self.buf[self.partial_off:self.partial_off + 2 * n].view(torch.float16).view(
+            rows, self.width)
+
+    def reduce_and_gather(self, rows: int, shift: int, row_scale, weight_scale, residual,
+                          gate=None, labels=None):
+        """Sums the partials written by every rank into `residual` (fp16 [rows, width],
+        updated in place on every rank)."""
+        self.epoch += 1
+        ops.peer_reduce(self.bases, self.world, self.rank, 0, self.partial_off, self.block_off,
+                        rows, self.width, shift, row_scale, weight_scale, residual, gate, labels,
+                        self.epoch)
+        ops.peer_gather(self.bases, self.world, self.rank, 0, self.block_off, rows, self.width,
+                        residual, self.epoch)
+        return residual
+
+
+_WORKSPACES: dict = {}
+
+
+def workspace(group, device, width: int, rows: int) -> PeerWorkspace:
+    """Cached per (group, device, width); re-created (a collective step on every rank,
+    which all take together since they see the same shapes) when `rows` outgrows it."""
+    key = (_group_name(group), torch.device(device), int(width))
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.capacity < rows:
+        if ws is not None:
+            torch.cuda.synchronize(ws.device)
+            dist.barrier(group=group if isinstance(group, dist.ProcessGroup) else None)
+        cap = max(int(rows), 0 if ws is None else 2 * ws.capacity)
+        ws = PeerWorkspace(group, device, width, cap)
+        _WORKSPACES[key] = ws
+    return ws
+
+
+def release() -> None:
+    """Drops the cached workspaces (call on every rank, before destroy_process_group)."""
+    for ws in _WORKSPACES.values():
+        torch.cuda.synchronize(ws.device)
+    _WORKSPACES.clear()

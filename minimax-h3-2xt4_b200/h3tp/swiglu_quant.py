@@ -22,6 +22,7 @@ import torch
 
 from . import comm as C
 from . import ops
+from . import peer as P
 from . import transport as T
 from .row_quant import label
 
@@ -110,6 +111,16 @@ def _finish_quantized(q, scale, weight, weight_scale, comm, scaled_transport=Tru
             return ops.int8_gemm_row_dequant(q, weight, scale, weight_scale, out_dtype)
     if scaled_transport:
         shift = T.shift_for(local_k, world)
+        if (transport == "p2p" and residual is not None and finish_fn is None
+                and residual.is_contiguous() and residual.shape[-1] % 8 == 0 and P.available(comm)):
+            # GEMM encode straight into the peer-mapped buffer, then the peer-memory
+            # reduce + gated residual + gather (csrc/h3_peer.cu).
+            rows = q.shape[0]
+            ws = P.workspace(comm, q.device, weight.shape[0], rows)
+            with label("int8_gemm_scaled_fp16_encode"):
+                ops.int8_gemm_row_encode(q, weight, shift, out=ws.partial(rows))
+            with label("scaled_fp16_peer_reduce_gather"):
+                return ws.reduce_and_gather(rows, shift, scale, weight_scale, residual, gate, labels)
         with label("int8_gemm_scaled_fp16_encode"):
             payload = ops.int8_gemm_row_encode(q, weight, shift)
         if finish_fn is not None:

@@ -93,7 +93,9 @@ def reduce_and_finish(payload: torch.Tensor, comm, shift: int, activation_scale,
         with label("scaled_fp16_fused_epilogue"):
             return ops.row_reduce_finish(payload, shift, activation_scale, weight_scale, out_dtype,
                                          residual=residual, gate=gate, labels=labels)
-    if transport != "rowblock":
+    if transport not in ("rowblock", "p2p"):
+        # 'p2p' reaches here only for the forms the peer kernels do not cover (no
+        # residual, or a non-NCCL comm); the row-block exchange gives the same bits.
         raise ValueError("Unknown row transport")
     with label("scaled_fp16_exchange"):
         parts, a, b = C.exchange_row_blocks(payload, comm)

@@ -1,0 +1,109 @@
+"""The peer-memory row transport kernels (h3_peer_reduce / h3_peer_gather) on one GPU.
+
+Each emulated rank gets its own workspace buffer on the same device; every flag a
+kernel waits for is set before that kernel is launched (by an earlier kernel of the
+same stream or by the test), so no kernel ever waits for another one that runs at the
+same time.  The reduced, gated residual of every rank is compared bit for bit with the
+oracle's rank-order reduction; a flag that nothing sets checks the bounded wait.
+The same kernels across real NCCL ranks are covered by tests/test_gpu_tp_nccl.py."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+FLAGS, READY, DONE = 1024, 0, 256
+
+
+def _buffers(dev, world, rows, width):
+    part = -(-rows * width * 2 // 256) * 256
+    bufs = [torch.zeros(FLAGS + 2 * part, dtype=torch.uint8, device=dev) for _ in range(world)]
+    return bufs, FLAGS, FLAGS + part
+
+
+def _set(buf, region, ranks, epoch):
+    flags = buf[:FLAGS].view(torch.int32)
+    for w in ranks:
+        flags[region // 4 + w] = epoch
+
+
+@pytest.mark.parametrize("world,rows,width", [(2, 130, 512), (4, 77, 264), (8, 99, 1024)])
+def test_peer_reduce_gather_bit_exact(cuda_device, oracle, world, rows, width):
+    from h3tp import ops, transport
+    rng = np.random.default_rng(world)
+    k_local = 1024
+    shift = transport.shift_for(k_local, world)
+    parts = [rng.integers(-2 ** 22, 2 ** 22, size=(rows, width)).astype(np.int32) for _ in range(world)]
+    enc = np.stack([oracle.fp16_encode(p, shift) for p in parts])
+    a = rng.uniform(1e-4, 1e-2, size=rows).astype(np.float32)
+    s = rng.uniform(1e-5, 1e-4, size=width).astype(np.float32)
+    X = rng.standard_normal((rows, width)).astype(np.float16)
+    G = rng.standard_normal((3, width)).astype(np.float32)
+    labels = rng.integers(0, 3, size=rows).astype(np.int32)
+    ref = X.copy()
+    oracle.row_reduce_finish(enc, shift, a, s, out="residual", residual=ref, gate=G, labels=labels)
+
+    dev = cuda_device
+    bufs, poff, boff = _buffers(dev, world, rows, width)
+    bases = [b.data_ptr() for b in bufs]
+    for w in range(world):
+        bufs[w][poff:poff + 2 * rows * width].view(torch.float16).copy_(
+            torch.from_numpy(enc[w].reshape(-1)).to(dev))
+    A, S = torch.from_numpy(a).to(dev), torch.from_numpy(s).to(dev)
+    Gd, L = torch.from_numpy(G).to(dev), torch.from_numpy(labels).to(dev)
+    res = [torch.from_numpy(X.copy()).to(dev) for _ in range(world)]
+    for epoch in (1, 2):  # the second call reuses the buffers and advances the epoch
+        if epoch == 2:
+            for r in range(world):
+                res[r].copy_(torch.from_numpy(X))
+        for b in bufs:
+            _set(b, READY, range(world), epoch)
+        for r in range(world):
+            ops.peer_reduce(bases, world, r, 0, poff, boff, rows, width, shift, A, S, res[r], Gd, L,
+                            epoch)
+        for r in range(world):
+            ops.peer_gather(bases, world, r, 0, boff, rows, width, res[r], epoch)
+        torch.cuda.synchronize()
+        for r in range(world):
+            got = res[r].cpu().numpy()
+            assert np.array_equal(got.view(np.uint16), ref.view(np.uint16)), f"rank {r} epoch {epoch}"
+            done = bufs[r][:FLAGS].view(torch.int32)[DONE // 4: DONE // 4 + world].cpu().numpy()
+            assert (done == epoch).all()
+            assert int(bufs[r][:FLAGS].view(torch.int32)[128]) == 0  # counter reset
+    from h3tp import _native
+    assert _native.device_error(dev.index or 0) == 0
+
+
+def test_peer_wait_gives_up_with_timeout_status(cuda_device):
+    """Rank 1 never signals: the reduce gives up after its bounded wait, records
+    H3_ERR_TIMEOUT, publishes no done flag, and the gather gives up too."""
+    from h3tp import _native, ops
+    dev = cuda_device
+    rows, width = 16, 256
+    bufs, poff, boff = _buffers(dev, 2, rows, width)
+    bases = [b.data_ptr() for b in bufs]
+    res = torch.zeros((rows, width), dtype=torch.float16, device=dev)
+    A = torch.ones(rows, dtype=torch.float32, device=dev)
+    S = torch.ones(width, dtype=torch.float32, device=dev)
+    assert _native.device_error(dev.index or 0) == 0
+    ops.peer_reduce(bases, 2, 0, 0, poff, boff, rows, width, 0, A, S, res, None, None, 1)
+    assert _native.device_error(dev.index or 0) == _native.H3_ERR_TIMEOUT
+    assert int(bufs[1][:FLAGS].view(torch.int32)[DONE // 4]) == 0
+    ops.peer_gather(bases, 2, 0, 0, boff, rows, width, res, 1)
+    assert _native.device_error(dev.index or 0) == _native.H3_ERR_TIMEOUT
+    assert _native.device_error(dev.index or 0) == 0  # reading clears it
+
+
+def test_peer_rejects_bad_geometry(cuda_device):
+    from h3tp import ops
+    dev = cuda_device
+    bufs, poff, boff = _buffers(dev, 2, 4, 256)
+    bases = [b.data_ptr() for b in bufs]
+    A = torch.ones(4, dtype=torch.float32, device=dev)
+    with pytest.raises(ValueError):   # world 3 is not a TP size of the path
+        ops.peer_reduce(bases + [bases[0]], 3, 0, 0, poff, boff, 4, 256, 0, A,
+                        torch.ones(256, device=dev), torch.zeros((4, 256), dtype=torch.float16,
+                                                                 device=dev))
+    with pytest.raises(ValueError):   # width not a multiple of 8
+        ops.peer_gather(bases, 2, 0, 0, boff, 4, 252, torch.zeros((4, 252), dtype=torch.float16,
+                                                                   device=dev))
