@@ -6,7 +6,7 @@
  * (H3_OK or an H3_ERR_* code).  Nothing here allocates the caller's tensors:
  * outputs are written into caller-provided device buffers, the way the reference's
  * native extension (comfy_kitchen._C.cublas_gemm_int8 / dequantize_int8_linear,
- * called from patches/optimized_tp.py:331-340 and patches/parallel_int8.py:247-259)
+ * called from patches/optimized_tp.py:34-43 and patches/parallel_int8.py:53-65)
  * receives DLPack tensors plus a raw stream.  Geometry is checked before any launch
  * and rejected with H3_ERR_INVALID, the way the reference raises ValueError before
  * either rank enters a collective (patches/tilelang_swiglu_quant.py:95-105).
@@ -43,7 +43,7 @@ enum {
   H3_IN_ACT_F16 = 2     /* fp16 [rows, width] post-SwiGLU activation                    */
 };
 
-/* Quantizer division (patches/tilelang_row_quant.py:156,169) */
+/* Quantizer division (patches/tilelang_row_quant.py:27,40) */
 enum { H3_DIV_RN = 0, H3_DIV_FAST = 1 };
 
 /* Output kinds */
@@ -76,7 +76,7 @@ int h3_column_quantize(const void* x_f16, int64_t rows, int64_t k, int convrot,
                        int8_t* q, float* scale, void* stream);
 
 /* Direct INT8 GEMM, INT32 out: out[m, n] = sum_k q[m, k] * w[n, k], exact.
- * Replaces optimized_tp.py:331-340 (native_int_mm) and parallel_int8.py:240-244. */
+ * Replaces optimized_tp.py:34-43 (native_int_mm) and parallel_int8.py:46-50. */
 int h3_int8_gemm_i32(const int8_t* q, const int8_t* w, int64_t m, int64_t n, int64_t k,
                      int32_t* out, void* stream);
 
@@ -153,7 +153,7 @@ int h3_int8_gemm_row_encode(const int8_t* q, const int8_t* w, int64_t m, int64_t
                             int64_t k, int shift, void* out_f16, void* stream);
 
 /* TP=1 row GEMM with the dequant fused (exact INT32, no transport):
- *   y = (f32(acc) *rn row_scale[m]) *rn weight_scale[n]   (parallel_int8.py:260)
+ *   y = (f32(acc) *rn row_scale[m]) *rn weight_scale[n]   (parallel_int8.py:66)
  * out_kind F32/F16 store y into out; H3_OUT_RESIDUAL updates residual_f16 in place
  * with X = f16(fma(f32(f16(y)), G[labels[m], n], f32(X))) (tilelang_dit_fusion.py:
  * 57-77); gate == NULL means G = 1.  labels may be NULL when gate_rows == 1. */
@@ -184,7 +184,7 @@ int h3_row_reduce_finish(const void* parts_f16, int world, int64_t part_stride,
                          void* residual_f16, const float* gate, int64_t gate_rows,
                          const int32_t* labels, void* stream);
 
-/* INT32 dequantisation of parallel_int8.dequantize (parallel_int8.py:247-263):
+/* INT32 dequantisation of parallel_int8.dequantize (parallel_int8.py:53-69):
  *   y = ((f32(acc) *rn row_scale[m]) *rn weight_scale[n]) [+rn bias[n]]
  * stored as out_kind F32 or F16. */
 int h3_dequantize_i32(const int32_t* acc, int64_t rows, int64_t width,
@@ -277,7 +277,7 @@ int h3_silu_compare(const float* g, int64_t n, float* fast, float* ieee, float* 
 /* INT8 codes of x[i] / scale[i] two ways: fast[i] as the kernels compute them
  * (one correctly rounded reciprocal per scale, a Markstein quotient correction and
  * magic-number rounding), ieee[i] with IEEE division, rintf and a float-to-int
- * conversion (tilelang_row_quant.py:169-173, division 'rn').  They must agree. */
+ * conversion (tilelang_row_quant.py:40-44, division 'rn').  They must agree. */
 int h3_quant_compare(const float* x, const float* scale, int64_t n, int8_t* fast,
                      int8_t* ieee, void* stream);
 

@@ -23,7 +23,7 @@ namespace h3 {
 // ---------------------------------------------------------------------------
 H3_DEV float f32_bits(uint32_t b) { return __uint_as_float(b); }
 
-// float32(1/127): tilelang_row_quant.py:167, tilelang_swiglu_quant.py:58
+// float32(1/127): tilelang_row_quant.py:38, tilelang_swiglu_quant.py:58
 #define H3_INV127_BITS 0x3c010204u
 // float32(1e-30): the scale floor of the same lines
 #define H3_SCALE_FLOOR_BITS 0x0da24260u
@@ -129,14 +129,14 @@ H3_DEV float silu_fast(float g) {
 //   a = (gate /rn (1 +rn exp(-gate))) *rn up
 H3_DEV float swiglu_f32(float gate, float up) { return __fmul_rn(silu_fast(gate), up); }
 
-// Row scale of the production row quantizer (tilelang_row_quant.py:166-167):
+// Row scale of the production row quantizer (tilelang_row_quant.py:37-38):
 //   scale = fmaxf(fminf(max, FLT_MAX) *rn float32(1/127), 1e-30)
 H3_DEV float row_scale_from_max(float m) {
   const float mm = fminf(m, 3.4028234663852886e38f);
   return fmaxf(__fmul_rn(mm, f32_bits(H3_INV127_BITS)), f32_bits(H3_SCALE_FLOOR_BITS));
 }
 
-// One INT8 code (tilelang_row_quant.py:169-173).  division: 0 = IEEE (__fdiv_rn),
+// One INT8 code (tilelang_row_quant.py:40-44).  division: 0 = IEEE (__fdiv_rn),
 // 1 = the reference's production '__fdividef' fast division.
 H3_DEV int8_t quantize_code(float x, float scale, int division) {
   const float scaled = division ? __fdividef(x, scale) : __fdiv_rn(x, scale);

@@ -4,7 +4,7 @@ patches/parallel_int8.py) on B200.
 gather / packed_rows are layout helpers; int_mm and dequantize run the sm_100a
 kernels (exact INT32 tcgen05 GEMM; ((acc * a) * w) + bias dequant).  row_linear is
 the exact full-gather route used when a rank's K-shard does not own whole 256-groups
-(parallel_int8.py:266-288): every rank gathers the complete row, quantises it with
+(parallel_int8.py:72-94): every rank gathers the complete row, quantises it with
 one global row maximum, multiplies its own K-slice and the INT32 partials are summed.
 """
 from __future__ import annotations
@@ -36,7 +36,7 @@ def int_mm(q, weight):
 
 
 def dequantize(accumulator, activation_scale, weight_scale, dtype, bias=None):
-    """y = ((f32(acc) * a) * w) [+ bias], then cast (parallel_int8.py:247-263)."""
+    """y = ((f32(acc) * a) * w) [+ bias], then cast (parallel_int8.py:53-69)."""
     out_dtype = torch.float16 if dtype == torch.float16 else torch.float32
     y = ops.dequantize_i32(accumulator, activation_scale, weight_scale, out_dtype, bias)
     return y if y.dtype == dtype else y.to(dtype)
@@ -55,7 +55,7 @@ def packed_rows(weight, scale, rank, world_size, components):
 
 def row_linear(x, weight, weight_scale, comm, world_size, groupsize=256, input_act=None,
                bias=None, residual=None, residual_scale=None, *, division="rn"):
-    """Exact full-gather route (parallel_int8.py:266-288) with the B200 quantiser."""
+    """Exact full-gather route (parallel_int8.py:72-94) with the B200 quantiser."""
     if groupsize != 256:
         raise ValueError("Only regular ConvRot256 groups are supported")
     full, start, length = gather(x, comm, -1)

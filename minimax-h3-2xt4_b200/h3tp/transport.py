@@ -35,14 +35,14 @@ def shift_for(local_k: int, world_size: int = 2) -> int:
 
 
 def encode(partial: torch.Tensor, scheme: str, local_k: int, world_size: int = 2) -> torch.Tensor:
-    """Standalone encode of an INT32 partial (tilelang_transport_p2.py:156-160)."""
+    """Standalone encode of an INT32 partial (tilelang_transport_p2.py:50-54)."""
     if scheme != "fp16":
         raise ValueError(scheme)
     return ops.fp16_encode(partial, shift_for(local_k, world_size))
 
 
 def collect(payload: torch.Tensor, scheme: str, comm) -> torch.Tensor:
-    """NCCL fp16 SUM (tilelang_transport_p2.py:163-168)."""
+    """NCCL fp16 SUM (tilelang_transport_p2.py:57-58)."""
     if scheme != "fp16":
         raise ValueError(scheme)
     if C.world_of(comm) > 1:
@@ -52,7 +52,7 @@ def collect(payload: torch.Tensor, scheme: str, comm) -> torch.Tensor:
 
 def finish(payload, activation_scale, weight_scale, scheme, local_k, world_size: int = 2,
            out_dtype=torch.float32):
-    """Decode + FP32 dequant of a reduced payload (tilelang_transport_p2.py:171-174)."""
+    """Decode + FP32 dequant of a reduced payload (tilelang_transport_p2.py:65-69)."""
     if scheme != "fp16":
         raise ValueError(scheme)
     return ops.row_reduce_finish(payload, shift_for(local_k, world_size), activation_scale,

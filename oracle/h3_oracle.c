@@ -135,7 +135,7 @@ EXPORT void h3o_convrot256(float* A) {
   for (int i = 0; i < 256; ++i) A[i] = A[i] * (1.0f / 16.0f);
 }
 
-/* Row scale and one code of the row quantizer (tilelang_row_quant.py:166-173),
+/* Row scale and one code of the row quantizer (tilelang_row_quant.py:37-44),
  * division 'rn' (IEEE). */
 static inline float row_scale(float m) {
   const float mm = fminf(m, FLT_MAX);
@@ -331,7 +331,7 @@ EXPORT void h3o_row_reduce_finish(const uint16_t* parts, int world, int64_t part
     }
 }
 
-/* parallel_int8.dequantize CPU branch (parallel_int8.py:260-263):
+/* parallel_int8.dequantize CPU branch (parallel_int8.py:66-69):
  * y = ((f32(acc) * a) * w) [+ bias], then cast. out_kind 0 fp32, 1 fp16,
  * 2 gated residual update (tilelang_dit_fusion.py gate order). */
 EXPORT void h3o_dequantize_i32(const int32_t* acc, int64_t rows, int64_t width, const float* A,

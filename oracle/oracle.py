@@ -211,7 +211,7 @@ def row_reduce_finish(parts, shift, row_scale, weight_scale, out="f32", residual
 
 def dequantize_i32(acc, row_scale, weight_scale, bias=None, out="f32", residual=None,
                    gate=None, labels=None):
-    """parallel_int8.dequantize CPU branch (parallel_int8.py:260-263)."""
+    """parallel_int8.dequantize CPU branch (parallel_int8.py:66-69)."""
     acc = _c(acc, np.int32)
     rows, width = acc.shape
     o = OUT[out]
@@ -245,7 +245,7 @@ def gated_add(y, residual, gate=None, labels=None):
 # composite chains (the whole operator, as the reference runs it)
 # ----------------------------------------------------------------------------
 def packed_rows(weight, scale, rank, world_size, components):
-    """parallel_int8.packed_rows (parallel_int8.py:291-297)."""
+    """parallel_int8.packed_rows (parallel_int8.py:97-103)."""
     if weight.shape[0] % (components * world_size):
         raise ValueError("Packed components must divide evenly across ranks")
     wc = np.split(weight, components, axis=0)

@@ -8,7 +8,7 @@ sm_75/sm_120 GPU and its comfy_kitchen dependency is not installed): a stub
 functions whose CPU path never touches it are called:
 
   patches/parallel_int8.py         int_mm (torch._int_mm, CPU), dequantize (CPU
-                                   branch, :260-263), packed_rows (:97-103)
+                                   branch, :66-69), packed_rows (:97-103)
   patches/tilelang_transport_tradeoffs.py  shift_for (:20-22)
   benchmarks/tp2_tradeoffs.py      transport_reference (:66-78), extracted from the
                                    module source because the module's own imports
