@@ -106,28 +106,81 @@ H3_DEV float silu_ieee(float g) {
   return __fdiv_rn(g, __fadd_rn(1.0f, h3_expf(-g)));
 }
 
-// The same value for every float g, without operands that make the IEEE division
-// leave its common path.  A denominator above 2^64 only occurs for g < -44; there
-// both operands are multiplied by 2^-32, which is exact (|g| * 2^-32 >= 2^-27 and
-// den * 2^-32 < 2^96 stay normal), so the quotient - itself >= 44 / FLT_MAX, a normal
-// float - and its rounding are unchanged.  An infinite denominator with a finite g
-// (g < -88.7) gives g / inf = -0, produced as -0 / 1.  Verified bit-identical to
-// silu_ieee on all 65536 fp16 gate values (tests/test_gpu_kernels.py).
+// The same value as silu_ieee for every gate that is an fp16 value (the only gates the
+// path has: the reference rounds them to fp16 first, tilelang_swiglu_quant.py:21),
+// branch-free and without the IEEE division's slow path.  Both operands are scaled,
+// exactly, by 2^-64 (|g| >= 2^-24 or g = 0, den in [1, FLT_MAX]), so the reciprocal
+// and every intermediate below stay normal.  The quotient is computed by division of
+// our own: y0 = rcp.approx(den'), one Newton step y1 = y0 + y0 (1 - den' y0), then the
+// quotient correction of P. Markstein (IBM J. Res. Dev. 34(1), 1990): q0 = g' y1,
+// r = g' - q0 den' (exact), q = q0 + r y1.  Infinite and NaN quotients keep q0 (the
+// IEEE result for g = +-inf or NaN), an infinite denominator (g < -88.7) gives g * 0
+// (-0 for a finite g, NaN for -inf, as g / inf does), and a zero quotient takes the
+// sign of g.  Verified bit-identical to silu_ieee on all 65536 fp16 gate values
+// (tests/test_gpu_kernels.py).
 H3_DEV float silu_fast(float g) {
-  float den = silu_den(g);
-  float num = g;
-  const bool big = den > 18446744073709551616.0f;  // 2^64
-  const bool inf_den = (den == __uint_as_float(0x7f800000u)) && (fabsf(g) < __uint_as_float(0x7f800000u));
-  num = big ? __fmul_rn(num, 2.3283064365386963e-10f) : num;  // 2^-32
-  den = big ? __fmul_rn(den, 2.3283064365386963e-10f) : den;
-  num = inf_den ? -0.0f : num;
-  den = inf_den ? 1.0f : den;
-  return __fdiv_rn(num, den);
+  const float den = silu_den(g);
+  const float a = __fmul_rn(g, 5.421010862427522e-20f);      // 2^-64
+  const float nb = __fmul_rn(den, -5.421010862427522e-20f);  // -den * 2^-64
+  float y0;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y0) : "f"(-nb));
+  const float y1 = __fmaf_rn(__fmaf_rn(nb, y0, 1.0f), y0, y0);
+  const float q0 = __fmul_rn(a, y1);
+  float q = __fmaf_rn(__fmaf_rn(q0, nb, a), y1, q0);
+  const float inf = __uint_as_float(0x7f800000u);
+  q = fabsf(q0) < inf ? q : q0;
+  q = den == inf ? __fmul_rn(g, 0.0f) : q;
+  return __uint_as_float((__float_as_uint(q) & 0x7fffffffu) | (__float_as_uint(g) & 0x80000000u));
 }
 
 // FP32 SwiGLU of one (gate, up) pair, in the order of tilelang_swiglu_quant.py:21-24:
 //   a = (gate /rn (1 +rn exp(-gate))) *rn up
 H3_DEV float swiglu_f32(float gate, float up) { return __fmul_rn(silu_fast(gate), up); }
+
+// ---------------------------------------------------------------------------
+// Packed FP32 pairs.  sm_100's add / sub / mul / fma .rn.f32x2 instructions work on two
+// floats held in one 64-bit register pair and round each lane exactly as the scalar
+// .rn instruction does, so two independent computations written with them give the
+// same bits as the scalar form at half the instruction issue.
+// ---------------------------------------------------------------------------
+typedef uint64_t f32x2;
+
+H3_DEV f32x2 pk2(float lo, float hi) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+H3_DEV f32x2 dup2(float v) { return pk2(v, v); }
+H3_DEV float lo2(f32x2 v) {
+  float a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+  return a;
+}
+H3_DEV float hi2(f32x2 v) {
+  float a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+  return b;
+}
+H3_DEV f32x2 add2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+H3_DEV f32x2 sub2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+H3_DEV f32x2 mul2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+H3_DEV f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
+  f32x2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
 
 // Row scale of the production row quantizer (tilelang_row_quant.py:37-38):
 //   scale = fmaxf(fminf(max, FLT_MAX) *rn float32(1/127), 1e-30)
@@ -214,6 +267,77 @@ H3_DEV void convrot256_halfwarp(float (&v)[16], float* tile, int b) {
 #pragma unroll
   for (int j = 0; j < 16; ++j) v[j] = tile[b * 17 + j];
   __syncwarp();
+}
+
+// The same rotation on two groups at once: lane 0 of every pair holds one group's
+// value, lane 1 the other's, and every addition is the f32x2 form of the scalar one
+// above ((a+b)+c)+(-d) = ((a+b)+c)-d, and -a+b = b-a, are the same IEEE operations).
+template <int S>
+H3_DEV void radix4_stage2(f32x2 (&v)[16]) {
+#pragma unroll
+  for (int base = 0; base < 16; ++base) {
+    if ((base / S) % 4 != 0) continue;
+    const f32x2 a = v[base], b = v[base + S], c = v[base + 2 * S], d = v[base + 3 * S];
+    const f32x2 ab = add2(a, b);
+    v[base]         = sub2(add2(ab, c), d);
+    v[base + S]     = add2(sub2(ab, c), d);
+    v[base + 2 * S] = add2(add2(sub2(a, b), c), d);
+    v[base + 3 * S] = add2(add2(sub2(b, a), c), d);
+  }
+}
+
+// convrot256_halfwarp on two groups; tile: 16 x 17 pairs private to this half warp.
+H3_DEV void convrot256_halfwarp2(f32x2 (&v)[16], f32x2* tile, int b) {
+  radix4_stage2<1>(v);
+  radix4_stage2<4>(v);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) tile[b * 17 + j] = v[j];
+  __syncwarp();
+#pragma unroll
+  for (int t = 0; t < 16; ++t) v[t] = tile[t * 17 + b];
+  __syncwarp();
+  radix4_stage2<1>(v);
+  radix4_stage2<4>(v);
+  const f32x2 sixteenth = dup2(0.0625f);
+#pragma unroll
+  for (int t = 0; t < 16; ++t) tile[t * 17 + b] = mul2(v[t], sixteenth);
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = tile[b * 17 + j];
+  __syncwarp();
+}
+
+// max(m, |a|, |b|), NaN if any operand is NaN (three-input max of sm_100).
+H3_DEV float max_abs2_nan(float m, float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(m), "f"(fabsf(a)), "f"(fabsf(b)));
+  return r;
+}
+
+// Codes of 16 pairs for a row whose maximum m (over the very values quantised) is
+// finite: then |x / scale| <= 127 * (1 + 2^-23), so the clamp of quantize_code_rn never
+// changes its input and the quotient is never infinite, and the code is the low byte
+// of RN(div_by_scale(x) + 1.5 * 2^23).  c0 receives lane 0's codes, c1 lane 1's.
+H3_DEV void quantize_pairs_finite(const f32x2 (&v)[16], float scale, float inv, uint4& c0,
+                                  uint4& c1) {
+  const f32x2 i2 = dup2(inv), ns = dup2(-scale), magic = dup2(12582912.0f);
+  uint32_t w0[4], w1[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    uint32_t lo[4], hi[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const f32x2 x = v[4 * k + e];
+      const f32x2 q0 = mul2(x, i2);
+      const f32x2 t = add2(fma2(fma2(q0, ns, x), i2, q0), magic);
+      lo[e] = __float_as_uint(lo2(t));
+      hi[e] = __float_as_uint(hi2(t));
+    }
+    w0[k] = __byte_perm(__byte_perm(lo[0], lo[1], 0x0040), __byte_perm(lo[2], lo[3], 0x0040), 0x5410);
+    w1[k] = __byte_perm(__byte_perm(hi[0], hi[1], 0x0040), __byte_perm(hi[2], hi[3], 0x0040), 0x5410);
+  }
+  c0 = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+  c1 = make_uint4(w1[0], w1[1], w1[2], w1[3]);
 }
 
 // ---------------------------------------------------------------------------

@@ -19,34 +19,58 @@ enum ProducerMode { MODE_MAX = 0, MODE_QUANT = 1, MODE_LOCAL = 2 };
 
 struct RowTeam {
   int threads;  // CTA size, multiple of 32
-  int nb;       // 16-value blocks per thread
+  int nb;       // packed pairs of 16-value blocks per thread
 };
 
+// Pairs of 16-value blocks per thread (nb = pairs) and CTA size for a row of `width`.
 static RowTeam row_team(int64_t width) {
   const int64_t blocks = width / 16;
-  int threads = (int)std::min<int64_t>(blocks, 512);
+  int threads = (int)std::min<int64_t>((blocks + 1) / 2, 512);
   threads = std::max(32, (threads + 31) / 32 * 32);
-  int nb = (int)((blocks + threads - 1) / threads);
-  return {threads, nb};
+  int pairs = (int)((blocks + 2 * threads - 1) / (2 * threads));
+  return {threads, pairs};
 }
 
-// Load the 16 activation values of block `blk` in row `row` (before rotation).
+// Dynamic shared memory of a producer CTA: one 16 x 17 tile of pairs per half warp and
+// the 32-float reduction buffer.
+static size_t producer_smem(int threads) {
+  return (size_t)(threads / 16) * 16 * 17 * sizeof(unsigned long long) + 32 * sizeof(float);
+}
+
+// Activation values of blocks blk0 (lane 0) and blk1 (lane 1) of row `row`, before
+// rotation; a block that is not valid reads as zeros.
 template <int KIND>
-H3_DEV void load_activation(const void* x, int64_t row, int64_t width, int64_t blk,
-                            float (&v)[16]) {
-  const int64_t e = blk * 16;
+H3_DEV void load_activation2(const void* x, int64_t row, int64_t width, int64_t blk0,
+                             int64_t blk1, bool ok0, bool ok1, f32x2 (&p)[16]) {
+  float a[16], b[16];
   if (KIND == H3_IN_GATEUP_F16) {
     const __half* xr = reinterpret_cast<const __half*>(x) + row * 2 * width;
-    float g[16], u[16];
-    load_half16_as_float(xr + e, g);
-    load_half16_as_float(xr + width + e, u);
+    float g0[16], g1[16];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = swiglu_f32(g[j], u[j]);
-  } else if (KIND == H3_IN_ACT_F32) {
-    load_float16(reinterpret_cast<const float*>(x) + row * width + e, v);
-  } else {
-    load_half16_as_float(reinterpret_cast<const __half*>(x) + row * width + e, v);
+    for (int j = 0; j < 16; ++j) g0[j] = g1[j] = a[j] = b[j] = 0.0f;
+    if (ok0) {
+      load_half16_as_float(xr + blk0 * 16, g0);
+      load_half16_as_float(xr + width + blk0 * 16, a);
+    }
+    if (ok1) {
+      load_half16_as_float(xr + blk1 * 16, g1);
+      load_half16_as_float(xr + width + blk1 * 16, b);
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) p[j] = pk2(swiglu_f32(g0[j], a[j]), swiglu_f32(g1[j], b[j]));
+    return;
   }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) a[j] = b[j] = 0.0f;
+  if (KIND == H3_IN_ACT_F32) {
+    if (ok0) load_float16(reinterpret_cast<const float*>(x) + row * width + blk0 * 16, a);
+    if (ok1) load_float16(reinterpret_cast<const float*>(x) + row * width + blk1 * 16, b);
+  } else {
+    if (ok0) load_half16_as_float(reinterpret_cast<const __half*>(x) + row * width + blk0 * 16, a);
+    if (ok1) load_half16_as_float(reinterpret_cast<const __half*>(x) + row * width + blk1 * 16, b);
+  }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) p[j] = pk2(a[j], b[j]);
 }
 
 H3_DEV float block_reduce_max(float v, float* red) {
@@ -61,43 +85,116 @@ H3_DEV float block_reduce_max(float v, float* red) {
   return m;
 }
 
-// FC2 producer.  One CTA per row (grid-stride over rows).
-template <int KIND, int MODE, int NB>
+// CTA maximum with NaN propagation (a NaN anywhere gives NaN).
+H3_DEV float block_reduce_max_nan(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, v, o);
+    asm("max.NaN.f32 %0, %0, %1;" : "+f"(v) : "f"(w));
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float m = 0.0f;
+  const int nw = blockDim.x >> 5;
+  for (int w = 0; w < nw; ++w) asm("max.NaN.f32 %0, %0, %1;" : "+f"(m) : "f"(red[w]));
+  __syncthreads();
+  return m;
+}
+
+// Maximum of |v| over the valid values of this thread, ignoring NaN (fmaxf), as the
+// reference's row maximum does; only rows that hold a NaN or an infinity need it.
+template <int NP>
+H3_DEV float local_max_ignoring_nan(const f32x2 (&v)[NP][16], const bool (&ok)[NP][2]) {
+  float m = 0.0f;
+#pragma unroll
+  for (int p = 0; p < NP; ++p)
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (ok[p][0]) m = fmaxf(m, fabsf(lo2(v[p][i])));
+      if (ok[p][1]) m = fmaxf(m, fabsf(hi2(v[p][i])));
+    }
+  return m;
+}
+
+// Codes of the valid blocks of this thread.  finite: the row maximum (over exactly
+// these values) is finite, so the packed form applies; otherwise each code goes
+// through the clamped scalar quantiser.
+template <int NP>
+H3_DEV void quantize_store(const f32x2 (&v)[NP][16], const bool (&ok)[NP][2],
+                           const int64_t (&blk)[NP][2], bool finite, float scale, float inv,
+                           int division, int8_t* qrow) {
+#pragma unroll
+  for (int p = 0; p < NP; ++p) {
+    if (finite && division == H3_DIV_RN) {
+      uint4 c0, c1;
+      quantize_pairs_finite(v[p], scale, inv, c0, c1);
+      if (ok[p][0]) *reinterpret_cast<uint4*>(qrow + blk[p][0] * 16) = c0;
+      if (ok[p][1]) *reinterpret_cast<uint4*>(qrow + blk[p][1] * 16) = c1;
+    } else {
+      int8_t c0[16], c1[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        c0[i] = quantize_code_mode(lo2(v[p][i]), scale, inv, division);
+        c1[i] = quantize_code_mode(hi2(v[p][i]), scale, inv, division);
+      }
+      if (ok[p][0]) store_int8x16(qrow + blk[p][0] * 16, c0);
+      if (ok[p][1]) store_int8x16(qrow + blk[p][1] * 16, c1);
+    }
+  }
+}
+
+// FC2 producer.  One CTA per row (grid-stride over rows); each thread owns NB = 2 * NP
+// 16-value blocks, processed as NP packed pairs of blocks that lie in different
+// ConvRot groups (blocks tid + (2p) * T and tid + (2p + 1) * T for T threads).
+template <int KIND, int MODE, int NP>
 __global__ void __launch_bounds__(512) swiglu_rotate_kernel(
     const void* __restrict__ x, int64_t rows, int64_t width, float* __restrict__ rotated,
     float* __restrict__ row_max, const float* __restrict__ row_max_in, int division,
     int8_t* __restrict__ q, float* __restrict__ scale_out) {
-  extern __shared__ float smem[];
+  extern __shared__ f32x2 smem2[];
   const int tid = threadIdx.x;
   const int half = tid >> 4, b = tid & 15;
-  float* tile = smem + half * (16 * 17);
-  float* red = smem + (blockDim.x / 16) * (16 * 17);
+  f32x2* tile = smem2 + half * (16 * 17);
+  float* red = reinterpret_cast<float*>(smem2 + (blockDim.x / 16) * (16 * 17));
   const int64_t blocks = width / 16;
+  int64_t blk[NP][2];
+  bool ok[NP][2];
+#pragma unroll
+  for (int p = 0; p < NP; ++p)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      blk[p][e] = tid + (int64_t)(2 * p + e) * blockDim.x;
+      ok[p][e] = blk[p][e] < blocks;  // uniform across each half warp
+    }
 
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
-    float v[NB][16];
-    float local_max = 0.0f;
+    f32x2 v[NP][16];
+    float m_nan = 0.0f;
 #pragma unroll
-    for (int j = 0; j < NB; ++j) {
-      const int64_t blk = tid + (int64_t)j * blockDim.x;
-      const bool valid = blk < blocks;  // uniform across each half warp
-      if (valid) {
-        load_activation<KIND>(x, row, width, blk, v[j]);
-      } else {
+    for (int p = 0; p < NP; ++p) {
+      load_activation2<KIND>(x, row, width, blk[p][0], blk[p][1], ok[p][0], ok[p][1], v[p]);
+      convrot256_halfwarp2(v[p], tile, b);
+      // invalid blocks rotate zeros, which leave the maximum unchanged
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[j][i] = 0.0f;
-      }
-      convrot256_halfwarp(v[j], tile, b);
-      if (valid) {
+      for (int i = 0; i < 16; ++i) m_nan = max_abs2_nan(m_nan, lo2(v[p][i]), hi2(v[p][i]));
+      if (MODE == MODE_MAX && rotated != nullptr) {
+        float r0[16], r1[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) local_max = fmaxf(local_max, fabsf(v[j][i]));
-        if (MODE == MODE_MAX && rotated != nullptr)
-          store_float16(rotated + row * width + blk * 16, v[j]);
+        for (int i = 0; i < 16; ++i) {
+          r0[i] = lo2(v[p][i]);
+          r1[i] = hi2(v[p][i]);
+        }
+        if (ok[p][0]) store_float16(rotated + row * width + blk[p][0] * 16, r0);
+        if (ok[p][1]) store_float16(rotated + row * width + blk[p][1] * 16, r1);
       }
     }
     float scale = 0.0f;
+    bool finite = false;
     if (MODE == MODE_MAX || MODE == MODE_LOCAL) {
-      const float m = block_reduce_max(local_max, red);
+      float m = block_reduce_max_nan(m_nan, red);
+      finite = m < __uint_as_float(0x7f800000u);  // false for +inf and NaN
+      if (!finite) m = block_reduce_max(local_max_ignoring_nan<NP>(v, ok), red);
       if (tid == 0) row_max[row] = m;
       scale = row_scale_from_max(m);
     } else {
@@ -105,69 +202,59 @@ __global__ void __launch_bounds__(512) swiglu_rotate_kernel(
     }
     if (MODE == MODE_QUANT || MODE == MODE_LOCAL) {
       const float inv = __fdiv_rn(1.0f, scale);
-#pragma unroll
-      for (int j = 0; j < NB; ++j) {
-        const int64_t blk = tid + (int64_t)j * blockDim.x;
-        if (blk < blocks) {
-          int8_t c[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) c[i] = quantize_code_mode(v[j][i], scale, inv, division);
-          store_int8x16(q + row * width + blk * 16, c);
-        }
-      }
+      // MODE_QUANT's maximum comes from outside and may be below |x|: scalar path
+      quantize_store<NP>(v, ok, blk, MODE == MODE_LOCAL && finite, scale, inv, division,
+                         q + row * width);
       if (tid == 0) scale_out[row] = scale;
     }
   }
 }
 
 // Column activation preparation (QKV / FC1 input): optional ConvRot256 with an fp16
-// rounding of the rotated value, then the row quantiser.  One CTA per row.
-template <int NB, bool ROTATE>
+// rounding of the rotated value, then the row quantiser.  One CTA per row, packed
+// pairs of blocks as in swiglu_rotate_kernel.
+template <int NP, bool ROTATE>
 __global__ void __launch_bounds__(512) column_quantize_kernel(
     const __half* __restrict__ x, int64_t rows, int64_t k, int8_t* __restrict__ q,
     float* __restrict__ scale_out) {
-  extern __shared__ float smem[];
+  extern __shared__ f32x2 smem2[];
   const int tid = threadIdx.x;
   const int half = tid >> 4, b = tid & 15;
-  float* tile = smem + half * (16 * 17);
-  float* red = smem + (blockDim.x / 16) * (16 * 17);
+  f32x2* tile = smem2 + half * (16 * 17);
+  float* red = reinterpret_cast<float*>(smem2 + (blockDim.x / 16) * (16 * 17));
   const int64_t blocks = k / 16;
-  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
-    float v[NB][16];
-    float local_max = 0.0f;
+  int64_t blk[NP][2];
+  bool ok[NP][2];
 #pragma unroll
-    for (int j = 0; j < NB; ++j) {
-      const int64_t blk = tid + (int64_t)j * blockDim.x;
-      const bool valid = blk < blocks;
-      if (valid) {
-        load_half16_as_float(x + row * k + blk * 16, v[j]);
-      } else {
+  for (int p = 0; p < NP; ++p)
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[j][i] = 0.0f;
-      }
-      if (ROTATE) {
-        convrot256_halfwarp(v[j], tile, b);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[j][i] = __half2float(__float2half_rn(v[j][i]));
-      }
-      if (valid) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) local_max = fmaxf(local_max, fabsf(v[j][i]));
-      }
+    for (int e = 0; e < 2; ++e) {
+      blk[p][e] = tid + (int64_t)(2 * p + e) * blockDim.x;
+      ok[p][e] = blk[p][e] < blocks;
     }
-    const float m = block_reduce_max(local_max, red);
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    f32x2 v[NP][16];
+    float m_nan = 0.0f;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+      load_activation2<H3_IN_ACT_F16>(x, row, k, blk[p][0], blk[p][1], ok[p][0], ok[p][1], v[p]);
+      if (ROTATE) {
+        convrot256_halfwarp2(v[p], tile, b);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 f = __half22float2(__floats2half2_rn(lo2(v[p][i]), hi2(v[p][i])));
+          v[p][i] = pk2(f.x, f.y);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) m_nan = max_abs2_nan(m_nan, lo2(v[p][i]), hi2(v[p][i]));
+    }
+    float m = block_reduce_max_nan(m_nan, red);
+    const bool finite = m < __uint_as_float(0x7f800000u);
+    if (!finite) m = block_reduce_max(local_max_ignoring_nan<NP>(v, ok), red);
     const float scale = row_scale_from_max(m);
     const float inv = __fdiv_rn(1.0f, scale);
-#pragma unroll
-    for (int j = 0; j < NB; ++j) {
-      const int64_t blk = tid + (int64_t)j * blockDim.x;
-      if (blk < blocks) {
-        int8_t c[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) c[i] = quantize_code_rn(v[j][i], scale, inv);
-        store_int8x16(q + row * k + blk * 16, c);
-      }
-    }
+    quantize_store<NP>(v, ok, blk, finite, scale, inv, H3_DIV_RN, q + row * k);
     if (tid == 0) scale_out[row] = scale;
   }
 }
@@ -221,25 +308,42 @@ __global__ void quant_compare_kernel(const float* __restrict__ x, const float* _
 // ---------------------------------------------------------------------------
 // Launch helpers
 // ---------------------------------------------------------------------------
+// Opts a kernel into more than 48 KB of dynamic shared memory (once per kernel).
+template <typename K>
+static bool allow_smem(K kernel, size_t smem, bool& done) {
+  if (smem <= 48 * 1024 || done) return true;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return false;
+  done = true;
+  return true;
+}
+
+template <int KIND, int MODE, int NP>
+static int launch_producer_np(const void* x, int64_t rows, int64_t width, float* rotated,
+                              float* row_max, const float* row_max_in, int division, int8_t* q,
+                              float* scale, int threads, cudaStream_t stream) {
+  static bool smem_set = false;
+  const size_t smem = producer_smem(threads);
+  if (!allow_smem(swiglu_rotate_kernel<KIND, MODE, NP>, smem, smem_set)) return H3_ERR_CUDA;
+  const int grid = (int)std::min<int64_t>(rows, 1 << 20);
+  swiglu_rotate_kernel<KIND, MODE, NP><<<grid, threads, smem, stream>>>(
+      x, rows, width, rotated, row_max, row_max_in, division, q, scale);
+  return h3host::check_launch();
+}
+
 template <int KIND, int MODE>
 static int launch_producer(const void* x, int64_t rows, int64_t width, float* rotated,
                            float* row_max, const float* row_max_in, int division, int8_t* q,
                            float* scale, cudaStream_t stream) {
   const RowTeam t = row_team(width);
-  const size_t smem = (size_t)(t.threads / 16) * 16 * 17 * 4 + 32 * 4;
-  const int64_t grid64 = std::min<int64_t>(rows, 1 << 20);
-  const int grid = (int)grid64;
-#define H3_LAUNCH_NB(NBV)                                                                  \
-  swiglu_rotate_kernel<KIND, MODE, NBV><<<grid, t.threads, smem, stream>>>(               \
-      x, rows, width, rotated, row_max, row_max_in, division, q, scale)
-  switch (t.nb) {
-    case 1: H3_LAUNCH_NB(1); break;
-    case 2: H3_LAUNCH_NB(2); break;
-    case 3: case 4: H3_LAUNCH_NB(4); break;
-    default: return H3_ERR_INVALID;
-  }
-#undef H3_LAUNCH_NB
-  return h3host::check_launch();
+  if (t.nb == 1)
+    return launch_producer_np<KIND, MODE, 1>(x, rows, width, rotated, row_max, row_max_in,
+                                             division, q, scale, t.threads, stream);
+  if (t.nb == 2)
+    return launch_producer_np<KIND, MODE, 2>(x, rows, width, rotated, row_max, row_max_in,
+                                             division, q, scale, t.threads, stream);
+  return H3_ERR_INVALID;
 }
 
 template <int MODE>
@@ -324,26 +428,23 @@ extern "C" int h3_column_quantize(const void* x_f16, int64_t rows, int64_t k, in
   int dev;
   if (int s = h3host::bind_device_of(x_f16, &dev)) return s;
   const RowTeam t = row_team(k);
-  const size_t smem = (size_t)(t.threads / 16) * 16 * 17 * 4 + 32 * 4;
+  const size_t smem = producer_smem(t.threads);
   const int grid = (int)std::min<int64_t>(rows, 1 << 20);
   cudaStream_t st = (cudaStream_t)stream;
   const __half* xh = reinterpret_cast<const __half*>(x_f16);
-#define H3_COLQ(NBV, ROT) \
-  column_quantize_kernel<NBV, ROT><<<grid, t.threads, smem, st>>>(xh, rows, k, q, scale)
-  if (convrot) {
-    switch (t.nb) {
-      case 1: H3_COLQ(1, true); break;
-      case 2: H3_COLQ(2, true); break;
-      case 3: case 4: H3_COLQ(4, true); break;
-      default: return H3_ERR_INVALID;
-    }
+  static bool smem_set[2][2] = {{false, false}, {false, false}};
+#define H3_COLQ(NPV, ROT)                                                                   \
+  do {                                                                                      \
+    if (!allow_smem(column_quantize_kernel<NPV, ROT>, smem, smem_set[NPV - 1][ROT]))        \
+      return H3_ERR_CUDA;                                                                   \
+    column_quantize_kernel<NPV, ROT><<<grid, t.threads, smem, st>>>(xh, rows, k, q, scale); \
+  } while (0)
+  if (t.nb == 1) {
+    if (convrot) H3_COLQ(1, true); else H3_COLQ(1, false);
+  } else if (t.nb == 2) {
+    if (convrot) H3_COLQ(2, true); else H3_COLQ(2, false);
   } else {
-    switch (t.nb) {
-      case 1: H3_COLQ(1, false); break;
-      case 2: H3_COLQ(2, false); break;
-      case 3: case 4: H3_COLQ(4, false); break;
-      default: return H3_ERR_INVALID;
-    }
+    return H3_ERR_INVALID;
   }
 #undef H3_COLQ
   return h3host::check_launch();
