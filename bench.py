@@ -12,9 +12,10 @@ that shape (no checkpoint or dataset is involved).
 value: whole-job INT8 TOPS = 2*M*(2*ffn*hidden + hidden*ffn) / device time per block
        (max over ranks, CUDA events, inputs resident in HBM; h alone is 201 MB, larger
        than the 126 MB L2, so no flush is needed between steps).
-e2e:   the same through the public module API with the step's inputs (h, residual)
+e2e:   the same through the public module API with every step's inputs (h, residual)
        copied host->device from pinned memory and the updated residual copied back,
-       inside the timed region.
+       inside the timed region (copies on two streams, overlapped with compute; at
+       TP > 1 each rank uploads 1/t of the rows and NCCL all-gathers them).
 roofline: the dominant kernel (the FC1 tcgen05 GEMM with the SwiGLU epilogue) timed
        with CUDA events inside the timed steps, against the INT8 tensor peak.
 cpu_baseline / --impl reference: the reference's CPU path (torch._int_mm, the CPU
@@ -43,7 +44,7 @@ METRIC = "INT8 TOPS/GPU and µs per DiT MLP block at M=32k, TP 1/2/4/8; % of INT
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--tokens", type=int, default=32768)
@@ -94,35 +95,58 @@ def make_inputs(M, hidden, seed=1):
 # clocks
 # ----------------------------------------------------------------------------
 class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples taken while the timed region runs.
+
+    The sampler is started, and its first sample awaited, before the region begins;
+    on exit it waits for one sample taken after the region ended, so even a short
+    region is covered.  Only samples taken inside the region are summarised."""
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_MS = 20
 
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.samples = []  # (monotonic time, line)
+        self.t0 = self.t1 = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            if line.strip():
+                self.samples.append((time.monotonic(), line))
+
+    def _wait_for(self, pred, timeout):
+        end = time.monotonic() + timeout
+        while time.monotonic() < end and not pred():
+            time.sleep(0.005)
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.QUERY,
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", str(self.PERIOD_MS)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+            self._wait_for(lambda: len(self.samples) > 0, 15.0)
         except OSError:
             self.proc = None
-        time.sleep(0.3)
+        self.t0 = time.monotonic()
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
+        self.t1 = time.monotonic()
         if self.proc is not None:
+            self._wait_for(lambda: self.samples and self.samples[-1][0] > self.t1, 2.0)
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+        inside = [l for t, l in self.samples if self.t0 <= t <= self.t1 + 0.001 * self.PERIOD_MS]
+        if not inside and self.samples:  # region shorter than one period: nearest sample
+            inside = [min(self.samples, key=lambda s: abs(s[0] - self.t1))[1]]
+        self.lines = inside
 
     def summary(self):
         sm, mx, reasons = [], None, set()
@@ -301,31 +325,69 @@ def run_ours(args):
         elapsed_ms, fc1_ms = float(t[0]), float(t[1])
         ms_per_step = elapsed_ms / args.steps
 
-        # e2e through the public module API with host buffers
+        # e2e through the public module API with host buffers: every step uploads its
+        # inputs from pinned host memory and reads the updated residual back.  Copies
+        # run on two copy streams (host->device, device->host) with double buffers, so
+        # they overlap each other and the previous / next step's compute.  At TP > 1
+        # each rank uploads only its 1/t row block and the blocks are all-gathered
+        # over NVLink (NCCL); rank 0 reads the (replicated) result back.
         e2e = None
         if not args.no_e2e:
             h_pin = h_cpu.pin_memory()
             x_pin = x_cpu.pin_memory()
-            out_pin = torch.empty_like(x_cpu).pin_memory()
-            hd = torch.empty_like(h)
-            xd = torch.empty_like(x)
+            out_pin = [torch.empty_like(x_cpu).pin_memory() for _ in range(2)]
+            hd = [torch.empty_like(h) for _ in range(2)]
+            xd = [torch.empty_like(x) for _ in range(2)]
+            per = M // world if M % world == 0 else M
+            a0, a1 = (rank * per, (rank + 1) * per) if per != M else (0, M)
+            up_s, down_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+            ev = lambda: torch.cuda.Event()  # noqa: E731
+            ev_up = [ev(), ev()]
+            ev_comp = [ev(), ev()]
+            ev_down = [ev(), ev()]
+            for e in ev_down:
+                e.record(down_s)
 
-            def e2e_step():
-                hd.copy_(h_pin, non_blocking=True)
-                xd.copy_(x_pin, non_blocking=True)
-                y = mlp(xd, hd)
-                out_pin.copy_(y, non_blocking=True)
+            def upload(j):
+                with torch.cuda.stream(up_s):
+                    up_s.wait_event(ev_down[j])  # the buffer's previous result was read
+                    hd[j][a0:a1].copy_(h_pin[a0:a1], non_blocking=True)
+                    xd[j][a0:a1].copy_(x_pin[a0:a1], non_blocking=True)
+                    ev_up[j].record(up_s)
 
-            for _ in range(2):
-                e2e_step()
+            def compute(j):
+                stream.wait_event(ev_up[j])
+                if per != M:
+                    dist.all_gather_into_tensor(hd[j], hd[j][a0:a1])
+                    dist.all_gather_into_tensor(xd[j], xd[j][a0:a1])
+                y = mlp(xd[j], hd[j])
+                ev_comp[j].record(stream)
+                return y
+
+            def download(j, y):
+                with torch.cuda.stream(down_s):
+                    down_s.wait_event(ev_comp[j])
+                    if rank == 0:
+                        out_pin[j].copy_(y, non_blocking=True)
+                    ev_down[j].record(down_s)
+
+            def run_e2e(n):
+                upload(0)
+                for i in range(n):
+                    if i + 1 < n:
+                        upload((i + 1) % 2)
+                    download(i % 2, compute(i % 2))
+                stream.wait_event(ev_down[(n - 1) % 2])
+
+            run_e2e(3)
             torch.cuda.synchronize()
             if comm:
                 dist.barrier()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            n_e2e = max(3, args.steps // 4)
-            for _ in range(n_e2e):
-                e2e_step()
+            up_s.wait_event(e0)
+            n_e2e = max(4, args.steps // 2)
+            run_e2e(n_e2e)
             e1.record(stream)
             torch.cuda.synchronize()
             te = torch.tensor([e0.elapsed_time(e1) / n_e2e], device=dev, dtype=torch.float64)
@@ -336,7 +398,10 @@ def run_ours(args):
                    "unit": "TOPS", "ms_per_step": round(e2e_ms, 4),
                    "h2d_bytes_per_step": h_cpu.numel() * 2 + x_cpu.numel() * 2,
                    "d2h_bytes_per_step": x_cpu.numel() * 2,
-                   "api": "TPDiTMLPINT8.forward (h3tp.tp_dit), pinned host buffers"}
+                   "api": "TPDiTMLPINT8.forward (h3tp.tp_dit) per step, inputs uploaded from "
+                          "pinned host memory (1/t per rank, all-gathered over NVLink at t > 1) "
+                          "and the residual read back by rank 0; copies overlapped on two "
+                          "streams; bytes are per step for the whole job"}
 
         err = _native.device_error(local)
         if comm:
@@ -382,7 +447,7 @@ def run_ours(args):
     }
     clk = clocks.summary()
     line["clocks"] = {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
-                      "reasons": clk["reasons"]}
+                      "reasons": clk["reasons"], "samples": clk["samples"]}
     if e2e is not None:
         line["e2e"] = e2e
     if world == 1 and not args.no_cpu:

@@ -233,9 +233,9 @@ int h3_peer_gather(const void* const* bases, int world, int rank, int64_t flags_
 
 /* ----------------------------------------------------------------------------
  * Column linear without allocation.  No counterpart in the reference: added for
- * callers that may not allocate device memory (code running during CUDA graph
- * capture, runtimes that budget all device memory through their own pool, paths that
- * cannot afford cudaMalloc's synchronisation).
+ * callers that may not allocate device memory (runtimes that budget all device
+ * memory through their own pool, paths that cannot afford cudaMalloc's implicit
+ * device synchronisation).
  * ------------------------------------------------------------------------- */
 
 /* Bytes of the file-scope static __device__ scratch array that every GPU loading

@@ -68,6 +68,7 @@ struct Args {
   int64_t N;          // output columns (SWIGLU: gate rows = n_packed / 2)
   int64_t K;
   int tiles_m, tiles_n, num_kb;
+  int group_m, group_n;  // tile raster (tile_coords)
   void* out;
   int out_kind;
   const float* row_scale;
@@ -259,13 +260,26 @@ H3_DEV void tmem_ld8_nowait(uint32_t taddr, uint32_t (&r)[8]) {
 
 H3_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// Tile order: groups of 16 M-blocks sweep all N-blocks, so concurrently running
-// CTAs share A rows and B columns in L2.
-H3_DEV void tile_coords(int tile, int tiles_m, int tiles_n, int& mb, int& nb) {
-  const int group = 16 * tiles_n;
+// Tile order.  group_n > 0: groups of group_n N-blocks (a weight slab that stays in
+// L2) sweep all M-blocks, N fastest, so A is read from HBM once per group; otherwise
+// groups of group_m M-blocks (16 when unset) sweep all N-blocks, M fastest, so B is
+// read once per group.  The host picks the form with less HBM traffic.
+H3_DEV void tile_coords(int tile, const Args& a, int& mb, int& nb) {
+  if (a.group_n > 0) {
+    const int group = a.group_n * a.tiles_m;
+    const int g = tile / group;
+    const int first_n = g * a.group_n;
+    const int gn = min(a.tiles_n - first_n, a.group_n);
+    const int local = tile - g * group;
+    nb = first_n + local % gn;
+    mb = local / gn;
+    return;
+  }
+  const int G = a.group_m > 0 ? a.group_m : 16;
+  const int group = G * a.tiles_n;
   const int g = tile / group;
-  const int first_m = g * 16;
-  const int gm = min(tiles_m - first_m, 16);
+  const int first_m = g * G;
+  const int gm = min(a.tiles_m - first_m, G);
   const int local = tile - g * group;
   mb = first_m + local % gm;
   nb = local / gm;
@@ -545,7 +559,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         int mb, nb;
-        tile_coords(tile, args.tiles_m, args.tiles_n, mb, nb);
+        tile_coords(tile, args, mb, nb);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(smem_u32(empty + stage), phase ^ 1u, abort_flag, args.err)) {
             ok = false;
@@ -622,7 +636,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
       int mb, nb;
-      tile_coords(tile, args.tiles_m, args.tiles_n, mb, nb);
+      tile_coords(tile, args, mb, nb);
       if (!mbar_wait(smem_u32(tfull + acc), acc_phase, abort_flag, args.err)) break;
       tc_fence_after();
       const int64_t row = (int64_t)mb * BM + quad * 32 + lane;
@@ -719,7 +733,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       bool ok = true;
       for (int tile = cluster_id; tile < total_tiles && ok; tile += clusters) {
         int mb, nb;
-        tile_coords(tile, args.tiles_m, args.tiles_n, mb, nb);
+        tile_coords(tile, args, mb, nb);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(smem_u32(empty + stage), phase ^ 1u, abort_flag, args.err)) {
             ok = false;
@@ -804,7 +818,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     uint32_t acc_phase = 0;
     for (int tile = cluster_id; tile < total_tiles; tile += clusters) {
       int mb, nb;
-      tile_coords(tile, args.tiles_m, args.tiles_n, mb, nb);
+      tile_coords(tile, args, mb, nb);
       if (!mbar_wait(smem_u32(tfull + acc), acc_phase, abort_flag, args.err)) break;
       tc_fence_after();
       const int64_t row = (int64_t)mb * BM2 + (int64_t)rank * BM + quad * 32 + lane;
@@ -871,6 +885,21 @@ static bool device_is_sm100(int dev) {
   return cache[dev] == 1;
 }
 
+// Chooses the tile raster: keep a slab of A (group_m M-blocks) or of B (group_n
+// N-blocks) of about 32 MB resident in the 126 MB L2 while the other operand streams,
+// whichever reads fewer bytes from HBM: A + B * ceil(tiles_m / group_m) against
+// B + A * ceil(tiles_n / group_n).
+static void set_raster(Args& a, int64_t a_block_bytes, int64_t b_block_bytes) {
+  const int64_t budget = 32ll << 20;
+  const int64_t gm = std::max<int64_t>(1, std::min<int64_t>(a.tiles_m, budget / a_block_bytes));
+  const int64_t gn = std::max<int64_t>(1, std::min<int64_t>(a.tiles_n, budget / b_block_bytes));
+  const int64_t A = a_block_bytes * a.tiles_m, B = b_block_bytes * a.tiles_n;
+  const int64_t m_cost = A + B * ((a.tiles_m + gm - 1) / gm);
+  const int64_t n_cost = B + A * ((a.tiles_n + gn - 1) / gn);
+  a.group_m = n_cost < m_cost ? 0 : (int)gm;
+  a.group_n = n_cost < m_cost ? (int)gn : 0;
+}
+
 template <int EPI>
 static int launch(const int8_t* q, const int8_t* w, int64_t M, int64_t N, int64_t K, Args args,
                   cudaStream_t stream) {
@@ -902,6 +931,7 @@ static int launch(const int8_t* q, const int8_t* w, int64_t M, int64_t N, int64_
   args.tiles_m = (int)((M + (pair ? BM2 : BM) - 1) / (pair ? BM2 : BM));
   args.tiles_n = (int)((N + tile_n - 1) / tile_n);
   args.num_kb = (int)((K + BK - 1) / BK);
+  set_raster(args, (pair ? BM2 : BM) * K, (EPI == EPI_SWIGLU ? 2 * tile_n : tile_n) * K);
   args.err = h3host::error_word(dev);
   if (args.err == nullptr) return H3_ERR_CUDA;
   if (args.row.err == nullptr) args.row.err = args.err;
@@ -1027,12 +1057,10 @@ extern "C" int h3_int8_gemm_row_dequant(const int8_t* q, const int8_t* w, int64_
 // ---------------------------------------------------------------------------
 // Column linear that allocates nothing.
 //
-// For callers that must not allocate device memory: code running while a CUDA
-// stream is being captured into a graph (an allocation there is illegal or breaks
-// the capture), runtimes that account for every byte of device memory through their
-// own pool (the ComfyUI rank worker budgets weights and activations; an allocation
-// behind its back defeats that budget), and latency-critical paths where
-// cudaMalloc's implicit synchronisation is unacceptable.  The activation codes, the
+// For callers that must not allocate device memory: runtimes that account for every
+// byte of device memory through their own pool (the ComfyUI rank worker budgets
+// weights and activations; an allocation behind its back defeats that budget), and
+// latency-critical paths where cudaMalloc's implicit synchronisation is unacceptable.  The activation codes, the
 // row scales and the device error word live in one file-scope static __device__
 // array of H3_NOALLOC_SCRATCH_BYTES, held by every GPU that loads this library until
 // the process exits.  Every call on a device shares that array and leaves its
@@ -1116,6 +1144,7 @@ extern "C" int h3_column_linear_noalloc(const void* x_f16, int64_t m, int64_t k,
   args.tiles_m = (int)((m + (pair ? BM2 : BM) - 1) / (pair ? BM2 : BM));
   args.tiles_n = (int)((n + BN - 1) / BN);
   args.num_kb = (int)((k + BK - 1) / BK);
+  set_raster(args, (pair ? BM2 : BM) * k, BN * k);
   args.err = err;
   args.row.err = err;
   const int64_t tiles = (int64_t)args.tiles_m * args.tiles_n;

@@ -1,6 +1,6 @@
 """h3_column_linear_noalloc: the column linear for callers that may not allocate device
-memory (during CUDA graph capture, inside runtimes that budget every device byte
-through their own pool, on paths that cannot take cudaMalloc's synchronisation).
+memory (inside runtimes that budget every device byte through their own pool, on
+paths that cannot take cudaMalloc's implicit synchronisation).
 
 It is called directly through the C ABI and must reproduce, bit for bit, the result of
 the existing two-call path (h3_column_quantize then h3_int8_gemm_column) on two calls
