@@ -210,25 +210,26 @@ int h3_gated_add(const void* branch, int branch_kind, int64_t rows, int64_t widt
  *
  * bases[w] (w < world, world in {2, 4, 8}) is rank w's workspace buffer mapped into
  * this process (every rank's buffer has the same layout; the caller maps them, e.g.
- * with torch symmetric memory):
+ * with torch symmetric memory).  Rank r owns rows [r*per, min(rows, (r+1)*per)),
+ * per = ceil(rows / world).  Layout of each buffer:
  *   flags_off    1024 bytes of u32 flags, zeroed on every rank before the first call
- *   partial_off  fp16 [rows, width] partial of that rank (h3_int8_gemm_row_encode)
- *   block_off    fp16 [rows, width] finished rows of that rank's row block
- * Rank r owns rows [r*per, min(rows, (r+1)*per)), per = ceil(rows / world).
- * h3_peer_reduce: fixed rank-order reduction of the owned rows from every rank's
- * partial, decode, dequant and gated residual update of those rows of residual_f16
- * (also copied into this rank's block); h3_peer_gather: copies the peers' finished
- * rows into residual_f16.  Every rank calls both, in that order, on one stream, with
- * the same `epoch` (1, 2, 3, ... per call).  Waits for peers are bounded (2 s); a
- * wait that gives up leaves H3_ERR_TIMEOUT in h3_device_error and the workspace must
- * be re-created.  width % 8 == 0; pointers 16-byte aligned. */
+ *   partial_off  fp16 [rows][width]: that rank's partial (h3_int8_gemm_row_encode)
+ *   final_off    fp16 [rows][width]: the other ranks' finished rows
+ * One call, on one stream, the same `epoch` (1, 2, 3, ... per call) on every rank:
+ *   h3_peer_reduce  loads the owned rows of every rank's partial (NVLink loads), fixed
+ *       rank-order reduction, decode, dequant and gated residual update of those rows
+ *       of residual_f16, also stored into every peer's final area (NVLink stores);
+ *   h3_peer_gather  copies the peers' finished rows into residual_f16.
+ * Waits for peers are bounded (2 s); a wait that gives up leaves H3_ERR_TIMEOUT in
+ * h3_device_error and the workspace must be re-created.  width % 8 == 0; pointers
+ * 16-byte aligned. */
 int h3_peer_reduce(const void* const* bases, int world, int rank, int64_t flags_off,
-                   int64_t partial_off, int64_t block_off, int64_t rows, int64_t width,
+                   int64_t partial_off, int64_t final_off, int64_t rows, int64_t width,
                    int shift, const float* row_scale, const float* weight_scale,
                    void* residual_f16, const float* gate, int64_t gate_rows,
                    const int32_t* labels, uint32_t epoch, void* stream);
 int h3_peer_gather(const void* const* bases, int world, int rank, int64_t flags_off,
-                   int64_t block_off, int64_t rows, int64_t width, void* residual_f16,
+                   int64_t final_off, int64_t rows, int64_t width, void* residual_f16,
                    uint32_t epoch, void* stream);
 
 /* ----------------------------------------------------------------------------

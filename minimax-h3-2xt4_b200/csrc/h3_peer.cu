@@ -4,33 +4,35 @@
 //
 // Every rank owns one buffer of the same layout, mapped into every other rank's
 // address space (torch symmetric memory); `bases[w]` is rank w's buffer as seen from
-// this process:
+// this process.  Rank r owns rows [r * per, min(rows, (r + 1) * per)) of the output.
 //
 //   [flags_off]    ready[64] u32 | done[64] u32 | counter u32   (zeroed once at set-up)
-//   [partial_off]  fp16 [rows, width]   this rank's encoded partial (written by the
-//                                       row GEMM's encode epilogue)
-//   [block_off]    fp16 [rows, width]   finished residual rows of this rank's block
+//   [partial_off]  fp16 [rows][width]: this rank's encoded partial (written by the row
+//                  GEMM's encode epilogue)
+//   [final_off]    fp16 [rows][width]: the other ranks' finished rows, stored there by
+//                  their reduce kernels
 //
 // One call with epoch e (the same on every rank, increasing by one per call):
 //   reduce kernel  each CTA stores e into ready[rank] of every rank (release, system
-//                  scope), waits until its own ready[w] >= e for every w, then sums the
-//                  partials of this rank's row block [row_begin, row_end) in rank
-//                  order 0..world-1 (fp32, one fp16 rounding at the end, the bits of an
-//                  NCCL fp16 SUM at world 2), decodes, dequantises and applies the
-//                  gated residual to those rows of the local residual, and copies the
-//                  finished rows into its block buffer.  The last CTA to finish stores
-//                  e into done[rank] of every rank.
+//                  scope), waits until its own ready[w] >= e for every w, then loads
+//                  the rows it owns from every rank's partial (coalesced NVLink
+//                  loads), sums them in rank order 0..world-1 (fp32, one fp16 rounding
+//                  at the end, the bits of an NCCL fp16 SUM at world 2), decodes,
+//                  dequantises and applies the gated residual to those rows of the
+//                  local residual, and stores the finished rows into every peer's final
+//                  area (coalesced NVLink stores, in the other direction of the links).
+//                  The last CTA to finish stores e into done[rank] of every rank.
 //   gather kernel  waits until done[w] >= e for every peer w and copies the peers'
-//                  finished rows from their block buffers into the local residual.
+//                  finished rows from its own final area into the residual (local).
 //
-// Reuse across calls is ordered by the flags: a rank rewrites its partial only after
-// its gather of the previous call, which waited for every peer's done (so every peer
-// has finished reading it), and a rank rewrites its block buffer only after every peer
-// signalled ready for the new call (so every peer's previous gather has finished).
-// All waits are bounded (2 s of %globaltimer); a wait that gives up records
-// H3_ERR_TIMEOUT in the library's device error word, and a reduce that timed out
-// publishes no done flag, so the peers' gathers time out too rather than read
-// unfinished rows.
+// Reuse across calls is ordered by the flags: a rank rewrites its partial only in its
+// next row GEMM, after its gather of this call, which waited for every peer's done
+// (so every peer has finished loading it); and a rank stores into a peer's final area
+// only after that peer signalled ready for the new call (so the peer's previous
+// gather has finished).  All waits are bounded (2 s of %globaltimer); a wait that
+// gives up records H3_ERR_TIMEOUT in the library's device error word, and a reduce
+// that timed out publishes no done flag, so the peers' gathers time out too rather
+// than read unfinished rows.
 
 #include "h3_common.cuh"
 
@@ -44,7 +46,7 @@ constexpr int THREADS = 256;
 
 struct Args {
   uint64_t bases[MAX_WORLD];
-  int64_t flags_off, partial_off, block_off;
+  int64_t flags_off, partial_off, final_off;
   int world, rank;
   int64_t rows, width, row_begin, row_end, per;
   float up;
@@ -98,6 +100,12 @@ H3_DEV bool wait_all(const Args& a, int64_t region, bool skip_self) {
   return ok;
 }
 
+// Reads data another GPU stored into this GPU's memory (through L2, not L1).
+H3_DEV uint4 load_received(uint64_t base, int64_t off) {
+  return __ldcg(reinterpret_cast<const uint4*>(base + off));
+}
+
+// Reads another GPU's memory over NVLink (not cached).
 H3_DEV uint4 load_peer(uint64_t base, int64_t off) {
   return __ldcv(reinterpret_cast<const uint4*>(base + off));
 }
@@ -161,7 +169,8 @@ H3_DEV uint4 finish_chunk(const Args& a, const uint4 (&u)[W], int64_t r, int64_t
 
 template <int W>
 __global__ void __launch_bounds__(THREADS) reduce_kernel(const Args a) {
-  // Phase 0: this rank's partial is complete (stream order); announce it to every rank.
+  // Phase 0: this rank's partial is complete (stream order after the row GEMM);
+  // announce it to every rank.
   if ((int)threadIdx.x < W) {
     __threadfence_system();
     store_release(flag(a, threadIdx.x, READY, a.rank), a.epoch);
@@ -170,28 +179,33 @@ __global__ void __launch_bounds__(THREADS) reduce_kernel(const Args a) {
   if (ok) {
     const int64_t chunks = a.width >> 3;
     const int64_t total = (a.row_end - a.row_begin) * chunks;
-    uint4* block = reinterpret_cast<uint4*>(a.bases[a.rank] + a.block_off);
+    const int64_t first = a.row_begin * chunks;  // uint4 index of the block's first chunk
     uint4* res = reinterpret_cast<uint4*>(a.residual);
     for (int64_t i = blockIdx.x * (int64_t)THREADS + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * THREADS) {
-      const int64_t r = a.row_begin + i / chunks;
-      const int64_t c0 = (i % chunks) << 3;
-      const int64_t e = r * chunks + (c0 >> 3);  // uint4 index of the chunk
+      const int64_t e = first + i;  // uint4 index of the chunk in [rows][width]
+      const int64_t r = e / chunks;
+      const int64_t c0 = (e - r * chunks) << 3;
       uint4 u[W];
 #pragma unroll
-      for (int w = 0; w < W; ++w) u[w] = load_peer(a.bases[w], a.partial_off + e * 16);
+      for (int w = 0; w < W; ++w)
+        u[w] = w == a.rank ? load_received(a.bases[w], a.partial_off + e * 16)
+                           : load_peer(a.bases[w], a.partial_off + e * 16);
       const uint4 y = finish_chunk<W>(a, u, r, c0, res[e]);
       res[e] = y;
-      block[e] = y;
+#pragma unroll
+      for (int w = 0; w < W; ++w)
+        if (w != a.rank) reinterpret_cast<uint4*>(a.bases[w] + a.final_off)[e] = y;
     }
   } else if (threadIdx.x == 0) {
     atomicExch(a.err, H3_ERR_TIMEOUT);
   }
-  // Count this CTA (failures in the high half-word); the last one resets the counter
-  // and, when every CTA succeeded, publishes done to every rank.
+  // Every thread fences its stores to the peers; then count this CTA (failures in the
+  // high half-word); the last one resets the counter and, when every CTA succeeded,
+  // publishes done to every rank.
+  __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
     unsigned int* counter =
         reinterpret_cast<unsigned int*>(a.bases[a.rank] + a.flags_off + COUNTER);
     const unsigned int old = atomicAdd(counter, ok ? 1u : 0x10000u);
@@ -215,14 +229,14 @@ __global__ void __launch_bounds__(THREADS) gather_kernel(const Args a) {
   const int64_t chunks = a.width >> 3;
   const int64_t own = a.row_end - a.row_begin;
   const int64_t total = (a.rows - own) * chunks;
+  const uint64_t fin = a.bases[a.rank] + a.final_off;
   uint4* res = reinterpret_cast<uint4*>(a.residual);
   for (int64_t i = blockIdx.x * (int64_t)THREADS + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * THREADS) {
     int64_t r = i / chunks;
     if (r >= a.row_begin) r += own;
-    const int owner = (int)(r / a.per);
     const int64_t e = r * chunks + i % chunks;
-    res[e] = load_peer(a.bases[owner], a.block_off + e * 16);
+    res[e] = load_received(fin, e * 16);
   }
 }
 
@@ -236,13 +250,13 @@ cudaError_t launch(const Args& a, int blocks, bool gather, cudaStream_t st) {
 }
 
 int run(const void* const* bases, int world, int rank, int64_t flags_off, int64_t partial_off,
-        int64_t block_off, int64_t rows, int64_t width, int shift, const float* row_scale,
+        int64_t final_off, int64_t rows, int64_t width, int shift, const float* row_scale,
         const float* weight_scale, void* residual_f16, const float* gate, int64_t gate_rows,
         const int32_t* labels, uint32_t epoch, bool gather, void* stream) {
   if (bases == nullptr || residual_f16 == nullptr || (world != 2 && world != 4 && world != 8) ||
       rank < 0 || rank >= world || rows < 0 || width <= 0 || width % 8 || epoch == 0 ||
-      flags_off < 0 || partial_off < 0 || block_off < 0 || flags_off % 16 ||
-      partial_off % 16 || block_off % 16 || !h3host::aligned(residual_f16, 16))
+      flags_off < 0 || partial_off < 0 || final_off < 0 || flags_off % 16 ||
+      partial_off % 16 || final_off % 16 || !h3host::aligned(residual_f16, 16))
     return H3_ERR_INVALID;
   if (!gather) {
     if (row_scale == nullptr || weight_scale == nullptr || shift < 0 || shift > 60 ||
@@ -261,7 +275,7 @@ int run(const void* const* bases, int world, int rank, int64_t flags_off, int64_
   if (int s = h3host::bind_device_of(residual_f16, &dev)) return s;
   a.flags_off = flags_off;
   a.partial_off = partial_off;
-  a.block_off = block_off;
+  a.final_off = final_off;
   a.world = world;
   a.rank = rank;
   a.rows = rows;
@@ -296,19 +310,19 @@ int run(const void* const* bases, int world, int rank, int64_t flags_off, int64_
 }  // namespace h3
 
 extern "C" int h3_peer_reduce(const void* const* bases, int world, int rank, int64_t flags_off,
-                              int64_t partial_off, int64_t block_off, int64_t rows,
+                              int64_t partial_off, int64_t final_off, int64_t rows,
                               int64_t width, int shift, const float* row_scale,
                               const float* weight_scale, void* residual_f16, const float* gate,
                               int64_t gate_rows, const int32_t* labels, uint32_t epoch,
                               void* stream) {
-  return h3::peer::run(bases, world, rank, flags_off, partial_off, block_off, rows, width, shift,
+  return h3::peer::run(bases, world, rank, flags_off, partial_off, final_off, rows, width, shift,
                        row_scale, weight_scale, residual_f16, gate, gate_rows, labels, epoch,
                        false, stream);
 }
 
 extern "C" int h3_peer_gather(const void* const* bases, int world, int rank, int64_t flags_off,
-                              int64_t block_off, int64_t rows, int64_t width, void* residual_f16,
+                              int64_t final_off, int64_t rows, int64_t width, void* residual_f16,
                               uint32_t epoch, void* stream) {
-  return h3::peer::run(bases, world, rank, flags_off, 0, block_off, rows, width, 0, nullptr,
+  return h3::peer::run(bases, world, rank, flags_off, 0, final_off, rows, width, 0, nullptr,
                        nullptr, residual_f16, nullptr, 0, nullptr, epoch, true, stream);
 }

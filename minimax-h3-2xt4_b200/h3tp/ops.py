@@ -328,31 +328,31 @@ def gated_add(residual, branch, gate=None, labels=None):
     return residual
 
 
-def peer_reduce(bases, world: int, rank: int, flags_off: int, partial_off: int, block_off: int,
+def peer_reduce(bases, world: int, rank: int, flags_off: int, partial_off: int, final_off: int,
                 rows: int, width: int, shift: int, row_scale, weight_scale, residual,
                 gate=None, labels=None, epoch: int = 1):
-    """Reduce + fused gated-residual epilogue of this rank's row block over peer
-    memory (h3_peer_reduce); `bases` are the world buffer addresses (ints)."""
+    """Reduce + fused gated-residual epilogue of this rank's row block from every rank's
+    partial, finished rows stored into the peers' final areas (h3_peer_reduce)."""
     a = _vec(row_scale, rows, "row_scale")
     ws = _vec(weight_scale, width, "weight_scale")
     if not residual.is_contiguous():
         raise ValueError("residual must be contiguous (updated in place)")
     res, g, grows, lab = _gate_args(residual, gate, labels, rows, width)
     arr = (ctypes.c_void_p * world)(*bases)
-    N.call("h3_peer_reduce", arr, world, rank, flags_off, partial_off, block_off, rows, width,
+    N.call("h3_peer_reduce", arr, world, rank, flags_off, partial_off, final_off, rows, width,
            int(shift), a.data_ptr(), ws.data_ptr(), res.data_ptr(), _ptr(g), grows, _ptr(lab),
            int(epoch), _stream(res))
     return residual
 
 
-def peer_gather(bases, world: int, rank: int, flags_off: int, block_off: int, rows: int,
+def peer_gather(bases, world: int, rank: int, flags_off: int, final_off: int, rows: int,
                 width: int, residual, epoch: int = 1):
     """Copies the peers' finished row blocks into `residual` (h3_peer_gather)."""
     res = _need(residual, torch.float16, "residual", 2)
     if res.data_ptr() != residual.data_ptr() or tuple(res.shape) != (rows, width):
         raise ValueError("residual must be a contiguous fp16 [rows, width] tensor")
     arr = (ctypes.c_void_p * world)(*bases)
-    N.call("h3_peer_gather", arr, world, rank, flags_off, block_off, rows, width, res.data_ptr(),
+    N.call("h3_peer_gather", arr, world, rank, flags_off, final_off, rows, width, res.data_ptr(),
            int(epoch), _stream(res))
     return residual
 

@@ -2,14 +2,16 @@
 
 The reference sums the per-rank scaled-FP16 partials with NCCL's fp16 all-reduce and
 then runs the fused row-gate epilogue (tilelang_swiglu_quant.py:119-124,
-tilelang_dit_fusion.py:146-151).  Over NVSwitch every GPU can load from every peer's
-HBM directly, so here the exchange is two kernels of our own (csrc/h3_peer.cu):
+tilelang_dit_fusion.py:146-151).  Over NVSwitch every GPU can load from and store
+into every peer's HBM directly, so here the exchange is two kernels of our own
+(csrc/h3_peer.cu):
 
   1. the row GEMM's encode epilogue writes the partial straight into this rank's
      peer-mapped buffer (no staging copy);
-  2. h3_peer_reduce: each rank loads its row block of every rank's partial from peer
-     memory, sums in rank order, decodes, dequantises and updates its rows of the
-     gated residual (the same bits as h3_row_reduce_finish);
+  2. h3_peer_reduce: each rank loads its rows of every rank's partial (NVLink loads),
+     sums in rank order, decodes, dequantises and updates its rows of the gated
+     residual (the same bits as h3_row_reduce_finish), and stores the finished rows
+     into every peer (NVLink stores, the other direction of the links);
   3. h3_peer_gather: each rank copies the peers' finished rows into its residual.
 
 The buffers are torch symmetric memory (one allocation per rank, mapped into every
@@ -47,7 +49,8 @@ def available(comm) -> bool:
 
 
 class PeerWorkspace:
-    """One symmetric buffer per rank: flags | partial fp16 [rows, width] | block fp16."""
+    """One symmetric buffer per rank: flags | partial [rows][width] fp16 | final rows
+    [rows][width] fp16, for up to `rows` rows of `width` columns."""
 
     def __init__(self, group, device: torch.device, width: int, rows: int):
         import torch.distributed._symmetric_memory as symm
@@ -56,10 +59,10 @@ class PeerWorkspace:
         self.device = torch.device(device)
         self.width = int(width)
         self.capacity = int(rows)
-        part = -(-self.capacity * self.width * 2 // _ALIGN) * _ALIGN
+        region = -(-self.capacity * self.width * 2 // _ALIGN) * _ALIGN
         self.partial_off = FLAGS_BYTES
-        self.block_off = FLAGS_BYTES + part
-        nbytes = FLAGS_BYTES + 2 * part
+        self.final_off = FLAGS_BYTES + region
+        nbytes = FLAGS_BYTES + 2 * region
         with torch.cuda.device(self.device):
             self.buf = symm.empty(nbytes, dtype=torch.uint8, device=self.device)
             self.buf[:FLAGS_BYTES].zero_()
@@ -80,13 +83,13 @@ class PeerWorkspace:
 
     def reduce_and_gather(self, rows: int, shift: int, row_scale, weight_scale, residual,
                           gate=None, labels=None):
-        """Sums the partials written by every rank into `residual` (fp16 [rows, width],
-        updated in place on every rank)."""
+        """Sums the partials every rank wrote into partial() into `residual` (fp16
+        [rows, width], updated in place on every rank)."""
         self.epoch += 1
-        ops.peer_reduce(self.bases, self.world, self.rank, 0, self.partial_off, self.block_off,
+        ops.peer_reduce(self.bases, self.world, self.rank, 0, self.partial_off, self.final_off,
                         rows, self.width, shift, row_scale, weight_scale, residual, gate, labels,
                         self.epoch)
-        ops.peer_gather(self.bases, self.world, self.rank, 0, self.block_off, rows, self.width,
+        ops.peer_gather(self.bases, self.world, self.rank, 0, self.final_off, rows, self.width,
                         residual, self.epoch)
         return residual
 

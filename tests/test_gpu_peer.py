@@ -1,11 +1,14 @@
-"""The peer-memory row transport kernels (h3_peer_reduce / h3_peer_gather) on one GPU.
+"""The peer-memory row transport kernels (h3_peer_reduce, h3_peer_gather) on one GPU.
 
-Each emulated rank gets its own workspace buffer on the same device; every flag a
-kernel waits for is set before that kernel is launched (by an earlier kernel of the
-same stream or by the test), so no kernel ever waits for another one that runs at the
-same time.  The reduced, gated residual of every rank is compared bit for bit with the
-oracle's rank-order reduction; a flag that nothing sets checks the bounded wait.
-The same kernels across real NCCL ranks are covered by tests/test_gpu_tp_nccl.py."""
+Each emulated rank gets its own workspace buffer on the same device, and its row GEMM
+(h3_int8_gemm_row_encode) writes the encoded partial into that buffer; the partials
+are checked against the oracle's INT8 GEMM + encode.  Every flag a reduce or
+gather kernel waits for is set before that kernel is launched (by an earlier kernel
+of the same stream or by the test), so no kernel ever waits for another one that runs
+at the same time.  The reduced, gated residual of every rank is compared bit for bit
+with the oracle's rank-order reduction; a flag that nothing sets checks the bounded
+wait.  The same kernels across real NCCL ranks are covered by
+tests/test_gpu_tp_nccl.py."""
 import numpy as np
 import pytest
 import torch
@@ -15,10 +18,15 @@ pytestmark = pytest.mark.gpu
 FLAGS, READY, DONE = 1024, 0, 256
 
 
+def _region(rows, width):
+    return -(-rows * width * 2 // 256) * 256
+
+
 def _buffers(dev, world, rows, width):
-    part = -(-rows * width * 2 // 256) * 256
-    bufs = [torch.zeros(FLAGS + 2 * part, dtype=torch.uint8, device=dev) for _ in range(world)]
-    return bufs, FLAGS, FLAGS + part
+    partial = FLAGS
+    final = FLAGS + _region(rows, width)
+    nbytes = final + _region(rows, width)
+    return [torch.zeros(nbytes, dtype=torch.uint8, device=dev) for _ in range(world)], partial, final
 
 
 def _set(buf, region, ranks, epoch):
@@ -27,14 +35,15 @@ def _set(buf, region, ranks, epoch):
         flags[region // 4 + w] = epoch
 
 
-@pytest.mark.parametrize("world,rows,width", [(2, 130, 512), (4, 77, 264), (8, 99, 1024)])
-def test_peer_reduce_gather_bit_exact(cuda_device, oracle, world, rows, width):
-    from h3tp import ops, transport
+@pytest.mark.parametrize("world,rows,width,k", [(2, 130, 512, 512), (4, 77, 264, 256),
+                                                (8, 99, 1024, 256)])
+def test_peer_transport_bit_exact(cuda_device, oracle, world, rows, width, k):
+    from h3tp import _native, ops, transport
     rng = np.random.default_rng(world)
-    k_local = 1024
-    shift = transport.shift_for(k_local, world)
-    parts = [rng.integers(-2 ** 22, 2 ** 22, size=(rows, width)).astype(np.int32) for _ in range(world)]
-    enc = np.stack([oracle.fp16_encode(p, shift) for p in parts])
+    shift = transport.shift_for(k, world)
+    qs = [rng.integers(-128, 128, size=(rows, k), dtype=np.int8) for _ in range(world)]
+    ws = [rng.integers(-127, 128, size=(width, k), dtype=np.int8) for _ in range(world)]
+    enc = np.stack([oracle.fp16_encode(oracle.int8_gemm(q, w), shift) for q, w in zip(qs, ws)])
     a = rng.uniform(1e-4, 1e-2, size=rows).astype(np.float32)
     s = rng.uniform(1e-5, 1e-4, size=width).astype(np.float32)
     X = rng.standard_normal((rows, width)).astype(np.float16)
@@ -44,33 +53,36 @@ def test_peer_reduce_gather_bit_exact(cuda_device, oracle, world, rows, width):
     oracle.row_reduce_finish(enc, shift, a, s, out="residual", residual=ref, gate=G, labels=labels)
 
     dev = cuda_device
-    bufs, poff, boff = _buffers(dev, world, rows, width)
+    bufs, roff, foff = _buffers(dev, world, rows, width)
     bases = [b.data_ptr() for b in bufs]
-    for w in range(world):
-        bufs[w][poff:poff + 2 * rows * width].view(torch.float16).copy_(
-            torch.from_numpy(enc[w].reshape(-1)).to(dev))
     A, S = torch.from_numpy(a).to(dev), torch.from_numpy(s).to(dev)
     Gd, L = torch.from_numpy(G).to(dev), torch.from_numpy(labels).to(dev)
+    qd = [torch.from_numpy(q).to(dev) for q in qs]
+    wd = [torch.from_numpy(w).to(dev) for w in ws]
     res = [torch.from_numpy(X.copy()).to(dev) for _ in range(world)]
     for epoch in (1, 2):  # the second call reuses the buffers and advances the epoch
-        if epoch == 2:
-            for r in range(world):
-                res[r].copy_(torch.from_numpy(X))
+        for r in range(world):
+            res[r].copy_(torch.from_numpy(X))
+            part = bufs[r][roff:roff + rows * width * 2].view(torch.float16).view(rows, width)
+            ops.int8_gemm_row_encode(qd[r], wd[r], shift, out=part)
+        torch.cuda.synchronize()
+        for r in range(world):
+            got = bufs[r][roff:roff + rows * width * 2].view(torch.float16).cpu().numpy()
+            assert np.array_equal(got.view(np.uint16), enc[r].reshape(-1).view(np.uint16)), r
         for b in bufs:
             _set(b, READY, range(world), epoch)
         for r in range(world):
-            ops.peer_reduce(bases, world, r, 0, poff, boff, rows, width, shift, A, S, res[r], Gd, L,
+            ops.peer_reduce(bases, world, r, 0, roff, foff, rows, width, shift, A, S, res[r], Gd, L,
                             epoch)
         for r in range(world):
-            ops.peer_gather(bases, world, r, 0, boff, rows, width, res[r], epoch)
+            ops.peer_gather(bases, world, r, 0, foff, rows, width, res[r], epoch)
         torch.cuda.synchronize()
         for r in range(world):
             got = res[r].cpu().numpy()
             assert np.array_equal(got.view(np.uint16), ref.view(np.uint16)), f"rank {r} epoch {epoch}"
-            done = bufs[r][:FLAGS].view(torch.int32)[DONE // 4: DONE // 4 + world].cpu().numpy()
-            assert (done == epoch).all()
-            assert int(bufs[r][:FLAGS].view(torch.int32)[128]) == 0  # counter reset
-    from h3tp import _native
+            flags = bufs[r][:FLAGS].view(torch.int32)
+            assert (flags[DONE // 4: DONE // 4 + world].cpu().numpy() == epoch).all()
+            assert int(flags[128]) == 0  # counter reset
     assert _native.device_error(dev.index or 0) == 0
 
 
@@ -80,16 +92,16 @@ def test_peer_wait_gives_up_with_timeout_status(cuda_device):
     from h3tp import _native, ops
     dev = cuda_device
     rows, width = 16, 256
-    bufs, poff, boff = _buffers(dev, 2, rows, width)
+    bufs, roff, foff = _buffers(dev, 2, rows, width)
     bases = [b.data_ptr() for b in bufs]
     res = torch.zeros((rows, width), dtype=torch.float16, device=dev)
     A = torch.ones(rows, dtype=torch.float32, device=dev)
     S = torch.ones(width, dtype=torch.float32, device=dev)
     assert _native.device_error(dev.index or 0) == 0
-    ops.peer_reduce(bases, 2, 0, 0, poff, boff, rows, width, 0, A, S, res, None, None, 1)
+    ops.peer_reduce(bases, 2, 0, 0, roff, foff, rows, width, 0, A, S, res, None, None, 1)
     assert _native.device_error(dev.index or 0) == _native.H3_ERR_TIMEOUT
     assert int(bufs[1][:FLAGS].view(torch.int32)[DONE // 4]) == 0
-    ops.peer_gather(bases, 2, 0, 0, boff, rows, width, res, 1)
+    ops.peer_gather(bases, 2, 0, 0, foff, rows, width, res, 1)
     assert _native.device_error(dev.index or 0) == _native.H3_ERR_TIMEOUT
     assert _native.device_error(dev.index or 0) == 0  # reading clears it
 
@@ -97,13 +109,13 @@ def test_peer_wait_gives_up_with_timeout_status(cuda_device):
 def test_peer_rejects_bad_geometry(cuda_device):
     from h3tp import ops
     dev = cuda_device
-    bufs, poff, boff = _buffers(dev, 2, 4, 256)
+    bufs, roff, foff = _buffers(dev, 2, 4, 256)
     bases = [b.data_ptr() for b in bufs]
     A = torch.ones(4, dtype=torch.float32, device=dev)
     with pytest.raises(ValueError):   # world 3 is not a TP size of the path
-        ops.peer_reduce(bases + [bases[0]], 3, 0, 0, poff, boff, 4, 256, 0, A,
+        ops.peer_reduce(bases + [bases[0]], 3, 0, 0, roff, foff, 4, 256, 0, A,
                         torch.ones(256, device=dev), torch.zeros((4, 256), dtype=torch.float16,
                                                                  device=dev))
     with pytest.raises(ValueError):   # width not a multiple of 8
-        ops.peer_gather(bases, 2, 0, 0, boff, 4, 252, torch.zeros((4, 252), dtype=torch.float16,
+        ops.peer_gather(bases, 2, 0, 0, foff, 4, 252, torch.zeros((4, 252), dtype=torch.float16,
                                                                    device=dev))
