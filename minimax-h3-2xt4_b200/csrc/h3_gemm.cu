@@ -41,7 +41,9 @@ constexpr int EPI_WARPS = 16;                // four warps per 32-lane TMEM quad
 constexpr int EPI_PARTS = EPI_WARPS / 4;     // column slices of a tile, one per warp
 constexpr int THREADS = 64 + 32 * EPI_WARPS;  // warp 0 TMA, warp 1 MMA, warps 2.. epilogue
 constexpr int TMEM_COLS = 512;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+// per epilogue warp: 64 floats of staged weight scales (EPI_SWIGLU)
+constexpr int EPI_SMEM = EPI_WARPS * 64 * 4;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + EPI_SMEM;
 constexpr unsigned long long TIMEOUT_NS = 2000000000ull;
 
 // 2-SM (cta_group::2) variant: a CTA pair computes a 256 x 256 tile; each CTA stages
@@ -51,7 +53,7 @@ constexpr int BM2 = 256;
 constexpr int B_HALF = (BN / 2) * BK;          // 16 KiB
 constexpr int STAGES2 = 6;
 constexpr int STAGE2_BYTES = A_STAGE + B_HALF;  // 32 KiB per CTA
-constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 256;
+constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 256 + EPI_SMEM;
 
 // Instruction descriptor, kind::i8: D = S32 (bits 4-5 = 2), A = B = signed 8-bit
 // (bits 7-9 and 10-12 = 1), both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
@@ -306,12 +308,20 @@ H3_DEV void store_f16_chunk(__half* dst, int64_t n0, int64_t N, const float (&v)
   }
 }
 
+// stream: evict-first stores (__stcs) for outputs that are not read again soon
 template <int C>
-H3_DEV void store_f32_chunk(float* dst, int64_t n0, int64_t N, const float (&v)[C], bool vec) {
+H3_DEV void store_f32_chunk(float* dst, int64_t n0, int64_t N, const float (&v)[C], bool vec,
+                            bool stream = false) {
   if (vec && n0 + C <= N) {
     float4* p = reinterpret_cast<float4*>(dst);
 #pragma unroll
-    for (int i = 0; i < C / 4; ++i) p[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    for (int i = 0; i < C / 4; ++i) {
+      const float4 f = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      if (stream)
+        __stcs(p + i, f);
+      else
+        p[i] = f;
+    }
   } else {
 #pragma unroll
     for (int j = 0; j < C; ++j)
@@ -382,7 +392,7 @@ H3_DEV void load_scales(const float* w, int64_t n0, int64_t N, int scalar, float
 // ---------------------------------------------------------------------------
 template <int EPI>
 H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool row_ok, int nb,
-                          int part) {
+                          int part, float* wsm) {
   const int64_t N = args.N;
   if (EPI == EPI_SWIGLU) {
     // accumulator columns [0,128) = gate rows, [128,256) = up rows of this tile
@@ -391,6 +401,16 @@ H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool ro
     const float a = row_ok ? __ldg(args.row_scale + row) : 0.0f;
     const bool vec4 = args.scale_vec != 0;
     constexpr int SW = 8;  // columns per step: keeps the SwiGLU epilogue within 96 registers
+    // This warp's 32 gate and 32 up weight scales, staged in shared memory once per
+    // tile (one coalesced load per lane) and read back as broadcasts.
+    const int lane = threadIdx.x & 31;
+    __syncwarp();
+    {
+      const int64_t nl = n_base + lane;
+      wsm[lane] = nl < N ? __ldg(args.weight_scale + nl) : 0.0f;
+      wsm[32 + lane] = nl < N ? __ldg(args.weight_scale + N + nl) : 0.0f;
+    }
+    __syncwarp();
 #pragma unroll 1
     for (int c = 0; c < GCOLS / SW; ++c) {
       const int64_t n0 = n_base + c * SW;
@@ -399,8 +419,13 @@ H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool ro
       tmem_ld8_nowait(tbase + part * GCOLS + c * SW, rg);
       tmem_ld8_nowait(tbase + BN / 2 + part * GCOLS + c * SW, ru);
       float wg[SW], wu[SW];
-      load_scales<SW>(args.weight_scale, n0, N, 0, wg, vec4);
-      load_scales<SW>(args.weight_scale + N, n0, N, 0, wu, vec4);
+#pragma unroll
+      for (int i = 0; i < SW / 4; ++i) {
+        const float4 g4 = reinterpret_cast<const float4*>(wsm + c * SW)[i];
+        const float4 u4 = reinterpret_cast<const float4*>(wsm + 32 + c * SW)[i];
+        wg[4 * i] = g4.x; wg[4 * i + 1] = g4.y; wg[4 * i + 2] = g4.z; wg[4 * i + 3] = g4.w;
+        wu[4 * i] = u4.x; wu[4 * i + 1] = u4.y; wu[4 * i + 2] = u4.z; wu[4 * i + 3] = u4.w;
+      }
       float bg[SW], bu[SW];
       if (args.bias != nullptr) {
         load_scales<SW>(args.bias, n0, N, 0, bg, vec4);
@@ -423,7 +448,7 @@ H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool ro
       if (row_ok) {
         if (args.out_kind == H3_OUT_F32)
           store_f32_chunk<SW>(reinterpret_cast<float*>(args.out) + row * N + n0, n0, N, y,
-                              (N & 3) == 0);
+                              (N & 3) == 0, true);
         else
           store_f16_chunk<SW>(reinterpret_cast<__half*>(args.out) + row * N + n0, n0, N, y,
                               (N & 7) == 0);
@@ -517,6 +542,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* wsm = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + 256) +
+               (threadIdx.x / 32 >= 2 ? (threadIdx.x / 32 - 2) * 64 : 0);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -641,7 +668,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const int64_t row = (int64_t)mb * BM + quad * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-      epilogue_tile<EPI>(args, tbase, row, row < args.M, nb, part);
+      epilogue_tile<EPI>(args, tbase, row, row < args.M, nb, part, wsm);
       tc_fence_before();
       mbar_arrive(smem_u32(tempty + acc));
       acc ^= 1;
@@ -686,6 +713,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* wsm = reinterpret_cast<float*>(smem + STAGES2 * STAGE2_BYTES + 256) +
+               (threadIdx.x / 32 >= 2 ? (threadIdx.x / 32 - 2) * 64 : 0);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -823,7 +852,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const int64_t row = (int64_t)mb * BM2 + (int64_t)rank * BM + quad * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-      epilogue_tile<EPI>(args, tbase, row, row < args.M, nb, part);
+      epilogue_tile<EPI>(args, tbase, row, row < args.M, nb, part, wsm);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(cluster_addr(smem_u32(tempty + acc), 0));
