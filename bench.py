@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--ffn", type=int, default=8192)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--payload", choices=["fp16", "int8_gather"], default="fp16",
+                    help="row partial payload at TP > 1 (scaled fp16, or the packed INT8 scheme)")
     return ap.parse_args()
 
 
@@ -272,7 +274,9 @@ def run_ours(args):
     M, hidden, ffn = args.tokens, args.hidden, args.ffn
     w1, s1, w2, s2 = make_weights(hidden, ffn)
     h_cpu, x_cpu = make_inputs(M, hidden)
-    mlp = TPDiTMLPINT8(hidden, ffn, rank, world, device=dev, comm=comm)
+    from h3tp.h3_operator_policy import H3OperatorPolicy
+    mlp = TPDiTMLPINT8(hidden, ffn, rank, world, device=dev, comm=comm,
+                       policy=H3OperatorPolicy(row_payload=args.payload))
     mlp.fc1.load_shard_from_full(w1, s1)
     mlp.fc2.load_shard_from_full(w2, s2)
     h = h_cpu.to(dev)
@@ -295,7 +299,8 @@ def run_ours(args):
             fc1_events.append((e0, e1))
         sq.row_linear(act, mlp.fc2.weight, mlp.fc2.weight_scale, comm,
                       mode=mlp.fc2.operator_policy.fc2_quantizer, scaled_transport=True,
-                      residual=x, transport=mlp.fc2.operator_policy.row_transport)
+                      residual=x, transport=mlp.fc2.operator_policy.row_transport,
+                      payload=mlp.fc2.operator_policy.row_payload)
 
     with torch.no_grad():
         for _ in range(max(3, args.warmup)):
@@ -435,6 +440,7 @@ def run_ours(args):
                    "tp": world, "parallelism": f"tp{world}",
                    "fc2_quantizer": mlp.fc2.operator_policy.fc2_quantizer,
                    "row_transport": mlp.fc2.operator_policy.row_transport,
+                   "row_payload": mlp.fc2.operator_policy.row_payload,
                    "l2": "inputs larger than L2 (h = 201 MB per step), no flush"},
         "roofline": {"kernel": "gemm_i8_kernel<EPI_SWIGLU> (FC1)", "bound": "tensor",
                      "achieved": round(achieved, 2), "peak": round(int8_peak, 1), "unit": "TOPS",

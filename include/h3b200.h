@@ -50,7 +50,8 @@ enum { H3_DIV_RN = 0, H3_DIV_FAST = 1 };
 enum {
   H3_OUT_F32 = 0,      /* fp32 store                                                   */
   H3_OUT_F16 = 1,      /* fp16 store (round to nearest even)                           */
-  H3_OUT_RESIDUAL = 2  /* gated residual update in place: X = f16(fma(f16(y), G, X))    */
+  H3_OUT_RESIDUAL = 2, /* gated residual update in place: X = f16(fma(f16(y), G, X))    */
+  H3_OUT_I32 = 3       /* h3_unpack8_finish only: the restored INT32 sum, no dequant    */
 };
 
 /* ----------------------------------------------------------------------------
@@ -202,6 +203,31 @@ int h3_gated_add(const void* branch, int branch_kind, int64_t rows, int64_t widt
                  const int32_t* labels, void* stream);
 
 /* ----------------------------------------------------------------------------
+ * Packed INT8 transport, the reference's 'int8_gather' scheme
+ * (tilelang_transport_tradeoffs.py:40-88, tilelang_transport_p2.py:28-42, torch
+ * statement benchmarks/tp2_tradeoffs.py:73-78).  Payload of a [rows, width] INT32
+ * partial (width % 128 == 0): uint8 [rows, width/128 * 132]; per 128-column group
+ * 128 codes then the 4 bytes of the fp32 scale:
+ *   scale = max(max|f32(P)| *rn f32(1/127), f32(1e-8)),
+ *   q = clamp(rint(f32(P) /rn scale), -127, 127)
+ * Reconstruction over `world` payloads, in rank order:
+ *   restored = rint( f32(q_0) *rn s_0 +rn f32(q_1) *rn s_1 +rn ... )
+ * ------------------------------------------------------------------------- */
+
+/* INT8 GEMM with the pack fused into the epilogue (int_mm + pack_int8). */
+int h3_int8_gemm_row_pack8(const int8_t* q, const int8_t* w, int64_t m, int64_t n,
+                           int64_t k, void* out_u8, void* stream);
+/* Standalone pack of an INT32 partial (pack_int8). */
+int h3_pack8(const int32_t* partial, int64_t rows, int64_t width, void* out_u8, void* stream);
+/* Reconstruction of `world` payloads (part_stride bytes apart) + the row epilogue
+ * y = (f32(restored) *rn row_scale[m]) *rn weight_scale[n], stored per out_kind as in
+ * h3_row_reduce_finish; out_kind H3_OUT_I32 stores the restored INT32 (unpack_int8). */
+int h3_unpack8_finish(const void* parts_u8, int world, int64_t part_stride, int64_t rows,
+                      int64_t width, const float* row_scale, const float* weight_scale,
+                      int out_kind, void* out, void* residual_f16, const float* gate,
+                      int64_t gate_rows, const int32_t* labels, void* stream);
+
+/* ----------------------------------------------------------------------------
  * Row transport over NVLink peer memory.  Replaces, for the residual form of the
  * row output, the reference's NCCL fp16 SUM of the encoded partials
  * (tilelang_transport_p2.py:57-58, tilelang_swiglu_quant.py:116-127) and the fused
@@ -228,6 +254,14 @@ int h3_peer_reduce(const void* const* bases, int world, int rank, int64_t flags_
                    int shift, const float* row_scale, const float* weight_scale,
                    void* residual_f16, const float* gate, int64_t gate_rows,
                    const int32_t* labels, uint32_t epoch, void* stream);
+/* h3_peer_reduce for packed INT8 payloads (h3_int8_gemm_row_pack8 output at
+ * partial_off): restored = rint(rank-order sum of f32(q_w) *rn s_w), then the same
+ * epilogue, final-row stores and flags.  width % 128 == 0. */
+int h3_peer_reduce_int8(const void* const* bases, int world, int rank, int64_t flags_off,
+                        int64_t partial_off, int64_t final_off, int64_t rows, int64_t width,
+                        const float* row_scale, const float* weight_scale, void* residual_f16,
+                        const float* gate, int64_t gate_rows, const int32_t* labels,
+                        uint32_t epoch, void* stream);
 int h3_peer_gather(const void* const* bases, int world, int rank, int64_t flags_off,
                    int64_t final_off, int64_t rows, int64_t width, void* residual_f16,
                    uint32_t epoch, void* stream);

@@ -63,7 +63,14 @@ constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >
 constexpr uint32_t IDESC2 = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
                             ((uint32_t)(BM2 >> 4) << 24);
 
-enum Epi { EPI_I32 = 0, EPI_COLUMN = 1, EPI_SWIGLU = 2, EPI_ROW_ENCODE = 3, EPI_ROW_DEQUANT = 4 };
+enum Epi {
+  EPI_I32 = 0,
+  EPI_COLUMN = 1,
+  EPI_SWIGLU = 2,
+  EPI_ROW_ENCODE = 3,
+  EPI_ROW_DEQUANT = 4,
+  EPI_ROW_PACK8 = 5
+};
 
 struct Args {
   int64_t M;          // rows of A / output rows
@@ -454,6 +461,54 @@ H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool ro
                               (N & 7) == 0);
       }
     }
+  } else if (EPI == EPI_ROW_PACK8) {
+    // Packed INT8 transport payload (tilelang_transport_tradeoffs.py:40-62): per row and
+    // 128-column group, scale = max(max|f32(P)| *rn f32(1/127), 1e-8) and
+    // q = clamp(rint(f32(P) /rn scale), -127, 127).  A group is the columns of two warps
+    // of the same TMEM lane quadrant (parts 2g', 2g'+1); each warp reads the whole group
+    // from TMEM for the maximum (no exchange between warps) and codes its own 64.
+    constexpr int COLS = BN / EPI_PARTS;  // 64
+    const int gl = part >> 1;             // group within the tile
+    const int64_t g = (int64_t)nb * (BN / 128) + gl;
+    if (g * 128 >= N) return;  // warp-uniform: the whole group is past the last column
+    float m = 0.0f;
+#pragma unroll 1
+    for (int c = 0; c < 128 / 16; ++c) {
+      uint32_t r[16];
+      tmem_ld16_nowait(tbase + gl * 128 + c * 16, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) m = fmaxf(m, fabsf(__int2float_rn((int32_t)r[j])));
+    }
+    const float scale = fmaxf(__fmul_rn(m, f32_bits(H3_INV127_BITS)), f32_bits(0x322bcc77u));
+    const float inv = __fdiv_rn(1.0f, scale);
+    uint8_t* dst = reinterpret_cast<uint8_t*>(args.out) + row * ((N / 128) * 132) + g * 132;
+#pragma unroll 1
+    for (int c = 0; c < COLS / 16; ++c) {
+      uint32_t r[16];
+      tmem_ld16_nowait(tbase + part * COLS + c * 16, r);
+      tmem_wait_ld();
+      if (!row_ok) continue;
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        uint32_t b[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          // |x / scale| <= 127 (1 + 2^-23): the clamp is kept for form's sake, the code
+          // is the low byte of RN(q + 1.5 * 2^23)
+          const float q = fminf(127.0f, fmaxf(-127.0f, div_by_scale(
+                                                             __int2float_rn((int32_t)r[4 * k + e]),
+                                                             scale, inv)));
+          b[e] = __float_as_uint(__fadd_rn(q, 12582912.0f));
+        }
+        w[k] = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
+      }
+      uint32_t* d = reinterpret_cast<uint32_t*>(dst + (part & 1) * COLS + c * 16);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) d[k] = w[k];
+    }
+    if (row_ok && (part & 1) == 0) *reinterpret_cast<float*>(dst + 128) = scale;
   } else {
     constexpr int COLS = BN / EPI_PARTS;  // accumulator columns of this warp
     const int64_t n_base = (int64_t)nb * BN + part * COLS;
@@ -1055,6 +1110,14 @@ extern "C" int h3_int8_gemm_row_encode(const int8_t* q, const int8_t* w, int64_t
   a.out = out_f16;
   a.enc_factor = ldexpf(1.0f, -shift);
   return launch<EPI_ROW_ENCODE>(q, w, m, n, k, a, (cudaStream_t)stream);
+}
+
+extern "C" int h3_int8_gemm_row_pack8(const int8_t* q, const int8_t* w, int64_t m, int64_t n,
+                                      int64_t k, void* out_u8, void* stream) {
+  if (out_u8 == nullptr || n % 128 != 0 || !h3host::aligned(out_u8, 16)) return H3_ERR_INVALID;
+  Args a = blank_args();
+  a.out = out_u8;
+  return launch<EPI_ROW_PACK8>(q, w, m, n, k, a, (cudaStream_t)stream);
 }
 
 extern "C" int h3_int8_gemm_row_dequant(const int8_t* q, const int8_t* w, int64_t m, int64_t n,

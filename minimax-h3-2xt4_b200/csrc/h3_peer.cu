@@ -110,10 +110,10 @@ H3_DEV uint4 load_peer(uint64_t base, int64_t off) {
   return __ldcv(reinterpret_cast<const uint4*>(base + off));
 }
 
-// One 8-column chunk: rank-order fp32 sum of the partials, one fp16 rounding, decode,
-// dequant, then X = f16(fma(f32(f16(y)), G[lab], f32(X))).
+// fp16 payloads (scaled-FP16 scheme): rank-order fp32 sum of the W partial chunks, one
+// fp16 rounding, truncating decode (tilelang_transport_p2.py:15-47).
 template <int W>
-H3_DEV uint4 finish_chunk(const Args& a, const uint4 (&u)[W], int64_t r, int64_t c0, uint4 x) {
+H3_DEV void restore_fp16(const Args& a, const uint4 (&u)[W], int32_t (&q)[8]) {
   float t[8];
 #pragma unroll
   for (int w = 0; w < W; ++w) {
@@ -130,6 +130,51 @@ H3_DEV uint4 finish_chunk(const Args& a, const uint4 (&u)[W], int64_t r, int64_t
       }
     }
   }
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    q[k] = __float2int_rz(__fmul_rn(__half2float(__float2half_rn(t[k])), a.up));
+}
+
+// Packed INT8 payloads ('int8_gather', tilelang_transport_tradeoffs.py:40-62 and
+// tilelang_transport_p2.py:28-42): rows of groups * 132 bytes, per 128-column group 128
+// codes then the fp32 scale.  restored = rint(sum_w f32(q_w) *rn s_w), rank order.
+template <int W>
+H3_DEV void load_restore_int8(const Args& a, int64_t r, int64_t c0, int32_t (&q)[8]) {
+  const int64_t g = c0 >> 7;
+  const int64_t row = a.partial_off + r * ((a.width >> 7) * 132) + g * 132;
+  const int64_t off = row + (c0 - (g << 7));
+  uint32_t w0[W], w1[W];
+  float sc[W];
+#pragma unroll
+  for (int w = 0; w < W; ++w) {
+    const uint64_t base = a.bases[w];
+    if (w == a.rank) {
+      w0[w] = __ldcg(reinterpret_cast<const unsigned int*>(base + off));
+      w1[w] = __ldcg(reinterpret_cast<const unsigned int*>(base + off + 4));
+      sc[w] = __ldcg(reinterpret_cast<const float*>(base + row + 128));
+    } else {
+      w0[w] = __ldcv(reinterpret_cast<const unsigned int*>(base + off));
+      w1[w] = __ldcv(reinterpret_cast<const unsigned int*>(base + off + 4));
+      sc[w] = __ldcv(reinterpret_cast<const float*>(base + row + 128));
+    }
+  }
+  float t[8];
+#pragma unroll
+  for (int w = 0; w < W; ++w)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t word = k < 4 ? w0[w] : w1[w];
+      const float x = __fmul_rn((float)(int8_t)(word >> (8 * (k & 3))), sc[w]);
+      t[k] = w == 0 ? x : __fadd_rn(t[k], x);
+    }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) q[k] = __float2int_rn(t[k]);
+}
+
+// The shared epilogue of one 8-column chunk from its restored INT32 sums: dequant
+// y = (f32(q) *rn A[r]) *rn W[c], then X = f16(fma(f32(f16(y)), G[lab], f32(X))).
+H3_DEV uint4 epilogue_chunk(const Args& a, const int32_t (&q)[8], int64_t r, int64_t c0,
+                            uint4 x) {
   const float s = __ldg(a.row_scale + r);
   const float4 w0 = __ldg(reinterpret_cast<const float4*>(a.weight_scale + c0));
   const float4 w1 = __ldg(reinterpret_cast<const float4*>(a.weight_scale + c0) + 1);
@@ -156,9 +201,7 @@ H3_DEV uint4 finish_chunk(const Args& a, const uint4 (&u)[W], int64_t r, int64_t
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int k = 2 * j + e;
-      const float reduced = __half2float(__float2half_rn(t[k]));
-      const int32_t restored = __float2int_rz(__fmul_rn(reduced, a.up));
-      const float y = __fmul_rn(__fmul_rn(__int2float_rn(restored), s), ws[k]);
+      const float y = __fmul_rn(__fmul_rn(__int2float_rn(q[k]), s), ws[k]);
       b[e] = __half2float(__float2half_rn(y));
     }
     const float2 xf = __half22float2(xh[j]);
@@ -167,7 +210,7 @@ H3_DEV uint4 finish_chunk(const Args& a, const uint4 (&u)[W], int64_t r, int64_t
   return x;
 }
 
-template <int W>
+template <int W, bool PACKED>
 __global__ void __launch_bounds__(THREADS) reduce_kernel(const Args a) {
   // Phase 0: this rank's partial is complete (stream order after the row GEMM);
   // announce it to every rank.
@@ -186,12 +229,18 @@ __global__ void __launch_bounds__(THREADS) reduce_kernel(const Args a) {
       const int64_t e = first + i;  // uint4 index of the chunk in [rows][width]
       const int64_t r = e / chunks;
       const int64_t c0 = (e - r * chunks) << 3;
-      uint4 u[W];
+      int32_t q[8];
+      if (PACKED) {
+        load_restore_int8<W>(a, r, c0, q);
+      } else {
+        uint4 u[W];
 #pragma unroll
-      for (int w = 0; w < W; ++w)
-        u[w] = w == a.rank ? load_received(a.bases[w], a.partial_off + e * 16)
-                           : load_peer(a.bases[w], a.partial_off + e * 16);
-      const uint4 y = finish_chunk<W>(a, u, r, c0, res[e]);
+        for (int w = 0; w < W; ++w)
+          u[w] = w == a.rank ? load_received(a.bases[w], a.partial_off + e * 16)
+                             : load_peer(a.bases[w], a.partial_off + e * 16);
+        restore_fp16<W>(a, u, q);
+      }
+      const uint4 y = epilogue_chunk(a, q, r, c0, res[e]);
       res[e] = y;
 #pragma unroll
       for (int w = 0; w < W; ++w)
@@ -241,18 +290,20 @@ __global__ void __launch_bounds__(THREADS) gather_kernel(const Args a) {
 }
 
 template <int W>
-cudaError_t launch(const Args& a, int blocks, bool gather, cudaStream_t st) {
+cudaError_t launch(const Args& a, int blocks, bool gather, bool packed, cudaStream_t st) {
   if (gather)
     gather_kernel<W><<<blocks, THREADS, 0, st>>>(a);
+  else if (packed)
+    reduce_kernel<W, true><<<blocks, THREADS, 0, st>>>(a);
   else
-    reduce_kernel<W><<<blocks, THREADS, 0, st>>>(a);
+    reduce_kernel<W, false><<<blocks, THREADS, 0, st>>>(a);
   return cudaGetLastError();
 }
 
 int run(const void* const* bases, int world, int rank, int64_t flags_off, int64_t partial_off,
         int64_t final_off, int64_t rows, int64_t width, int shift, const float* row_scale,
         const float* weight_scale, void* residual_f16, const float* gate, int64_t gate_rows,
-        const int32_t* labels, uint32_t epoch, bool gather, void* stream) {
+        const int32_t* labels, uint32_t epoch, bool gather, bool packed, void* stream) {
   if (bases == nullptr || residual_f16 == nullptr || (world != 2 && world != 4 && world != 8) ||
       rank < 0 || rank >= world || rows < 0 || width <= 0 || width % 8 || epoch == 0 ||
       flags_off < 0 || partial_off < 0 || final_off < 0 || flags_off % 16 ||
@@ -265,6 +316,7 @@ int run(const void* const* bases, int world, int rank, int64_t flags_off, int64_
     if (gate != nullptr &&
         (gate_rows < 1 || (labels == nullptr && gate_rows != 1) || !h3host::aligned(gate, 16)))
       return H3_ERR_INVALID;
+    if (packed && width % 128 != 0) return H3_ERR_INVALID;
   }
   Args a{};
   for (int w = 0; w < world; ++w) {
@@ -300,9 +352,9 @@ int run(const void* const* bases, int world, int rank, int64_t flags_off, int64_
   const int blocks = (int)std::max<int64_t>(
       1, std::min<int64_t>((items + THREADS - 1) / THREADS, (int64_t)h3host::sm_count(dev) * 8));
   cudaStream_t st = (cudaStream_t)stream;
-  cudaError_t e = world == 2 ? launch<2>(a, blocks, gather, st)
-                  : world == 4 ? launch<4>(a, blocks, gather, st)
-                               : launch<8>(a, blocks, gather, st);
+  cudaError_t e = world == 2 ? launch<2>(a, blocks, gather, packed, st)
+                  : world == 4 ? launch<4>(a, blocks, gather, packed, st)
+                               : launch<8>(a, blocks, gather, packed, st);
   return e == cudaSuccess ? H3_OK : H3_ERR_CUDA;
 }
 
@@ -317,12 +369,23 @@ extern "C" int h3_peer_reduce(const void* const* bases, int world, int rank, int
                               void* stream) {
   return h3::peer::run(bases, world, rank, flags_off, partial_off, final_off, rows, width, shift,
                        row_scale, weight_scale, residual_f16, gate, gate_rows, labels, epoch,
-                       false, stream);
+                       false, false, stream);
+}
+
+extern "C" int h3_peer_reduce_int8(const void* const* bases, int world, int rank,
+                                   int64_t flags_off, int64_t partial_off, int64_t final_off,
+                                   int64_t rows, int64_t width, const float* row_scale,
+                                   const float* weight_scale, void* residual_f16,
+                                   const float* gate, int64_t gate_rows, const int32_t* labels,
+                                   uint32_t epoch, void* stream) {
+  return h3::peer::run(bases, world, rank, flags_off, partial_off, final_off, rows, width, 0,
+                       row_scale, weight_scale, residual_f16, gate, gate_rows, labels, epoch,
+                       false, true, stream);
 }
 
 extern "C" int h3_peer_gather(const void* const* bases, int world, int rank, int64_t flags_off,
                               int64_t final_off, int64_t rows, int64_t width, void* residual_f16,
                               uint32_t epoch, void* stream) {
   return h3::peer::run(bases, world, rank, flags_off, 0, final_off, rows, width, 0, nullptr,
-                       nullptr, residual_f16, nullptr, 0, nullptr, epoch, true, stream);
+                       nullptr, residual_f16, nullptr, 0, nullptr, epoch, true, false, stream);
 }

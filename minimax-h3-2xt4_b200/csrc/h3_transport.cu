@@ -122,6 +122,81 @@ __global__ void gated_add_kernel(const void* __restrict__ branch, int branch_kin
   }
 }
 
+// ---------------------------------------------------------------------------
+// Packed INT8 transport ('int8_gather', tilelang_transport_tradeoffs.py:40-62 and
+// tilelang_transport_p2.py:28-42).  Wire format per row: for each 128-column group,
+// 128 code bytes then the 4 bytes of the fp32 scale; row pitch groups * 132 bytes.
+// ---------------------------------------------------------------------------
+// One warp per (row, group): lane l owns columns 4l..4l+3.
+__global__ void pack8_kernel(const int32_t* __restrict__ p, int64_t rows, int64_t width,
+                             uint8_t* __restrict__ out) {
+  const int64_t groups = width / 128, pitch = groups * 132;
+  const int lane = threadIdx.x & 31;
+  const int64_t total = rows * groups;
+  for (int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; t < total;
+       t += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int64_t r = t / groups, g = t - r * groups;
+    const int4 v = __ldg(reinterpret_cast<const int4*>(p + r * width + g * 128) + lane);
+    const float x[4] = {__int2float_rn(v.x), __int2float_rn(v.y), __int2float_rn(v.z),
+                        __int2float_rn(v.w)};
+    float m = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+    m = warp_max(m);
+    const float scale = fmaxf(__fmul_rn(m, f32_bits(H3_INV127_BITS)), f32_bits(0x322bcc77u));
+    const float inv = __fdiv_rn(1.0f, scale);
+    uint32_t b[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float q = fminf(127.0f, fmaxf(-127.0f, div_by_scale(x[e], scale, inv)));
+      b[e] = __float_as_uint(__fadd_rn(q, 12582912.0f));
+    }
+    uint8_t* o = out + r * pitch + g * 132;
+    reinterpret_cast<uint32_t*>(o)[lane] =
+        __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
+    if (lane == 0) *reinterpret_cast<float*>(o + 128) = scale;
+  }
+}
+
+// restored = rint(sum_w f32(q_w) *rn s_w) in rank order, then the row epilogue; 4 columns
+// (one 32-bit word of codes per rank) per thread.
+__global__ void unpack8_finish_kernel(const uint8_t* __restrict__ parts, int world,
+                                      int64_t part_stride, int64_t rows, int64_t width,
+                                      const float* __restrict__ row_scale,
+                                      const float* __restrict__ weight_scale, RowOut o) {
+  const int64_t groups = width / 128, pitch = groups * 132;
+  const int64_t quads = width / 4;
+  const int64_t total = rows * quads;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / quads;
+    const int64_t c0 = (i - r * quads) * 4;
+    const int64_t g = c0 / 128, off = r * pitch + g * 132;
+    float t[4];
+    for (int w = 0; w < world; ++w) {
+      const uint8_t* b = parts + w * part_stride + off;
+      const float s = __ldg(reinterpret_cast<const float*>(b + 128));
+      const uint32_t q = __ldg(reinterpret_cast<const uint32_t*>(b + (c0 - g * 128)));
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float x = __fmul_rn((float)(int8_t)(q >> (8 * e)), s);
+        t[e] = w == 0 ? x : __fadd_rn(t[e], x);
+      }
+    }
+    if (o.kind == H3_OUT_I32) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        reinterpret_cast<int32_t*>(o.out)[r * width + c0 + e] = __float2int_rn(t[e]);
+      continue;
+    }
+    const float a = __ldg(row_scale + r);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int32_t restored = __float2int_rn(t[e]);
+      row_store(o, r, c0 + e, width,
+                __fmul_rn(__fmul_rn(__int2float_rn(restored), a), __ldg(weight_scale + c0 + e)));
+    }
+  }
+}
+
 static int elementwise_grid(int64_t total, int dev) {
   return (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256,
                                                      (int64_t)h3host::sm_count(dev) * 32));
@@ -254,5 +329,52 @@ extern "C" int h3_gated_add(const void* branch, int branch_kind, int64_t rows, i
   if (o.err == nullptr) return H3_ERR_CUDA;
   gated_add_kernel<<<elementwise_grid(rows * width, dev), 256, 0, (cudaStream_t)stream>>>(
       branch, branch_kind, rows, width, o);
+  return h3host::check_launch();
+}
+
+extern "C" int h3_pack8(const int32_t* partial, int64_t rows, int64_t width, void* out_u8,
+                        void* stream) {
+  if (partial == nullptr || out_u8 == nullptr || rows < 0 || width <= 0 || width % 128 != 0 ||
+      !h3host::aligned(partial, 16) || !h3host::aligned(out_u8, 4))
+    return H3_ERR_INVALID;
+  if (rows == 0) return H3_OK;
+  int dev;
+  if (int s = h3host::bind_device_of(partial, &dev)) return s;
+  pack8_kernel<<<elementwise_grid(rows * (width / 128) * 32, dev), 256, 0, (cudaStream_t)stream>>>(
+      partial, rows, width, reinterpret_cast<uint8_t*>(out_u8));
+  return h3host::check_launch();
+}
+
+extern "C" int h3_unpack8_finish(const void* parts_u8, int world, int64_t part_stride,
+                                 int64_t rows, int64_t width, const float* row_scale,
+                                 const float* weight_scale, int out_kind, void* out,
+                                 void* residual_f16, const float* gate, int64_t gate_rows,
+                                 const int32_t* labels, void* stream) {
+  if (parts_u8 == nullptr || world < 1 || world > 64 || rows < 0 || width <= 0 ||
+      width % 128 != 0 || !h3host::aligned(parts_u8, 4) || part_stride % 4 != 0)
+    return H3_ERR_INVALID;
+  if (world > 1 && part_stride < rows * (width / 128) * 132) return H3_ERR_INVALID;
+  if (out_kind != H3_OUT_I32 && (row_scale == nullptr || weight_scale == nullptr))
+    return H3_ERR_INVALID;
+  if (out_kind == H3_OUT_I32) {
+    if (out == nullptr || !h3host::aligned(out, 4)) return H3_ERR_INVALID;
+  } else if (out_kind == H3_OUT_RESIDUAL) {
+    if (residual_f16 == nullptr) return H3_ERR_INVALID;
+    if (gate != nullptr && (gate_rows < 1 || (labels == nullptr && gate_rows != 1)))
+      return H3_ERR_INVALID;
+  } else if (out_kind == H3_OUT_F32 || out_kind == H3_OUT_F16) {
+    if (out == nullptr) return H3_ERR_INVALID;
+  } else {
+    return H3_ERR_INVALID;
+  }
+  if (rows == 0) return H3_OK;
+  int dev;
+  if (int s = h3host::bind_device_of(parts_u8, &dev)) return s;
+  RowOut o{out_kind, out, reinterpret_cast<__half*>(residual_f16), gate, gate_rows, labels,
+           h3host::error_word(dev)};
+  if (o.err == nullptr) return H3_ERR_CUDA;
+  unpack8_finish_kernel<<<elementwise_grid(rows * width / 4, dev), 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const uint8_t*>(parts_u8), world, part_stride, rows, width, row_scale,
+      weight_scale, o);
   return h3host::check_launch();
 }

@@ -26,6 +26,7 @@ DIV_FAST = 1
 OUT_F32 = 0
 OUT_F16 = 1
 OUT_RESIDUAL = 2
+OUT_I32 = 3
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -55,6 +56,11 @@ SIGNATURES = {
     "h3_row_reduce_finish": [_P, _I, _I64, _I64, _I64, _I, _P, _P, _I, _P, _P, _P, _I64, _P, _P],
     "h3_dequantize_i32": [_P, _I64, _I64, _P, _P, _I64, _P, _I, _P, _P],
     "h3_gated_add": [_P, _I, _I64, _I64, _P, _P, _I64, _P, _P],
+    "h3_int8_gemm_row_pack8": [_P, _P, _I64, _I64, _I64, _P, _P],
+    "h3_pack8": [_P, _I64, _I64, _P, _P],
+    "h3_unpack8_finish": [_P, _I, _I64, _I64, _I64, _P, _P, _I, _P, _P, _P, _I64, _P, _P],
+    "h3_peer_reduce_int8": [_PP, _I, _I, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _P,
+                            _U32, _P],
     "h3_peer_reduce": [_PP, _I, _I, _I64, _I64, _I64, _I64, _I64, _I, _P, _P, _P, _P, _I64, _P,
                        _U32, _P],
     "h3_peer_gather": [_PP, _I, _I, _I64, _I64, _I64, _I64, _P, _U32, _P],

@@ -108,6 +108,7 @@ def row_gated(module, value, residual, gate, segments, comm, input_act=None):
         gate = gate.contiguous()
     ws = module.weight_scale.reshape(-1)
     transport = getattr(policy, "row_transport", "rowblock")
+    payload = getattr(policy, "row_payload", "fp16")
     division = getattr(policy, "quant_division", "rn")
     scaled = policy.row_linear_backend in ("tilelang_scaled_fp16", "b200_scaled_fp16")
     if input_act == "swiglu":
@@ -118,11 +119,12 @@ def row_gated(module, value, residual, gate, segments, comm, input_act=None):
                        and not torch.is_grad_enabled() and type(value) is torch.Tensor)
         return row_linear(value, module.weight, ws, comm, mode=policy.fc2_quantizer,
                           scaled_transport=scaled, consume_input=consume, residual=residual,
-                          gate=gate, labels=labels, transport=transport, division=division)
+                          gate=gate, labels=labels, transport=transport, division=division,
+                          payload=payload)
     if value.dtype not in (torch.float16, torch.float32) or value.shape[1] != kl:
         return None
     from .row_quant import global_row_quantize
     from .swiglu_quant import _finish_quantized
     q, scale = global_row_quantize(value, comm, world, 256, None, division=division)
     return _finish_quantized(q, scale, module.weight, ws, comm, scaled, transport,
-                             residual=residual, gate=gate, labels=labels)
+                             residual=residual, gate=gate, labels=labels, payload=payload)

@@ -14,6 +14,9 @@ New B200 fields:
                   or 'allreduce' (NCCL fp16 SUM, the reference's form).  All three give
                   the same bits; 'p2p' needs a torch.distributed NCCL group and the
                   residual form of the row output, and uses 'rowblock' otherwise.
+  row_payload     'fp16' (the scaled-FP16 partials, default) or 'int8_gather' (the
+                  reference's packed INT8 group-128 payload,
+                  tilelang_transport_tradeoffs.py:40-88), with any row_transport
   quant_division  'rn' (IEEE, bit-exact with the CPU oracle) or 'fast' (__fdividef)
   fc1_swiglu_epilogue  FC1 stores the FP32 SwiGLU activation instead of fp16 [gate|up]
 """
@@ -43,6 +46,7 @@ class H3OperatorPolicy:
     dit_p0_a1_turing: bool = True
     dit_p0_c_local_rotation: bool = True
     row_transport: str = "p2p"
+    row_payload: str = "fp16"
     quant_division: str = "rn"
     fc1_swiglu_epilogue: bool = True
 
@@ -60,6 +64,8 @@ class H3OperatorPolicy:
             raise ValueError("Unknown column linear backend")
         if self.row_transport not in ("p2p", "rowblock", "allreduce"):
             raise ValueError("Unknown row transport")
+        if self.row_payload not in ("fp16", "int8_gather"):
+            raise ValueError("Unknown row payload")
         if self.quant_division not in ("rn", "fast"):
             raise ValueError("Unknown quantizer division")
 
@@ -109,14 +115,16 @@ def row_linear(module, x, fallback, comm, input_act=None):
             return quant.row_linear(x, module.weight, module.weight_scale, comm,
                                     mode=policy.fc2_quantizer,
                                     scaled_transport=policy.scaled_transport,
-                                    transport=policy.row_transport, division=division)
+                                    transport=policy.row_transport, division=division,
+                                    payload=policy.row_payload)
         _fallback("FC2 fused quantizer", str(x.device), None)
     if input_act is None and x.shape[-1] % 256 == 0 and module.convrot_groupsize == 256:
         # O projection: local ConvRot of owned groups, global row max, quantise.
         from .row_quant import global_row_quantize
         q, scale = global_row_quantize(x, comm, module.world_size, 256, None, division=division)
         out = quant._finish_quantized(q, scale, module.weight, module.weight_scale.reshape(-1),
-                                      comm, policy.scaled_transport, policy.row_transport)
+                                      comm, policy.scaled_transport, policy.row_transport,
+                                      payload=policy.row_payload)
         return out.reshape(*x.shape[:-1], module.weight.shape[0])
     args = (x, module.weight, module.weight_scale, comm, module.world_size,
             module.convrot_groupsize, input_act)

@@ -296,6 +296,75 @@ def row_reduce_finish(parts, shift, row_scale, weight_scale, out_dtype=torch.flo
     return out
 
 
+# ----------------------------------------------------------------------------
+# packed INT8 transport ('int8_gather')
+# ----------------------------------------------------------------------------
+def pack8_pitch(width: int) -> int:
+    """Bytes per row of a packed payload: 128 codes + 4 scale bytes per 128 columns."""
+    if width % 128:
+        raise ValueError("Whole group128 outputs required")
+    return width // 128 * 132
+
+
+def int8_gemm_row_pack8(q, w, out: torch.Tensor | None = None) -> torch.Tensor:
+    """INT8 GEMM with the group-128 INT8 pack fused: uint8 [M, N/128*132]."""
+    q = _need(q, torch.int8, "q", 2)
+    w = _need(w, torch.int8, "weight", 2)
+    M, K = q.shape
+    if w.shape[1] != K:
+        raise ValueError("Input and weight inner dimensions must match")
+    pitch = pack8_pitch(w.shape[0])
+    if out is None:
+        out = torch.empty((M, pitch), dtype=torch.uint8, device=q.device)
+    elif (out.dtype != torch.uint8 or tuple(out.shape) != (M, pitch) or not out.is_contiguous()
+          or out.device != q.device):
+        raise ValueError("out must be a contiguous uint8 [M, N/128*132] tensor on q's device")
+    N.call("h3_int8_gemm_row_pack8", q.data_ptr(), w.data_ptr(), M, w.shape[0], K,
+           out.data_ptr(), _stream(q))
+    return out
+
+
+def pack8(partial) -> torch.Tensor:
+    """Group-128 INT8 pack of an INT32 partial (pack_int8): uint8 [rows, width/128*132]."""
+    p = _need(partial, torch.int32, "partial", 2)
+    rows, width = p.shape
+    out = torch.empty((rows, pack8_pitch(width)), dtype=torch.uint8, device=p.device)
+    N.call("h3_pack8", p.data_ptr(), rows, width, out.data_ptr(), _stream(p))
+    return out
+
+
+def unpack8_finish(parts, width: int, row_scale=None, weight_scale=None, out_dtype=torch.float32,
+                   residual=None, gate=None, labels=None):
+    """parts: uint8 [world, rows, pitch] (or [rows, pitch]).  Rank-order reconstruction,
+    then the row epilogue; out_dtype torch.int32 returns the restored sums."""
+    parts = _need(parts, torch.uint8, "parts")
+    if parts.ndim == 2:
+        parts = parts.unsqueeze(0)
+    world, M, pitch = parts.shape
+    if pitch != pack8_pitch(width):
+        raise ValueError("payload pitch does not match the width")
+    if out_dtype == torch.int32 and residual is None:
+        out = torch.empty((M, width), dtype=torch.int32, device=parts.device)
+        N.call("h3_unpack8_finish", parts.data_ptr(), world, M * pitch, M, width, None, None,
+               N.OUT_I32, out.data_ptr(), None, None, 0, None, _stream(parts))
+        return out
+    a = _vec(row_scale, M, "row_scale")
+    ws = _vec(weight_scale, width, "weight_scale")
+    if residual is not None:
+        if not residual.is_contiguous():
+            raise ValueError("residual must be contiguous (updated in place)")
+        res, g, grows, lab = _gate_args(residual, gate, labels, M, width)
+        N.call("h3_unpack8_finish", parts.data_ptr(), world, M * pitch, M, width, a.data_ptr(),
+               ws.data_ptr(), N.OUT_RESIDUAL, None, res.data_ptr(), _ptr(g), grows, _ptr(lab),
+               _stream(parts))
+        return residual
+    kind = {torch.float32: N.OUT_F32, torch.float16: N.OUT_F16}[out_dtype]
+    out = torch.empty((M, width), dtype=out_dtype, device=parts.device)
+    N.call("h3_unpack8_finish", parts.data_ptr(), world, M * pitch, M, width, a.data_ptr(),
+           ws.data_ptr(), kind, out.data_ptr(), None, None, 0, None, _stream(parts))
+    return out
+
+
 def dequantize_i32(acc, row_scale, weight_scale, out_dtype=torch.float32, bias=None):
     """parallel_int8.dequantize order: ((acc * a) * w) + bias."""
     acc = _need(acc, torch.int32, "accumulator", 2)
@@ -342,6 +411,22 @@ def peer_reduce(bases, world: int, rank: int, flags_off: int, partial_off: int, 
     N.call("h3_peer_reduce", arr, world, rank, flags_off, partial_off, final_off, rows, width,
            int(shift), a.data_ptr(), ws.data_ptr(), res.data_ptr(), _ptr(g), grows, _ptr(lab),
            int(epoch), _stream(res))
+    return residual
+
+
+def peer_reduce_int8(bases, world: int, rank: int, flags_off: int, partial_off: int,
+                     final_off: int, rows: int, width: int, row_scale, weight_scale, residual,
+                     gate=None, labels=None, epoch: int = 1):
+    """peer_reduce for packed INT8 payloads (h3_peer_reduce_int8)."""
+    a = _vec(row_scale, rows, "row_scale")
+    ws = _vec(weight_scale, width, "weight_scale")
+    if not residual.is_contiguous():
+        raise ValueError("residual must be contiguous (updated in place)")
+    res, g, grows, lab = _gate_args(residual, gate, labels, rows, width)
+    arr = (ctypes.c_void_p * world)(*bases)
+    N.call("h3_peer_reduce_int8", arr, world, rank, flags_off, partial_off, final_off, rows, width,
+           a.data_ptr(), ws.data_ptr(), res.data_ptr(), _ptr(g), grows, _ptr(lab), int(epoch),
+           _stream(res))
     return residual
 
 

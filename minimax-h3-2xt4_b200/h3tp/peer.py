@@ -81,14 +81,24 @@ class PeerWorkspace:
         return self.buf[self.partial_off:self.partial_off + 2 * n].view(torch.float16).view(
             rows, self.width)
 
+    def partial_u8(self, rows: int) -> torch.Tensor:
+        """The same area as a packed INT8 payload, uint8 [rows, width/128*132]."""
+        pitch = ops.pack8_pitch(self.width)
+        return self.buf[self.partial_off:self.partial_off + rows * pitch].view(rows, pitch)
+
     def reduce_and_gather(self, rows: int, shift: int, row_scale, weight_scale, residual,
-                          gate=None, labels=None):
-        """Sums the partials every rank wrote into partial() into `residual` (fp16
-        [rows, width], updated in place on every rank)."""
+                          gate=None, labels=None, packed: bool = False):
+        """Sums the partials every rank wrote into partial() (or, packed, partial_u8())
+        into `residual` (fp16 [rows, width], updated in place on every rank)."""
         self.epoch += 1
-        ops.peer_reduce(self.bases, self.world, self.rank, 0, self.partial_off, self.final_off,
-                        rows, self.width, shift, row_scale, weight_scale, residual, gate, labels,
-                        self.epoch)
+        if packed:
+            ops.peer_reduce_int8(self.bases, self.world, self.rank, 0, self.partial_off,
+                                 self.final_off, rows, self.width, row_scale, weight_scale,
+                                 residual, gate, labels, self.epoch)
+        else:
+            ops.peer_reduce(self.bases, self.world, self.rank, 0, self.partial_off,
+                            self.final_off, rows, self.width, shift, row_scale, weight_scale,
+                            residual, gate, labels, self.epoch)
         ops.peer_gather(self.bases, self.world, self.rank, 0, self.final_off, rows, self.width,
                         residual, self.epoch)
         return residual

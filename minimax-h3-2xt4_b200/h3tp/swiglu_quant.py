@@ -96,7 +96,7 @@ def supported(x, weight, weight_scale, world_size, groupsize) -> bool:
 
 def _finish_quantized(q, scale, weight, weight_scale, comm, scaled_transport=True,
                       transport="rowblock", *, residual=None, gate=None, labels=None,
-                      out_dtype=torch.float32, finish_fn=None):
+                      out_dtype=torch.float32, finish_fn=None, payload="fp16"):
     """GEMM -> (transport) -> epilogue of the quantised row activation (shared by FC2
     and the O projection; tilelang_swiglu_quant.py:116-127, tilelang_transport_p2.py:
     240-249).  Returns [M, N] in out_dtype, or the residual updated in place."""
@@ -109,6 +109,12 @@ def _finish_quantized(q, scale, weight, weight_scale, comm, scaled_transport=Tru
                 return ops.int8_gemm_row_dequant(q, weight, scale, weight_scale,
                                                  residual=residual, gate=gate, labels=labels)
             return ops.int8_gemm_row_dequant(q, weight, scale, weight_scale, out_dtype)
+    if scaled_transport and payload == "int8_gather":
+        if finish_fn is not None:
+            raise ValueError("The fused row-gate callback takes the fp16 payload")
+        return T.int8_row_exchange(q, weight, scale, weight_scale, comm, transport,
+                                   out_dtype=out_dtype, residual=residual, gate=gate,
+                                   labels=labels)
     if scaled_transport:
         shift = T.shift_for(local_k, world)
         if (transport == "p2p" and residual is not None and finish_fn is None
@@ -145,7 +151,8 @@ def _finish_quantized(q, scale, weight, weight_scale, comm, scaled_transport=Tru
 
 def row_linear(x, weight, weight_scale, comm, *, mode="fused_stored", scaled_transport=True,
                finish_fn=None, consume_input=False, p0_b=False, residual=None, gate=None,
-               labels=None, transport="rowblock", division="rn", out_dtype=torch.float32):
+               labels=None, transport="rowblock", division="rn", out_dtype=torch.float32,
+               payload="fp16"):
     """FC2 row linear (tilelang_swiglu_quant.py:108-128).
 
     Returns FP32 [..., N] (the caller adds LoRA, then stores once), or with
@@ -162,7 +169,7 @@ def row_linear(x, weight, weight_scale, comm, *, mode="fused_stored", scaled_tra
     del x
     out = _finish_quantized(q, scale, weight, weight_scale.reshape(-1), comm, scaled_transport,
                             transport, residual=residual, gate=gate, labels=labels,
-                            out_dtype=out_dtype, finish_fn=finish_fn)
+                            out_dtype=out_dtype, finish_fn=finish_fn, payload=payload)
     if residual is not None or finish_fn is not None:
         return out
     return out.reshape(*shape[:-1], weight.shape[0])

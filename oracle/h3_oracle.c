@@ -358,6 +358,63 @@ EXPORT void h3o_gated_add(const float* y, int64_t rows, int64_t width, uint16_t*
       row_out(2, NULL, residual, gate, labels, r, c, width, y[r * width + c]);
 }
 
+/* ---------------------------------------------------------------------------
+ * Packed INT8 transport ('int8_gather'): tilelang_transport_tradeoffs.py:40-62 (pack),
+ * tilelang_transport_p2.py:28-42 (reconstruction inside the epilogue), and its torch
+ * statement in benchmarks/tp2_tradeoffs.py:73-78.
+ * Wire format per row: for each 128-column group, 128 code bytes (two's complement)
+ * then the 4 bytes of the fp32 scale (little endian); row pitch = groups * 132.
+ * ------------------------------------------------------------------------- */
+static inline int32_t rint_i32(float v) {
+  if (v != v) return 0;
+  const float r = rintf(v); /* round half to even */
+  if (r >= 2147483648.0f) return INT32_MAX;
+  if (r <= -2147483648.0f) return INT32_MIN;
+  return (int32_t)r;
+}
+
+/* scale = max(max_i |f32(P_i)| *rn f32(1/127), f32(1e-8));
+ * q_i = clamp(rint(f32(P_i) /rn scale), -127, 127). */
+EXPORT void h3o_pack8(const int32_t* P, int64_t rows, int64_t width, uint8_t* out) {
+  const int64_t groups = width / 128, pitch = groups * 132;
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t g = 0; g < groups; ++g) {
+      const int32_t* p = P + r * width + g * 128;
+      uint8_t* o = out + r * pitch + g * 132;
+      float m = 0.0f;
+      for (int i = 0; i < 128; ++i) m = fmaxf(m, fabsf((float)p[i]));
+      const float s = fmaxf(m * bits2f(0x3c010204u), bits2f(0x322bcc77u));
+      for (int i = 0; i < 128; ++i) {
+        const float q = fminf(127.0f, fmaxf(-127.0f, rintf((float)p[i] / s)));
+        o[i] = (uint8_t)(int8_t)(int)q;
+      }
+      memcpy(o + 128, &s, 4);
+    }
+}
+
+/* restored = rint( sum_w f32(q_w) *rn s_w ), the sum in rank order with RN additions
+ * (the reference's two-rank form: x0 +rn x1). parts: world payloads, part_stride bytes
+ * apart. */
+EXPORT void h3o_unpack8_restore(const uint8_t* parts, int world, int64_t part_stride,
+                                int64_t rows, int64_t width, int32_t* out) {
+  const int64_t groups = width / 128, pitch = groups * 132;
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t c = 0; c < width; ++c) {
+      const int64_t g = c / 128, i = c % 128;
+      float total = 0.0f;
+      for (int w = 0; w < world; ++w) {
+        const uint8_t* o = parts + w * part_stride + r * pitch + g * 132;
+        float s;
+        memcpy(&s, o + 128, 4);
+        const float x = (float)(int8_t)o[i] * s;
+        total = w == 0 ? x : total + x;
+      }
+      out[r * width + c] = rint_i32(total);
+    }
+}
+
 /* shift_for of tilelang_transport_tradeoffs.py:20-22 on the full reduction length. */
 EXPORT int h3o_transport_shift(int64_t full_k) {
   if (full_k <= 0) return 0;

@@ -50,6 +50,8 @@ def lib() -> ctypes.CDLL:
         L.h3o_dequantize_i32.argtypes = [P, I64, I64, P, P, I64, P, I, P, P, P, P]
         L.h3o_gated_add.argtypes = [P, I64, I64, P, P, P]
         L.h3o_transport_shift.argtypes = [I64]
+        L.h3o_pack8.argtypes = [P, I64, I64, P]
+        L.h3o_unpack8_restore.argtypes = [P, I, I64, I64, I64, P]
         L.h3o_transport_shift.restype = I
         _LIB = L
     return _LIB
@@ -179,6 +181,28 @@ def fp16_decode(Y, shift: int) -> np.ndarray:
     P = np.empty(Y.shape, np.int32)
     lib().h3o_fp16_decode(_p(Y), Y.size, int(shift), _p(P))
     return P
+
+
+def pack8(P) -> np.ndarray:
+    """'int8_gather' pack of an INT32 partial (tilelang_transport_tradeoffs.py:40-62):
+    uint8 [rows, groups * 132], per group 128 codes then the fp32 scale's bytes."""
+    P = _c(P, np.int32)
+    rows, width = P.shape
+    assert width % 128 == 0
+    out = np.empty((rows, width // 128 * 132), np.uint8)
+    lib().h3o_pack8(_p(P), rows, width, _p(out))
+    return out
+
+
+def unpack8_restore(parts, width: int) -> np.ndarray:
+    """Rank-order reconstruction of packed payloads [world, rows, groups * 132] into the
+    restored INT32 sum (tilelang_transport_p2.py:28-42, tp2_tradeoffs.py:73-78)."""
+    parts = _c(parts, np.uint8)
+    world, rows, pitch = parts.shape
+    assert pitch == width // 128 * 132
+    out = np.empty((rows, width), np.int32)
+    lib().h3o_unpack8_restore(_p(parts), world, rows * pitch, rows, width, _p(out))
+    return out
 
 
 OUT = {"f32": 0, "f16": 1, "residual": 2}

@@ -14,7 +14,8 @@ functions whose CPU path never touches it are called:
                                    module source because the module's own imports
                                    name retired files
   benchmarks/test_tp2_p2_epilogue.py  its five known-answer patterns (:15-38), built
-                                   here on the CPU with the same seed and sizes
+                                   here on the CPU with the same seed and sizes, for
+                                   both of its schemes ('fp16' and 'int8_gather')
   patches/h3_tensor_flow.py        fold_linear (:82-103)
   patches/tilelang_dit_fusion.py   segment_key (:93-100)
 
@@ -113,6 +114,10 @@ def make(root: Path) -> None:
         out[f"kat_{pattern}_w"] = wv.numpy()
         out[f"kat_{pattern}_reduced_i32"] = independent.numpy()
         out[f"kat_{pattern}_expected"] = expected.numpy()
+        # the packed INT8 scheme of the same test (test_tp2_p2_epilogue.py:27-35)
+        restored8 = transport_reference(parts, "int8_gather", k)
+        out[f"kat_{pattern}_int8_restored"] = restored8.numpy()
+        out[f"kat_{pattern}_int8_expected"] = ((restored8.float() * a) * wv).numpy()
     out["kat_k"] = np.array([k], np.int64)
 
     # --- row-order contract (test_fp16_fc2_experiment.py:10-30) -------------------------

@@ -123,6 +123,35 @@ def dequantize_i32(acc, row_scale, weight_scale, out_dtype=torch.float32, bias=N
                                bias=None if bias is None else _n(bias), out=_F[out_dtype]))
 
 
+def int8_gemm_row_pack8(q, w, out=None):
+    r = _t(O.pack8(O.int8_gemm(_n(q), _n(w))))
+    if out is not None:
+        out.copy_(r)
+        return out
+    return r
+
+
+def pack8(partial):
+    return _t(O.pack8(_n(partial)))
+
+
+def unpack8_finish(parts, width, row_scale=None, weight_scale=None, out_dtype=torch.float32,
+                   residual=None, gate=None, labels=None):
+    p = _n(parts)
+    if p.ndim == 2:
+        p = p[None]
+    restored = O.unpack8_restore(p, width)
+    if out_dtype == torch.int32 and residual is None:
+        return _t(restored)
+    if residual is not None:
+        res = _n(residual).copy()
+        O.dequantize_i32(restored, _n(row_scale), _n(weight_scale), out="residual", residual=res,
+                         gate=None if gate is None else _n(gate),
+                         labels=None if labels is None else _n(labels))
+        return _residual_out(residual, res)
+    return _t(O.dequantize_i32(restored, _n(row_scale), _n(weight_scale), out=_F[out_dtype]))
+
+
 def gated_add(residual, branch, gate=None, labels=None):
     res = _n(residual).copy()
     O.gated_add(_n(branch).astype(np.float32), res, None if gate is None else _n(gate),
@@ -134,7 +163,7 @@ NAMES = ["transport_shift", "column_quantize", "int8_gemm_i32", "int8_gemm_colum
          "int8_gemm_swiglu", "swiglu_rotate_max", "swiglu_rotate_quantize",
          "swiglu_rotate_quantize_local", "row_quantize", "int8_gemm_row_encode",
          "int8_gemm_row_dequant", "fp16_encode", "fp16_decode", "row_reduce_finish",
-         "dequantize_i32", "gated_add"]
+         "dequantize_i32", "gated_add", "int8_gemm_row_pack8", "pack8", "unpack8_finish"]
 
 
 def install():

@@ -8,6 +8,8 @@ every output bit with the oracle's restatement of the reference arithmetic:
 Shapes include ragged M/N tails, K at the 16-byte minimum and widths that are single
 or many ConvRot groups.
 """
+from pathlib import Path
+
 import numpy as np
 import pytest
 import torch
@@ -393,6 +395,64 @@ def test_gemm_row_dequant_bit_exact(cuda_device, oracle, out):
 # ----------------------------------------------------------------------------
 # transport codec and reduction epilogue
 # ----------------------------------------------------------------------------
+# ----------------------------------------------------------------------------
+# packed INT8 transport ('int8_gather')
+# ----------------------------------------------------------------------------
+@pytest.mark.parametrize("world,rows,width", [(1, 5, 128), (2, 33, 384), (4, 17, 3072)])
+def test_pack8_unpack8_bit_exact(cuda_device, oracle, world, rows, width):
+    from h3tp import ops
+    rng = np.random.default_rng(world * 7 + rows)
+    parts = rng.integers(-2 ** 27, 2 ** 27, size=(world, rows, width)).astype(np.int32)
+    parts[0, 0, :128] = 0                      # an all-zero group: the 1e-8 scale floor
+    parts[-1, -1, 5] = 2 ** 31 - 1             # extremes
+    parts[-1, -1, 6] = -2 ** 31
+    packed = np.stack([oracle.pack8(p) for p in parts])
+    got = torch.stack([ops.pack8(_t(p, cuda_device)) for p in parts])
+    _bits_equal(_np(got), packed)
+    restored = oracle.unpack8_restore(packed, width)
+    _bits_equal(_np(ops.unpack8_finish(got, width, out_dtype=torch.int32)), restored)
+    a = rng.uniform(1e-6, 1e-4, rows).astype(np.float32)
+    w = rng.uniform(1e-4, 1e-3, width).astype(np.float32)
+    for out, dt in (("f32", torch.float32), ("f16", torch.float16)):
+        y = ops.unpack8_finish(got, width, _t(a, cuda_device), _t(w, cuda_device), dt)
+        _bits_equal(_np(y), oracle.dequantize_i32(restored, a, w, out=out))
+    X = rng.standard_normal((rows, width)).astype(np.float16)
+    G = rng.standard_normal((3, width)).astype(np.float32)
+    lab = rng.integers(0, 3, rows).astype(np.int32)
+    ref = X.copy()
+    oracle.dequantize_i32(restored, a, w, out="residual", residual=ref, gate=G, labels=lab)
+    Xd = _t(X, cuda_device)
+    ops.unpack8_finish(got, width, _t(a, cuda_device), _t(w, cuda_device), residual=Xd,
+                       gate=_t(G, cuda_device), labels=_t(lab, cuda_device))
+    _bits_equal(_np(Xd), ref)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 128, 256), (77, 384, 1024), (300, 3072, 2048)])
+def test_gemm_row_pack8_bit_exact(cuda_device, oracle, M, N, K):
+    from h3tp import ops
+    rng = np.random.default_rng(M + N)
+    A, W = _operands(rng, M, N, K)
+    got = ops.int8_gemm_row_pack8(_t(A, cuda_device), _t(W, cuda_device))
+    _bits_equal(_np(got), oracle.pack8(oracle.int8_gemm(A, W)))
+
+
+@pytest.mark.parametrize("pattern", ["random", "zero", "bounds", "cancellation", "ties_outliers"])
+def test_packed_known_answers_on_gpu(cuda_device, pattern):
+    """The reference's 'int8_gather' known-answer patterns (test_tp2_p2_epilogue.py:15-38,
+    outputs of its own transport_reference stored in tests/golden) through the GPU pack,
+    reconstruction and FP32 dequant."""
+    from h3tp import ops
+    G = np.load(Path(__file__).parent / "golden" / "reference_golden.npz")
+    parts = G[f"kat_{pattern}_parts"]
+    a, w = G[f"kat_{pattern}_a"], G[f"kat_{pattern}_w"]
+    packed = torch.stack([ops.pack8(_t(p, cuda_device)) for p in parts])
+    width = parts.shape[2]
+    _bits_equal(_np(ops.unpack8_finish(packed, width, out_dtype=torch.int32)),
+                G[f"kat_{pattern}_int8_restored"])
+    y = ops.unpack8_finish(packed, width, _t(a, cuda_device), _t(w, cuda_device))
+    _bits_equal(_np(y), G[f"kat_{pattern}_int8_expected"])
+
+
 def test_fp16_codec_bit_exact(cuda_device, oracle):
     from h3tp import ops
     rng = np.random.default_rng(744)

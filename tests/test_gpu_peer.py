@@ -86,6 +86,52 @@ def test_peer_transport_bit_exact(cuda_device, oracle, world, rows, width, k):
     assert _native.device_error(dev.index or 0) == 0
 
 
+@pytest.mark.parametrize("world,rows,width,k", [(2, 130, 512, 512), (8, 99, 1024, 256)])
+def test_peer_transport_packed_int8_bit_exact(cuda_device, oracle, world, rows, width, k):
+    """The same exchange with the packed INT8 payload ('int8_gather'): the row GEMM packs
+    in its epilogue, h3_peer_reduce_int8 reconstructs in rank order."""
+    from h3tp import _native, ops
+    rng = np.random.default_rng(world + 100)
+    qs = [rng.integers(-128, 128, size=(rows, k), dtype=np.int8) for _ in range(world)]
+    ws = [rng.integers(-127, 128, size=(width, k), dtype=np.int8) for _ in range(world)]
+    packed = np.stack([oracle.pack8(oracle.int8_gemm(q, w)) for q, w in zip(qs, ws)])
+    restored = oracle.unpack8_restore(packed, width)
+    a = rng.uniform(1e-6, 1e-4, size=rows).astype(np.float32)
+    s = rng.uniform(1e-5, 1e-4, size=width).astype(np.float32)
+    X = rng.standard_normal((rows, width)).astype(np.float16)
+    G = rng.standard_normal((3, width)).astype(np.float32)
+    labels = rng.integers(0, 3, size=rows).astype(np.int32)
+    ref = X.copy()
+    oracle.dequantize_i32(restored, a, s, out="residual", residual=ref, gate=G, labels=labels)
+
+    dev = cuda_device
+    bufs, poff, foff = _buffers(dev, world, rows, width)
+    bases = [b.data_ptr() for b in bufs]
+    pitch = ops.pack8_pitch(width)
+    A, S = torch.from_numpy(a).to(dev), torch.from_numpy(s).to(dev)
+    Gd, L = torch.from_numpy(G).to(dev), torch.from_numpy(labels).to(dev)
+    res = [torch.from_numpy(X.copy()).to(dev) for _ in range(world)]
+    for r in range(world):
+        part = bufs[r][poff:poff + rows * pitch].view(rows, pitch)
+        ops.int8_gemm_row_pack8(torch.from_numpy(qs[r]).to(dev), torch.from_numpy(ws[r]).to(dev),
+                                out=part)
+    torch.cuda.synchronize()
+    for r in range(world):
+        got = bufs[r][poff:poff + rows * pitch].view(rows, pitch).cpu().numpy()
+        assert np.array_equal(got, packed[r]), r
+    for b in bufs:
+        _set(b, READY, range(world), 1)
+    for r in range(world):
+        ops.peer_reduce_int8(bases, world, r, 0, poff, foff, rows, width, A, S, res[r], Gd, L, 1)
+    for r in range(world):
+        ops.peer_gather(bases, world, r, 0, foff, rows, width, res[r], 1)
+    torch.cuda.synchronize()
+    for r in range(world):
+        got = res[r].cpu().numpy()
+        assert np.array_equal(got.view(np.uint16), ref.view(np.uint16)), f"rank {r}"
+    assert _native.device_error(dev.index or 0) == 0
+
+
 def test_peer_wait_gives_up_with_timeout_status(cuda_device):
     """Rank 1 never signals: the reduce gives up after its bounded wait, records
     H3_ERR_TIMEOUT, publishes no done flag, and the gather gives up too."""

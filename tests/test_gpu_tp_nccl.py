@@ -36,7 +36,7 @@ def _weights():
     return h, X, w1, s1, w2, s2, G, segments
 
 
-def _rank(rank, world, port, outdir, transport):
+def _rank(rank, world, port, outdir, transport, payload):
     for p in (str(ROOT), str(ROOT / "minimax-h3-2xt4_b200")):
         sys.path.insert(0, p)
     try:
@@ -52,7 +52,7 @@ def _rank(rank, world, port, outdir, transport):
         from h3tp.tp_dit import TPDiTMLPINT8
         h, X, w1, s1, w2, s2, G, segments = _weights()
         mlp = TPDiTMLPINT8(HIDDEN, FFN, rank, world, device=dev, comm=dist,
-                           policy=H3OperatorPolicy(row_transport=transport))
+                           policy=H3OperatorPolicy(row_transport=transport, row_payload=payload))
         mlp.fc1.load_shard_from_full(torch.from_numpy(w1), torch.from_numpy(s1))
         mlp.fc2.load_shard_from_full(torch.from_numpy(w2), torch.from_numpy(s2))
         from h3tp import _native, peer
@@ -82,15 +82,18 @@ def _port():
     return p
 
 
-@pytest.mark.parametrize("transport", ["p2p", "rowblock", "allreduce"])
-def test_mlp_block_over_nccl_matches_oracle(cuda_device, oracle, tmp_path, transport):
+@pytest.mark.parametrize("transport,payload", [("p2p", "fp16"), ("rowblock", "fp16"),
+                                               ("allreduce", "fp16"), ("p2p", "int8_gather"),
+                                               ("allreduce", "int8_gather")])
+def test_mlp_block_over_nccl_matches_oracle(cuda_device, oracle, tmp_path, transport, payload):
     ngpu = torch.cuda.device_count()
     if ngpu < 2:
         pytest.skip("single-GPU box: multi-rank NCCL path not exercised here")
     world = 8 if ngpu >= 8 else (4 if ngpu >= 4 else 2)
-    if transport == "allreduce" and world != 2:
+    if transport == "allreduce" and payload == "fp16" and world != 2:
         world = 2  # NCCL's fp16 SUM is one RN addition only at two ranks
-    mp.spawn(_rank, args=(world, _port(), str(tmp_path), transport), nprocs=world, join=True)
+    mp.spawn(_rank, args=(world, _port(), str(tmp_path), transport, payload), nprocs=world,
+             join=True)
     h, X, w1, s1, w2, s2, G, segments = _weights()
     labels = np.zeros(M, np.int32)
     for a, b, r in segments:
@@ -103,8 +106,17 @@ def test_mlp_block_over_nccl_matches_oracle(cuda_device, oracle, tmp_path, trans
         acts.append(oracle.swiglu_epilogue(oracle.int8_gemm(q, w1r), a, s1r.ravel()))
         w2s.append(np.ascontiguousarray(w2[:, r * kl:(r + 1) * kl]))
     ref = X.copy()
-    oracle.fc2_fused_stored(acts, w2s, s2.ravel(), out="residual", residual=ref, gate=G,
-                            labels=labels, kind="act_f32")
+    if payload == "fp16":
+        oracle.fc2_fused_stored(acts, w2s, s2.ravel(), out="residual", residual=ref, gate=G,
+                                labels=labels, kind="act_f32")
+    else:  # group-128 INT8 payloads, rank-order reconstruction
+        rots = [oracle.fc2_rotate(a, "act_f32") for a in acts]
+        gmax = np.max(np.stack([m for _, m in rots]), 0)
+        qs = [oracle.row_quantize(R, gmax) for R, _ in rots]
+        packed = np.stack([oracle.pack8(oracle.int8_gemm(q, w)) for (q, _), w in zip(qs, w2s)])
+        restored = oracle.unpack8_restore(packed, HIDDEN)
+        oracle.dequantize_i32(restored, qs[0][1], s2.ravel(), out="residual", residual=ref,
+                              gate=G, labels=labels)
     for r in range(world):
         for call in range(2):
             got = np.load(tmp_path / f"r{r}_{call}.npy")

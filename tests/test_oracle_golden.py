@@ -66,6 +66,19 @@ def test_scaled_fp16_transport_known_answers(oracle, pattern):
     _eq(oracle.row_reduce_finish(enc, shift, a, w, out="f32"), G[f"kat_{pattern}_expected"])
 
 
+@pytest.mark.parametrize("pattern", ["random", "zero", "bounds", "cancellation", "ties_outliers"])
+def test_packed_int8_transport_known_answers(oracle, pattern):
+    """The 'int8_gather' scheme of the same test (test_tp2_p2_epilogue.py:27-35): per-rank
+    group-128 pack, rank-order reconstruction, FP32 dequant, bitwise equal to the
+    reference's transport_reference(parts, 'int8_gather') + eager dequant."""
+    parts = G[f"kat_{pattern}_parts"]
+    a, w = G[f"kat_{pattern}_a"], G[f"kat_{pattern}_w"]
+    packed = np.stack([oracle.pack8(p) for p in parts])
+    restored = oracle.unpack8_restore(packed, parts.shape[2])
+    _eq(restored, G[f"kat_{pattern}_int8_restored"])
+    _eq(oracle.dequantize_i32(restored, a, w, out="f32"), G[f"kat_{pattern}_int8_expected"])
+
+
 def test_row_order_contract(oracle):
     """INT32 partial SUM, then f32 * scale * ws, then FP32 LoRA, then one fp16 store
     (benchmarks/test_fp16_fc2_experiment.py:10-30)."""

@@ -47,6 +47,23 @@ def test_fc2_allreduce_transport_tp2(oracle, tmp_path):
         assert np.array_equal(np.load(tmp_path / f"r{r}.npy").view(np.uint16), ref.view(np.uint16))
 
 
+@pytest.mark.parametrize("world,transport", [(2, "allreduce"), (2, "rowblock"), (4, "rowblock")])
+def test_fc2_packed_int8_payload(oracle, tmp_path, world, transport):
+    """The 'int8_gather' payload: GEMM + group-128 pack per rank, exchange, rank-order
+    reconstruction, FP32 dequant and gated residual."""
+    _run(tp_worker.fc2_case, world, tmp_path, "fused_recompute", transport, True, "int8_gather")
+    xs, wr, ws, X, G, labels = tp_worker.problem(world, N=256)
+    rots = [oracle.fc2_rotate(x) for x in xs]
+    gmax = np.max(np.stack([m for _, m in rots]), 0)
+    qs = [oracle.row_quantize(R, gmax) for R, _ in rots]
+    packed = np.stack([oracle.pack8(oracle.int8_gemm(q, w)) for (q, _), w in zip(qs, wr)])
+    restored = oracle.unpack8_restore(packed, 256)
+    ref = X.copy()
+    oracle.dequantize_i32(restored, qs[0][1], ws, out="residual", residual=ref, gate=G, labels=labels)
+    for r in range(world):
+        assert np.array_equal(np.load(tmp_path / f"r{r}.npy").view(np.uint16), ref.view(np.uint16))
+
+
 def test_fc2_int32_sum_route(oracle, tmp_path):
     """scaled_transport=False: exact INT32 SUM, then ((acc*a)*w), then the gated add."""
     _run(tp_worker.fc2_case, 2, tmp_path, "fused_recompute", "rowblock", False)

@@ -42,17 +42,18 @@ def problem(world, M=37, kl=512, N=96, seed=5):
     return xs, wr, ws, X, G, labels
 
 
-def fc2_case(rank, world, port, outdir, mode, transport, scaled):
+def fc2_case(rank, world, port, outdir, mode, transport, scaled, payload="fp16"):
     import torch
     try:
         dist = _init(rank, world, port)
         from h3tp import swiglu_quant
-        xs, wr, ws, X, G, labels = problem(world)
+        xs, wr, ws, X, G, labels = problem(world, N=256 if payload == "int8_gather" else 96)
         res = torch.from_numpy(X.copy())
         out = swiglu_quant.row_linear(torch.from_numpy(xs[rank]), torch.from_numpy(wr[rank]),
                                       torch.from_numpy(ws), dist, mode=mode, scaled_transport=scaled,
                                       residual=res, gate=torch.from_numpy(G),
-                                      labels=torch.from_numpy(labels), transport=transport)
+                                      labels=torch.from_numpy(labels), transport=transport,
+                                      payload=payload)
         assert out.data_ptr() == res.data_ptr()
         np.save(os.path.join(outdir, f"r{rank}.npy"), res.numpy())
         dist.barrier()
