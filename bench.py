@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--ffn", type=int, default=8192)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--sweep", action="store_true",
+                    help="BASELINE config 5 shape sweep on one GPU: one JSON line per point")
     ap.add_argument("--payload", choices=["fp16", "int8_gather"], default="fp16",
                     help="row partial payload at TP > 1 (scaled fp16, or the packed INT8 scheme)")
     return ap.parse_args()
@@ -468,10 +470,57 @@ def run_ours(args):
     return 0
 
 
+def run_sweep(args):
+    """M x (K, N) through the column linear (rotation + row quant +
+    GEMM + ordered fp16 epilogue) and the TP1 row linear (post-SwiGLU fp16 input:
+    ConvRot + row quant + GEMM + FP32 dequant), TOPS and fraction of the INT8 estimate.
+    The (5120, 13824) point is the TE (Qwen3-VL) MLP shape."""
+    import torch
+    from h3tp import swiglu_quant as sq
+    from h3tp.dit_column_linear import column_linear
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peak = 2.0 * peaks()["bf16"]
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        ts = []
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    with torch.no_grad():
+        for K, N in ((3072, 3072), (3072, 16384), (8192, 3072), (5120, 13824)):
+            w = torch.randint(-127, 128, (N, K), generator=g, device=dev, dtype=torch.int8)
+            s = torch.rand((N, 1), generator=g, device=dev) * 9e-3 + 1e-3
+            for M in (256, 1024, 4096, 16384, 65536):
+                x = torch.randn((M, K), generator=g, device=dev).half()
+                for variant in ("column", "row"):
+                    if variant == "column":
+                        ms = timed(lambda: column_linear(x, w, s))
+                    else:
+                        ms = timed(lambda: sq.row_linear(x, w, s, None, mode="fused_recompute"))
+                    tops = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+                    print(json.dumps({"sweep": variant, "M": M, "K": K, "N": N,
+                                      "ms": round(ms, 4), "tops": round(tops, 2),
+                                      "frac_of_int8_estimate": round(tops / peak, 4)}), flush=True)
+                del x
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.sweep:
+        return run_sweep(args)
     return run_ours(args)
 
 

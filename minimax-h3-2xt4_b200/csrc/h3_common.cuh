@@ -225,53 +225,14 @@ H3_DEV int8_t quantize_code_mode(float x, float scale, float inv, int division) 
 }
 
 // ---------------------------------------------------------------------------
-// Regular ConvRot256 butterfly: one radix-4 stage over a 16-value register block.
-// Stage stride s in {1, 4}; output digit d of each 4-point set is
+// Regular ConvRot256 butterfly (tilelang_swiglu_quant.py:26-36,46) on two 256-value
+// groups at once: lane 0 of every f32x2 pair holds one group's value, lane 1 the
+// other's.  One radix-4 stage over a 16-value register block, stride S in {1, 4};
+// output digit d of each 4-point set (a, b, c, d) is
 //   d=0: ((a+b)+c)-d   d=1: ((a+b)-c)+d   d=2: ((a-b)+c)+d   d=3: ((b-a)+c)+d
-// which is B[i] = ((p+q)+r)+s with the negations of tilelang_swiglu_quant.py:28-33.
+// which is B[i] = ((p+q)+r)+s with the reference's negations; every addition is the
+// f32x2 form of the IEEE RN one (x + (-y) and x - y are the same operation).
 // ---------------------------------------------------------------------------
-template <int S>
-H3_DEV void radix4_stage(float (&v)[16]) {
-#pragma unroll
-  for (int base = 0; base < 16; ++base) {
-    if ((base / S) % 4 != 0) continue;
-    const float a = v[base], b = v[base + S], c = v[base + 2 * S], d = v[base + 3 * S];
-    const float ab = __fadd_rn(a, b);
-    v[base]         = __fadd_rn(__fadd_rn(ab, c), -d);
-    v[base + S]     = __fadd_rn(__fadd_rn(ab, -c), d);
-    v[base + 2 * S] = __fadd_rn(__fadd_rn(__fadd_rn(a, -b), c), d);
-    v[base + 3 * S] = __fadd_rn(__fadd_rn(__fadd_rn(-a, b), c), d);
-  }
-}
-
-// Full 256-point regular rotation of one group held by 16 consecutive lanes of a warp
-// (lane % 16 == block index b, v[j] = element 16*b + j on entry).  Stages 0-1 run on
-// the lane's own block, a transpose through shared memory hands every lane the 16
-// values {16*t + r}, stages 2-3 run on those, and a second transpose restores
-// v[j] = rotated element 16*b + j, already multiplied by 1/16.
-// tile: 16 x 17 floats of shared memory private to this half warp.
-H3_DEV void convrot256_halfwarp(float (&v)[16], float* tile, int b) {
-  radix4_stage<1>(v);
-  radix4_stage<4>(v);
-#pragma unroll
-  for (int j = 0; j < 16; ++j) tile[b * 17 + j] = v[j];
-  __syncwarp();
-#pragma unroll
-  for (int t = 0; t < 16; ++t) v[t] = tile[t * 17 + b];
-  __syncwarp();
-  radix4_stage<1>(v);
-  radix4_stage<4>(v);
-#pragma unroll
-  for (int t = 0; t < 16; ++t) tile[t * 17 + b] = __fmul_rn(v[t], 0.0625f);
-  __syncwarp();
-#pragma unroll
-  for (int j = 0; j < 16; ++j) v[j] = tile[b * 17 + j];
-  __syncwarp();
-}
-
-// The same rotation on two groups at once: lane 0 of every pair holds one group's
-// value, lane 1 the other's, and every addition is the f32x2 form of the scalar one
-// above ((a+b)+c)+(-d) = ((a+b)+c)-d, and -a+b = b-a, are the same IEEE operations).
 template <int S>
 H3_DEV void radix4_stage2(f32x2 (&v)[16]) {
 #pragma unroll
@@ -286,7 +247,12 @@ H3_DEV void radix4_stage2(f32x2 (&v)[16]) {
   }
 }
 
-// convrot256_halfwarp on two groups; tile: 16 x 17 pairs private to this half warp.
+// Full 256-point rotation of two groups held by 16 consecutive lanes of a warp (lane
+// % 16 == block index b, v[j] = element 16*b + j of each group on entry).  Stages 0-1
+// run on the lane's own block, a transpose through shared memory hands every lane the
+// 16 values {16*t + r}, stages 2-3 run on those, and a second transpose restores
+// v[j] = rotated element 16*b + j, multiplied by 1/16.  tile: 16 x 17 pairs of shared
+// memory private to this half warp.
 H3_DEV void convrot256_halfwarp2(f32x2 (&v)[16], f32x2* tile, int b) {
   radix4_stage2<1>(v);
   radix4_stage2<4>(v);

@@ -7,9 +7,11 @@
 // rotated, reduced and quantised from registers in a single pass.
 //
 // Thread layout: a row of `width` values is split into 16-value blocks; 16 lanes
-// (a half warp) own the 16 blocks of one 256-value ConvRot group.  Each lane loads
-// its block with 128-bit loads, the group is rotated by convrot256_halfwarp, and
-// each lane stores its 16 results with 128-bit stores.
+// (a half warp) own the 16 blocks of one 256-value ConvRot group, and every lane holds
+// two blocks of two different groups as packed f32x2 pairs.  Each lane loads its
+// blocks with 128-bit loads, the two groups are rotated together by
+// convrot256_halfwarp2 (f32x2 arithmetic, per-lane IEEE rounding), and the codes are
+// stored 16 bytes at a time.
 
 #include "h3_common.cuh"
 

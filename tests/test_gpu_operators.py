@@ -203,6 +203,46 @@ def test_o_projection_row_emulated_tp2(cuda_device, oracle):
     _eq(_np(y), oracle.row_reduce_finish(parts, shift, sr, s.ravel()))
 
 
+def test_te_shared_column_linears_k5120(cuda_device, oracle):
+    """TE (Qwen3-VL) column shapes: one rotation + quantisation of a K = 5120 input
+    shared by two projections (dit_column_linear.py:70-96)."""
+    from h3tp.dit_column_linear import shared_column_linears
+    rng = np.random.default_rng(12)
+    x = rng.standard_normal((96, 5120)).astype(np.float32)
+    x[:, rng.permutation(5120)[:51]] *= 20
+    x = x.astype(np.float16)
+    projections = [_weights(rng, 1536, 5120), _weights(rng, 512, 5120)]
+    with torch.no_grad():
+        outs = shared_column_linears(_t(x, cuda_device),
+                                     [(_t(w, cuda_device), _t(s, cuda_device)) for w, s in projections])
+    for (w, s), y in zip(projections, outs):
+        ref, _ = oracle.column_linear(x, w, s.ravel(), convrot=True)
+        _eq(_np(y), ref)
+
+
+def test_te_row_linear_parts_k12800(cuda_device, oracle):
+    """TE row shape: separate gate / up inputs of K = 12800 through row_linear_parts
+    (h3_operator_policy.py:240-255), the fused FC2 route at TP = 1."""
+    from h3tp.h3_operator_policy import H3OperatorPolicy, row_linear_parts
+    from h3tp.tp_dit import RowParallelLinearINT8
+    rng = np.random.default_rng(13)
+    M, kl, N = 64, 12800, 512
+    gate = rng.standard_normal((M, kl)).astype(np.float16)
+    up = rng.standard_normal((M, kl)).astype(np.float16)
+    w, s = _weights(rng, N, kl, fold=512)
+    mod = RowParallelLinearINT8(kl, N, 0, 1, device=cuda_device)
+    mod.load_shard_from_full(torch.from_numpy(w), torch.from_numpy(s))
+    mod.operator_policy = H3OperatorPolicy()
+
+    def fallback(*args):
+        raise AssertionError("the fused route must apply")
+
+    with torch.no_grad():
+        y = row_linear_parts(mod, _t(gate, cuda_device), _t(up, cuda_device), fallback, None)
+    ref, _, _ = oracle.fc2_fused_stored([np.concatenate([gate, up], 1)], [w], s.ravel(), out="f32")
+    _eq(_np(y), ref)
+
+
 def test_unsupported_geometry_raises_before_launch(cuda_device):
     from h3tp import ops
     x = torch.zeros((4, 300), dtype=torch.float16, device=cuda_device)
