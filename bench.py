@@ -512,6 +512,31 @@ def run_sweep(args):
                                       "ms": round(ms, 4), "tops": round(tops, 2),
                                       "frac_of_int8_estimate": round(tops / peak, 4)}), flush=True)
                 del x
+        # row 2 of the scope table: the column input producer, fused modulated RMSNorm ->
+        # ConvRot -> quant, against the unfused route (norm -> fp16 h -> quantiser)
+        from h3tp import ops
+        M = 32768
+        hbm = peaks()["hbm_gbs"]
+        for K in (3072, 5120, 5376):
+            x = torch.randn((M, K), generator=g, device=dev).half()
+            w = torch.rand((K,), generator=g, device=dev) + 0.5
+            sh = torch.randn((3, K), generator=g, device=dev) * 0.1
+            sc = torch.randn((3, K), generator=g, device=dev) * 0.1
+            lab = (torch.arange(M, device=dev) % 3).to(torch.int32)
+            fused = timed(lambda: ops.modulated_norm_quantize(x, w, 1e-6, sh, sc, lab))
+
+            def unfused():
+                _, _, h = ops.modulated_norm_quantize(x, w, 1e-6, sh, sc, lab, quantize=False)
+                ops.column_quantize(h, True)
+
+            sep = timed(unfused)
+            nbytes = M * K * 2 + M * K + 4 * M  # read x, write codes and scales
+            print(json.dumps({"sweep": "norm_producer", "M": M, "K": K, "ms_fused": round(fused, 4),
+                              "ms_unfused": round(sep, 4),
+                              "gbs_fused": round(nbytes / (fused * 1e-3) / 1e9, 1),
+                              "frac_of_hbm": round(nbytes / (fused * 1e-3) / 1e9 / hbm, 4)}),
+                  flush=True)
+            del x
     return 0
 
 

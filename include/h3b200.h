@@ -76,6 +76,21 @@ int h3_device_error(int device, int* code);
 int h3_column_quantize(const void* x_f16, int64_t rows, int64_t k, int convrot,
                        int8_t* q, float* scale, void* stream);
 
+/* The column input producer with the modulated RMSNorm in front (fused version of
+ * tilelang_dit_fusion.py:11-37 -> h3_column_quantize; h3_tensor_flow.py:134-143):
+ *   ss = sum_i f32(x_i)^2 (fixed order), inv = RN(1/sqrt(ss *rn f32(1/width) +rn eps)),
+ *   h_i = f16( (((f32(x_i) *rn inv) *rn W_i) *rn (1 +rn scale[l][i])) +rn shift[l][i] ),
+ * l = labels[row] (labels may be NULL when mod_rows == 1); then h goes through the
+ * column quantiser (ConvRot256 when convrot, f16 rounding, row scale, codes) without
+ * being stored.  q / row_scale may both be NULL to produce only h; h_f16 (fp16
+ * [rows, width]) may be NULL when quantising.  The reference's own kernel calls the
+ * approximate rsqrtf; this one is correctly rounded. */
+int h3_modulated_norm_quantize(const void* x_f16, int64_t rows, int64_t width,
+                               const float* norm_weight, float eps, const float* shift,
+                               const float* scale, int64_t mod_rows, const int32_t* labels,
+                               int convrot, int8_t* q, float* row_scale, void* h_f16,
+                               void* stream);
+
 /* Direct INT8 GEMM, INT32 out: out[m, n] = sum_k q[m, k] * w[n, k], exact.
  * Replaces optimized_tp.py:34-43 (native_int_mm) and parallel_int8.py:46-50. */
 int h3_int8_gemm_i32(const int8_t* q, const int8_t* w, int64_t m, int64_t n, int64_t k,

@@ -141,7 +141,10 @@ H3_DEV float swiglu_f32(float gate, float up) { return __fmul_rn(silu_fast(gate)
 // Packed FP32 pairs.  sm_100's add / sub / mul / fma .rn.f32x2 instructions work on two
 // floats held in one 64-bit register pair and round each lane exactly as the scalar
 // .rn instruction does, so two independent computations written with them give the
-// same bits as the scalar form at half the instruction issue.
+// same bits as the scalar form at half the instruction issue.  One caution, measured:
+// a mul.rn.f32x2 whose result feeds an add.rn.f32x2 can be contracted into a fused
+// multiply-add by the assembler, so a product that feeds an addition is written with
+// the scalar __fmul_rn / __fadd_rn (never contracted) or as an explicit fma.
 // ---------------------------------------------------------------------------
 typedef uint64_t f32x2;
 

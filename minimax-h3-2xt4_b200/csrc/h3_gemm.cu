@@ -267,7 +267,26 @@ H3_DEV void tmem_ld8_nowait(uint32_t taddr, uint32_t (&r)[8]) {
                : "r"(taddr));
 }
 
-H3_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// tcgen05.wait::ld with the 16 destination registers of the loads it completes passed
+// through it: the loads write those registers asynchronously, and the operands keep the
+// compiler from moving any use of them above the wait.
+H3_DEV void tmem_wait_ld(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
+
+H3_DEV void tmem_wait_ld(uint32_t (&a)[8], uint32_t (&b)[8]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]),
+                 "+r"(a[6]), "+r"(a[7]), "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]),
+                 "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7])
+               :
+               : "memory");
+}
 
 // Tile order.  group_n > 0: groups of group_n N-blocks (a weight slab that stays in
 // L2) sweep all M-blocks, N fastest, so A is read from HBM once per group; otherwise
@@ -438,7 +457,7 @@ H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool ro
         load_scales<SW>(args.bias, n0, N, 0, bg, vec4);
         load_scales<SW>(args.bias + N, n0, N, 0, bu, vec4);
       }
-      tmem_wait_ld();
+      tmem_wait_ld(rg, ru);
       float y[SW];
 #pragma unroll
       for (int j = 0; j < SW; ++j) {
@@ -476,7 +495,7 @@ H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool ro
     for (int c = 0; c < 128 / 16; ++c) {
       uint32_t r[16];
       tmem_ld16_nowait(tbase + gl * 128 + c * 16, r);
-      tmem_wait_ld();
+      tmem_wait_ld(r);
 #pragma unroll
       for (int j = 0; j < 16; ++j) m = fmaxf(m, fabsf(__int2float_rn((int32_t)r[j])));
     }
@@ -487,7 +506,7 @@ H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool ro
     for (int c = 0; c < COLS / 16; ++c) {
       uint32_t r[16];
       tmem_ld16_nowait(tbase + part * COLS + c * 16, r);
-      tmem_wait_ld();
+      tmem_wait_ld(r);
       if (!row_ok) continue;
       uint32_t w[4];
 #pragma unroll
@@ -532,7 +551,7 @@ H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool ro
       if (EPI == EPI_COLUMN || EPI == EPI_ROW_DEQUANT)
         load_scales<16>(args.weight_scale, n0, N, EPI == EPI_COLUMN ? args.scalar_w : 0, w,
                         args.scale_vec != 0);
-      tmem_wait_ld();
+      tmem_wait_ld(r);
       if (!row_ok) continue;
       if (EPI == EPI_I32) {
         int32_t* dst = reinterpret_cast<int32_t*>(args.out) + row * N + n0;

@@ -212,13 +212,109 @@ __global__ void __launch_bounds__(512) swiglu_rotate_kernel(
   }
 }
 
-// Column activation preparation (QKV / FC1 input): optional ConvRot256 with an fp16
-// rounding of the rotated value, then the row quantiser.  One CTA per row, packed
-// pairs of blocks as in swiglu_rotate_kernel.
-template <int NP, bool ROTATE>
+// Modulated RMSNorm in front of the column quantiser (tilelang_dit_fusion.py:11-37):
+// the activation tables and the per-row result.  Unused unless NORM.
+struct NormArgs {
+  const float* weight;  // [width]
+  const float* shift;   // [mod_rows, width]
+  const float* scale;   // [mod_rows, width]
+  const int32_t* labels;
+  int64_t mod_rows;
+  float eps, inv_width;
+  __half* h;  // optional fp16 output of the norm
+  int* err;
+};
+
+// CTA sum with the order the oracle restates: a warp xor butterfly, then the warps in
+// order.
+H3_DEV float block_reduce_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float m = 0.0f;
+  const int nw = blockDim.x >> 5;
+  for (int w = 0; w < nw; ++w) m = __fadd_rn(m, red[w]);
+  __syncthreads();
+  return m;
+}
+
+// h = f16( (((x *rn inv) *rn W) *rn (1 +rn Scale[l])) +rn Shift[l] ) for the pairs of
+// blocks of this thread, in place; the sum of squares runs in the order of
+// oracle/h3_oracle.c (per block over i, then the two lanes, then the pairs).
+template <int NP>
+H3_DEV void modulated_norm_pairs(f32x2 (&v)[NP][16], const int64_t (&blk)[NP][2],
+                                 const bool (&ok)[NP][2], int64_t row, int64_t width,
+                                 const NormArgs& na, float* red) {
+  // A product feeding an addition is written with the scalar __fmul_rn / __fadd_rn,
+  // which are never contracted into a fused multiply-add; pure products use f32x2.
+  float t = 0.0f;
+#pragma unroll
+  for (int p = 0; p < NP; ++p) {
+    float s0 = __fmul_rn(lo2(v[p][0]), lo2(v[p][0]));
+    float s1 = __fmul_rn(hi2(v[p][0]), hi2(v[p][0]));
+#pragma unroll
+    for (int i = 1; i < 16; ++i) {
+      s0 = __fadd_rn(s0, __fmul_rn(lo2(v[p][i]), lo2(v[p][i])));
+      s1 = __fadd_rn(s1, __fmul_rn(hi2(v[p][i]), hi2(v[p][i])));
+    }
+    const float tp = __fadd_rn(s0, s1);
+    t = p == 0 ? tp : __fadd_rn(t, tp);
+  }
+  const float total = block_reduce_sum(t, red);
+  const float inv = __frsqrt_rn(__fadd_rn(__fmul_rn(total, na.inv_width), na.eps));
+  int64_t lab = na.labels ? (int64_t)__ldg(na.labels + row) : 0;
+  if (lab < 0 || lab >= na.mod_rows) {
+    atomicExch(na.err, H3_ERR_INVALID);
+    lab = 0;
+  }
+  const float* sh = na.shift + lab * width;
+  const float* sc = na.scale + lab * width;
+  const f32x2 inv2 = dup2(inv), one = dup2(1.0f);
+#pragma unroll
+  for (int p = 0; p < NP; ++p) {
+    float w[2][16], f[2][16], d[2][16];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int64_t c = (ok[p][e] ? blk[p][e] : 0) * 16;
+      load_float16(na.weight + c, w[e]);
+      load_float16(sc + c, f[e]);
+      load_float16(sh + c, d[e]);
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const f32x2 scaled = mul2(mul2(mul2(v[p][i], inv2), pk2(w[0][i], w[1][i])),
+                                add2(one, pk2(f[0][i], f[1][i])));
+      const float y0 = __fadd_rn(lo2(scaled), d[0][i]), y1 = __fadd_rn(hi2(scaled), d[1][i]);
+      const float2 hf = __half22float2(__floats2half2_rn(y0, y1));
+      v[p][i] = pk2(ok[p][0] ? hf.x : 0.0f, ok[p][1] ? hf.y : 0.0f);
+    }
+    if (na.h != nullptr) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        if (!ok[p][e]) continue;
+        __half2 hv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          hv[j] = e == 0 ? __floats2half2_rn(lo2(v[p][2 * j]), lo2(v[p][2 * j + 1]))
+                         : __floats2half2_rn(hi2(v[p][2 * j]), hi2(v[p][2 * j + 1]));
+        uint4* dst = reinterpret_cast<uint4*>(na.h + row * width + blk[p][e] * 16);
+        dst[0] = *reinterpret_cast<uint4*>(&hv[0]);
+        dst[1] = *reinterpret_cast<uint4*>(&hv[4]);
+      }
+    }
+  }
+}
+
+// Column activation preparation (QKV / FC1 input): optional modulated RMSNorm
+// (NORM), optional ConvRot256 with an fp16 rounding of the rotated value, then the row
+// quantiser.  One CTA per row, packed pairs of blocks as in swiglu_rotate_kernel.
+// QUANT = false stops after the norm (its fp16 output only).
+template <int NP, bool ROTATE, bool NORM, bool QUANT>
 __global__ void __launch_bounds__(512) column_quantize_kernel(
     const __half* __restrict__ x, int64_t rows, int64_t k, int8_t* __restrict__ q,
-    float* __restrict__ scale_out) {
+    float* __restrict__ scale_out, const NormArgs na) {
   extern __shared__ f32x2 smem2[];
   const int tid = threadIdx.x;
   const int half = tid >> 4, b = tid & 15;
@@ -236,10 +332,14 @@ __global__ void __launch_bounds__(512) column_quantize_kernel(
     }
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     f32x2 v[NP][16];
+#pragma unroll
+    for (int p = 0; p < NP; ++p)
+      load_activation2<H3_IN_ACT_F16>(x, row, k, blk[p][0], blk[p][1], ok[p][0], ok[p][1], v[p]);
+    if (NORM) modulated_norm_pairs<NP>(v, blk, ok, row, k, na, red);
+    if (!QUANT) continue;
     float m_nan = 0.0f;
 #pragma unroll
     for (int p = 0; p < NP; ++p) {
-      load_activation2<H3_IN_ACT_F16>(x, row, k, blk[p][0], blk[p][1], ok[p][0], ok[p][1], v[p]);
       if (ROTATE) {
         convrot256_halfwarp2(v[p], tile, b);
 #pragma unroll
@@ -435,11 +535,13 @@ extern "C" int h3_column_quantize(const void* x_f16, int64_t rows, int64_t k, in
   cudaStream_t st = (cudaStream_t)stream;
   const __half* xh = reinterpret_cast<const __half*>(x_f16);
   static bool smem_set[2][2] = {{false, false}, {false, false}};
-#define H3_COLQ(NPV, ROT)                                                                   \
-  do {                                                                                      \
-    if (!allow_smem(column_quantize_kernel<NPV, ROT>, smem, smem_set[NPV - 1][ROT]))        \
-      return H3_ERR_CUDA;                                                                   \
-    column_quantize_kernel<NPV, ROT><<<grid, t.threads, smem, st>>>(xh, rows, k, q, scale); \
+#define H3_COLQ(NPV, ROT)                                                                  \
+  do {                                                                                     \
+    if (!allow_smem(column_quantize_kernel<NPV, ROT, false, true>, smem,                   \
+                    smem_set[NPV - 1][ROT]))                                               \
+      return H3_ERR_CUDA;                                                                  \
+    column_quantize_kernel<NPV, ROT, false, true>                                          \
+        <<<grid, t.threads, smem, st>>>(xh, rows, k, q, scale, NormArgs{});                \
   } while (0)
   if (t.nb == 1) {
     if (convrot) H3_COLQ(1, true); else H3_COLQ(1, false);
@@ -500,5 +602,57 @@ extern "C" int h3_quant_compare(const float* x, const float* scale, int64_t n, i
   if (int s = h3host::bind_device_of(x, &dev)) return s;
   const int grid = (int)std::min<int64_t>((n + 255) / 256, (int64_t)h3host::sm_count(dev) * 16);
   quant_compare_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(x, scale, n, fast, ieee);
+  return h3host::check_launch();
+}
+
+extern "C" int h3_modulated_norm_quantize(const void* x_f16, int64_t rows, int64_t width,
+                                          const float* norm_weight, float eps,
+                                          const float* shift, const float* scale,
+                                          int64_t mod_rows, const int32_t* labels, int convrot,
+                                          int8_t* q, float* row_scale, void* h_f16,
+                                          void* stream) {
+  const bool quant = q != nullptr || row_scale != nullptr;
+  if (x_f16 == nullptr || norm_weight == nullptr || shift == nullptr || scale == nullptr ||
+      rows < 0 || width <= 0 || width % 16 != 0 || width > 4 * 512 * 16 || mod_rows < 1 ||
+      (labels == nullptr && mod_rows != 1) || (quant && (q == nullptr || row_scale == nullptr)) ||
+      (!quant && h_f16 == nullptr) || (quant && convrot && width % 256 != 0))
+    return H3_ERR_INVALID;
+  if (!h3host::aligned(x_f16, 16) || !h3host::aligned(norm_weight, 16) ||
+      !h3host::aligned(shift, 16) || !h3host::aligned(scale, 16) ||
+      (q != nullptr && !h3host::aligned(q, 16)) || (h_f16 != nullptr && !h3host::aligned(h_f16, 16)))
+    return H3_ERR_INVALID;
+  if (rows == 0) return H3_OK;
+  int dev;
+  if (int s = h3host::bind_device_of(x_f16, &dev)) return s;
+  NormArgs na{norm_weight, shift, scale, labels, mod_rows, eps,
+              (float)(1.0 / (double)width), reinterpret_cast<__half*>(h_f16),
+              h3host::error_word(dev)};
+  if (na.err == nullptr) return H3_ERR_CUDA;
+  const RowTeam t = row_team(width);
+  const size_t smem = producer_smem(t.threads);
+  const int grid = (int)std::min<int64_t>(rows, 1 << 20);
+  cudaStream_t st = (cudaStream_t)stream;
+  const __half* xh = reinterpret_cast<const __half*>(x_f16);
+  static bool smem_set[2][3] = {{false, false, false}, {false, false, false}};
+#define H3_NORMQ(NPV, ROT, QU, SLOT)                                                       \
+  do {                                                                                     \
+    if (!allow_smem(column_quantize_kernel<NPV, ROT, true, QU>, smem,                      \
+                    smem_set[NPV - 1][SLOT]))                                              \
+      return H3_ERR_CUDA;                                                                  \
+    column_quantize_kernel<NPV, ROT, true, QU>                                             \
+        <<<grid, t.threads, smem, st>>>(xh, rows, width, q, row_scale, na);                \
+  } while (0)
+  if (t.nb == 1) {
+    if (!quant) H3_NORMQ(1, false, false, 0);
+    else if (convrot) H3_NORMQ(1, true, true, 1);
+    else H3_NORMQ(1, false, true, 2);
+  } else if (t.nb == 2) {
+    if (!quant) H3_NORMQ(2, false, false, 0);
+    else if (convrot) H3_NORMQ(2, true, true, 1);
+    else H3_NORMQ(2, false, true, 2);
+  } else {
+    return H3_ERR_INVALID;
+  }
+#undef H3_NORMQ
   return h3host::check_launch();
 }

@@ -57,6 +57,8 @@ SIGNATURES = {
     "h3_dequantize_i32": [_P, _I64, _I64, _P, _P, _I64, _P, _I, _P, _P],
     "h3_gated_add": [_P, _I, _I64, _I64, _P, _P, _I64, _P, _P],
     "h3_int8_gemm_row_pack8": [_P, _P, _I64, _I64, _I64, _P, _P],
+    "h3_modulated_norm_quantize": [_P, _I64, _I64, _P, ctypes.c_float, _P, _P, _I64, _P, _I, _P,
+                                   _P, _P, _P],
     "h3_pack8": [_P, _I64, _I64, _P, _P],
     "h3_unpack8_finish": [_P, _I, _I64, _I64, _I64, _P, _P, _I, _P, _P, _P, _I64, _P, _P],
     "h3_peer_reduce_int8": [_PP, _I, _I, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _P,

@@ -65,6 +65,19 @@ def column_linear(x, weight, weight_scale, *, convrot=True, convrot_groupsize=25
     return out.reshape(*shape[:-1], weight.shape[0])
 
 
+def column_linear_quantized(codes, row_scale, weight, weight_scale, *, bias=None, swiglu=False,
+                            swiglu_dtype=torch.float32):
+    """The GEMM + ordered epilogue of column_linear on activation codes that were
+    already produced (e.g. by the fused modulated-norm producer)."""
+    weight, ws = _check(codes, weight, weight_scale)
+    b = None if bias is None else bias.to(device=codes.device, dtype=torch.float32).reshape(-1)
+    if swiglu:
+        if ws.numel() != weight.shape[0]:
+            ws = ws.expand(weight.shape[0]).contiguous()
+        return ops.int8_gemm_swiglu(codes, weight, row_scale, ws, b, swiglu_dtype)
+    return ops.int8_gemm_column(codes, weight, row_scale, ws, b)
+
+
 def shared_column_linears(x, projections, *, convrot=True, convrot_groupsize=256):
     """One rotation + quantisation shared by several projections of the same input
     (dit_column_linear.py:70-96); one GEMM per projection."""

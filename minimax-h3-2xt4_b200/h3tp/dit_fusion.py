@@ -46,6 +46,45 @@ def _labels(rows, segments, device):
     return labels, ready
 
 
+def _norm_supported(norm, x, shift, scale):
+    return (isinstance(x, torch.Tensor) and x.is_cuda and x.ndim == 2 and x.shape[0] > 0
+            and x.dtype == torch.float16 and x.shape[1] % 16 == 0 and x.shape[1] <= 32768
+            and not getattr(norm, "layer_norm", False)
+            and tuple(getattr(norm, "normalized_shape", ())) == (x.shape[1],)
+            and getattr(norm, "weight", None) is not None
+            and norm.weight.dtype == torch.float32 and norm.weight.device == x.device
+            and shift.ndim == 2 and shift.shape == scale.shape and shift.shape[1] == x.shape[1]
+            and shift.dtype == torch.float32 and scale.dtype == torch.float32
+            and shift.device == x.device and scale.device == x.device)
+
+
+def modulated_norm(norm, x, shift, scale, segments):
+    """Fused modulated RMSNorm (tilelang_dit_fusion.py:127-134): fp16 h, or None when the
+    fused kernel does not apply (the caller then runs its own path)."""
+    if not _norm_supported(norm, x, shift, scale):
+        return None
+    labels = labels_for(x, segments, shift.shape[0])
+    if labels is None:
+        return None
+    _, _, h = ops.modulated_norm_quantize(x, norm.weight, float(norm.eps), shift.contiguous(),
+                                          scale.contiguous(), labels, quantize=False)
+    return h
+
+
+def modulated_norm_quantize(norm, x, shift, scale, segments, convrot=True):
+    """The column input producer: modulated RMSNorm -> (ConvRot256) -> per-row INT8
+    quantisation in one kernel, h never stored.  Returns (codes, row_scale), the
+    operands of ColumnParallelLinearINT8.forward_quantized, or None."""
+    if not _norm_supported(norm, x, shift, scale) or (convrot and x.shape[1] % 256):
+        return None
+    labels = labels_for(x, segments, shift.shape[0])
+    if labels is None:
+        return None
+    q, s, _ = ops.modulated_norm_quantize(x, norm.weight, float(norm.eps), shift.contiguous(),
+                                          scale.contiguous(), labels, convrot=convrot)
+    return q, s
+
+
 def labels_for(x, segments, modulation_rows=9):
     """Per-row modulation labels on x's device, cached (tilelang_dit_fusion.py:115-124)."""
     if segments is None:

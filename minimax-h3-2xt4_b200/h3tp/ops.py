@@ -69,6 +69,37 @@ def column_quantize(x: torch.Tensor, convrot: bool = True):
     return q, s
 
 
+def modulated_norm_quantize(x, weight, eps: float, shift, scale, labels=None, convrot=True,
+                            quantize=True, want_h=False):
+    """Modulated RMSNorm (tilelang_dit_fusion.py:11-37) fused with the column
+    activation quantiser: x fp16 [M, K] -> (codes int8 [M, K], row_scale fp32 [M, 1],
+    h fp16 [M, K] or None).  quantize=False returns (None, None, h)."""
+    x = _need(x, torch.float16, "x", 2)
+    M, K = x.shape
+    w = _vec(weight, K, "norm weight")
+    shift = _need(shift, torch.float32, "shift", 2)
+    scale = _need(scale, torch.float32, "scale", 2)
+    if shift.shape != scale.shape or shift.shape[1] != K:
+        raise ValueError("shift / scale tables must be [modulation_rows, K]")
+    lab = None
+    if labels is not None:
+        lab = _need(labels, torch.int32, "labels", 1)
+        if lab.numel() != M:
+            raise ValueError("one label per row required")
+    elif shift.shape[0] != 1:
+        raise ValueError("labels required for a multi-row modulation table")
+    q = s = h = None
+    if quantize:
+        q = torch.empty((M, K), dtype=torch.int8, device=x.device)
+        s = torch.empty((M, 1), dtype=torch.float32, device=x.device)
+    if want_h or not quantize:
+        h = torch.empty((M, K), dtype=torch.float16, device=x.device)
+    N.call("h3_modulated_norm_quantize", x.data_ptr(), M, K, w.data_ptr(), float(eps),
+           shift.data_ptr(), scale.data_ptr(), shift.shape[0], _ptr(lab), int(bool(convrot)),
+           _ptr(q), _ptr(s), _ptr(h), _stream(x))
+    return q, s, h
+
+
 def int8_gemm_i32(q: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """Exact INT32 q @ w.T on the tensor cores (tcgen05 kind::i8)."""
     q = _need(q, torch.int8, "q", 2)

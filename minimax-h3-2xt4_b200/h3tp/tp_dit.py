@@ -84,6 +84,16 @@ class ColumnParallelLinearINT8(nn.Module):
         out = out.view(*orig_shape[:-1], width)
         return adapter.add_to(x, out) if adapter is not None else out
 
+    def forward_quantized(self, codes: torch.Tensor, row_scale: torch.Tensor) -> torch.Tensor:
+        """forward() on activation codes from the fused modulated-norm producer
+        (h3tp.dit_fusion.modulated_norm_quantize); no LoRA (it needs the fp16 input)."""
+        from .dit_column_linear import column_linear_quantized
+        if getattr(self, "lora_adapter", None) is not None:
+            raise ValueError("forward_quantized has no LoRA path: use forward(h)")
+        swiglu = bool(self.components == 2 and getattr(self, "_swiglu_epilogue", False))
+        return column_linear_quantized(codes, row_scale, self.weight, self.weight_scale,
+                                       bias=self.bias, swiglu=swiglu)
+
 
 class RowParallelLinearINT8(nn.Module):
     """Row-parallel INT8 linear: input features split across TP ranks, partial sums

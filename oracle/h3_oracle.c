@@ -415,6 +415,127 @@ EXPORT void h3o_unpack8_restore(const uint8_t* parts, int world, int64_t part_st
     }
 }
 
+/* ---------------------------------------------------------------------------
+ * Modulated RMSNorm (tilelang_dit_fusion.py:11-37, h3_tensor_flow.py:134-143) as the
+ * fused column producer computes it:
+ *   ss = sum_i f32(x_i) *rn f32(x_i)            (the kernel's fixed order, below)
+ *   mean = ss *rn f32(1/width);  inv = RN(1/sqrt(mean +rn f32(eps)))
+ *   h_i = f16( (((f32(x_i) *rn inv) *rn W_i) *rn (1 +rn Scale[l][i])) +rn Shift[l][i] )
+ * The reference's rsqrtf is CUDA's approximation and its sum order TileLang's; here the
+ * reciprocal square root is correctly rounded and the order is fixed.
+ * ------------------------------------------------------------------------- */
+
+/* RN(1/sqrt(v)) for a positive finite float v, exactly: the double estimate is within
+ * one float ulp, and the final choice compares v against the squared midpoints in
+ * 128-bit integer arithmetic. */
+static float rsqrt_rn(float v) {
+  if (!(v > 0.0f)) return v == 0.0f ? INFINITY : NAN;
+  if (isinf(v)) return 0.0f;
+  float y = (float)(1.0 / sqrt((double)v));
+  int ev;
+  const double fv = frexp((double)v, &ev);               /* v = fv * 2^ev, fv in [0.5,1) */
+  const unsigned __int128 V = (unsigned __int128)(uint64_t)ldexp(fv, 24); /* 24 bits */
+  const int ve = ev - 24;
+  for (int it = 0; it < 3; ++it) {
+    /* candidate is correct iff lo_mid < 1/sqrt(v) < hi_mid, i.e. lo_mid^2 * v < 1 < hi_mid^2 * v */
+    const float up = nextafterf(y, INFINITY), dn = nextafterf(y, 0.0f);
+    int moved = 0;
+    for (int side = 0; side < 2; ++side) {
+      const double mid = 0.5 * ((double)y + (double)(side ? up : dn)); /* exact in double */
+      int em;
+      const double fm = frexp(mid, &em);                  /* mid = fm * 2^em */
+      const unsigned __int128 Mq = (unsigned __int128)(uint64_t)ldexp(fm, 26); /* 26 bits */
+      const unsigned __int128 prod = Mq * Mq * V;         /* mid^2 * v = prod * 2^e2 */
+      const int e2 = 2 * (em - 26) + ve;
+      /* compare prod * 2^e2 with 1 */
+      int cmp;
+      if (e2 >= 0) cmp = 1;                               /* prod >= 1, so > 1 unless prod==1 && e2==0 */
+      else if (-e2 >= 127) cmp = -1;
+      else {
+        const unsigned __int128 one = (unsigned __int128)1 << (-e2);
+        cmp = prod > one ? 1 : (prod < one ? -1 : 0);
+      }
+      if (e2 == 0 && prod == 1) cmp = 0;
+      if (side == 1 && cmp <= 0) { y = up; moved = 1; break; }    /* 1/sqrt(v) >= hi_mid */
+      if (side == 0 && cmp >= 0) { y = dn; moved = 1; break; }    /* 1/sqrt(v) <= lo_mid */
+    }
+    if (!moved) break;
+  }
+  return y;
+}
+
+/* The kernel's thread layout for a row of `width` values: 16-value blocks, T threads,
+ * each holding NP pairs of blocks (tid + (2p) T, tid + (2p + 1) T). */
+static void row_team(int64_t width, int* T, int* NP) {
+  const int64_t blocks = width / 16;
+  int t = (int)((blocks + 1) / 2 < 512 ? (blocks + 1) / 2 : 512);
+  t = (t + 31) / 32 * 32;
+  if (t < 32) t = 32;
+  *T = t;
+  *NP = (int)((blocks + 2 * t - 1) / (2 * t));
+}
+
+/* Sum of squares in the kernel's order: per thread, per pair p, the two blocks' squares
+ * summed separately over i = 0..15, then (lane 0 + lane 1), pairs accumulated in
+ * order; per warp an xor butterfly (offsets 16, 8, 4, 2, 1); warps summed in order. */
+static float sum_squares(const uint16_t* x, int64_t width) {
+  int T, NP;
+  row_team(width, &T, &NP);
+  const int64_t blocks = width / 16;
+  float tsum[512];
+  for (int tid = 0; tid < T; ++tid) {
+    float t = 0.0f;
+    for (int p = 0; p < NP; ++p) {
+      float s[2] = {0.0f, 0.0f};
+      for (int e = 0; e < 2; ++e) {
+        const int64_t blk = tid + (int64_t)(2 * p + e) * T;
+        for (int i = 0; i < 16; ++i) {
+          const float v = blk < blocks ? h3o_half_to_float(x[blk * 16 + i]) : 0.0f;
+          const float sq = v * v;
+          s[e] = i == 0 ? sq : s[e] + sq;
+        }
+      }
+      const float tp = s[0] + s[1];
+      t = p == 0 ? tp : t + tp;
+    }
+    tsum[tid] = t;
+  }
+  float total = 0.0f;
+  for (int w = 0; w < T / 32; ++w) {
+    float v[32];
+    for (int l = 0; l < 32; ++l) v[l] = tsum[32 * w + l];
+    for (int o = 16; o > 0; o >>= 1) {
+      float n[32];
+      for (int l = 0; l < 32; ++l) n[l] = v[l] + v[l ^ o];
+      memcpy(v, n, sizeof(v));
+    }
+    total = total + v[0];
+  }
+  return total;
+}
+
+EXPORT void h3o_modulated_norm(const uint16_t* x, int64_t rows, int64_t width, const float* W,
+                               float eps, const float* shift, const float* scale,
+                               const int32_t* labels, uint16_t* h) {
+  const float inv_width = (float)(1.0 / (double)width);
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < rows; ++r) {
+    const uint16_t* xr = x + r * width;
+    const float mean = sum_squares(xr, width) * inv_width;
+    const float inv = rsqrt_rn(mean + eps);
+    const int64_t l = labels ? labels[r] : 0;
+    for (int64_t i = 0; i < width; ++i) {
+      const float value = h3o_half_to_float(xr[i]) * inv;
+      const float gain = value * W[i];
+      const float factor = 1.0f + scale[l * width + i];
+      const float scaled = gain * factor;
+      h[r * width + i] = h3o_float_to_half(scaled + shift[l * width + i]);
+    }
+  }
+}
+
+EXPORT float h3o_rsqrt_rn(float v) { return rsqrt_rn(v); }
+
 /* shift_for of tilelang_transport_tradeoffs.py:20-22 on the full reduction length. */
 EXPORT int h3o_transport_shift(int64_t full_k) {
   if (full_k <= 0) return 0;

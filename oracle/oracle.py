@@ -51,6 +51,9 @@ def lib() -> ctypes.CDLL:
         L.h3o_gated_add.argtypes = [P, I64, I64, P, P, P]
         L.h3o_transport_shift.argtypes = [I64]
         L.h3o_pack8.argtypes = [P, I64, I64, P]
+        L.h3o_modulated_norm.argtypes = [P, I64, I64, P, F, P, P, P, P]
+        L.h3o_rsqrt_rn.argtypes = [F]
+        L.h3o_rsqrt_rn.restype = F
         L.h3o_unpack8_restore.argtypes = [P, I, I64, I64, I64, P]
         L.h3o_transport_shift.restype = I
         _LIB = L
@@ -181,6 +184,24 @@ def fp16_decode(Y, shift: int) -> np.ndarray:
     P = np.empty(Y.shape, np.int32)
     lib().h3o_fp16_decode(_p(Y), Y.size, int(shift), _p(P))
     return P
+
+
+def modulated_norm(x, weight, eps, shift, scale, labels=None) -> np.ndarray:
+    """Modulated RMSNorm of the fused column producer (tilelang_dit_fusion.py:11-37
+    order of operations, correctly rounded rsqrt, the kernel's fixed sum order):
+    fp16 [rows, width] -> fp16 h."""
+    x = _c(x, np.float16)
+    rows, width = x.shape
+    h = np.empty_like(x)
+    lib().h3o_modulated_norm(_p(x), rows, width, _p(_c(weight, np.float32).ravel()),
+                             float(np.float32(eps)), _p(_c(shift, np.float32)),
+                             _p(_c(scale, np.float32)),
+                             _p(None if labels is None else _c(labels, np.int32)), _p(h))
+    return h
+
+
+def rsqrt_rn(v: float) -> float:
+    return float(lib().h3o_rsqrt_rn(float(v)))
 
 
 def pack8(P) -> np.ndarray:

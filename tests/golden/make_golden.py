@@ -16,7 +16,8 @@ functions whose CPU path never touches it are called:
   benchmarks/test_tp2_p2_epilogue.py  its five known-answer patterns (:15-38), built
                                    here on the CPU with the same seed and sizes, for
                                    both of its schemes ('fp16' and 'int8_gather')
-  patches/h3_tensor_flow.py        fold_linear (:82-103)
+  patches/h3_tensor_flow.py        fold_linear (:82-103), modulated_norm's torch
+                                   path (:134-143)
   patches/tilelang_dit_fusion.py   segment_key (:93-100)
 
 The reference is not needed at test time: the outputs are stored as .npz files next
@@ -135,6 +136,23 @@ def make(root: Path) -> None:
     flow.fold_linear(m, flow.TensorFlowPolicy().divisor)
     out["fold_before"], out["fold_after"] = before.numpy(), m.weight_scale.detach().numpy()
     out["fold_divisor"] = np.array([flow.TensorFlowPolicy().divisor], np.float64)
+
+    # --- modulated RMSNorm, the reference's torch path (h3_tensor_flow.py:134-143) -------
+    gn = torch.Generator().manual_seed(21)
+    rows_n, width_n = 37, 1024
+    xn = (torch.randn((rows_n, width_n), generator=gn) * 3).half()
+    xn[5, :64] = 0  # a partly zero row
+    norm = types.SimpleNamespace(normalized_shape=(width_n,),
+                                 weight=(torch.rand(width_n, generator=gn) + .5).float(),
+                                 eps=1e-6)
+    shift_n = (torch.randn((3, width_n), generator=gn) * .1).float()
+    scale_n = (torch.randn((3, width_n), generator=gn) * .1).float()
+    segs = [(0, 10, 0), (10, 30, 2), (30, rows_n, 1)]
+    out["norm_x"], out["norm_w"] = xn.numpy(), norm.weight.numpy()
+    out["norm_shift"], out["norm_scale"] = shift_n.numpy(), scale_n.numpy()
+    out["norm_eps"] = np.array([norm.eps], np.float64)
+    out["norm_labels"] = np.concatenate([np.full(b - a, r, np.int32) for a, b, r in segs])
+    out["norm_h"] = flow.modulated_norm(norm, xn, shift_n, scale_n, segs, fused=False).numpy()
 
     # --- segment validation (tilelang_dit_fusion.py:93-100) -----------------------------
     cases = [(10, [(0, 4, 1), (4, 10, 2)]), (10, [(0, 4, 1), (5, 10, 2)]),

@@ -236,6 +236,48 @@ def test_column_quantize_special_rows(cuda_device, oracle, convrot):
     _bits_equal(_np(s).ravel(), s_ref)
 
 
+# ----------------------------------------------------------------------------
+# fused modulated RMSNorm -> ConvRot -> quant (the column input producer)
+# ----------------------------------------------------------------------------
+@pytest.mark.parametrize("rows,width,convrot", [(37, 1024, True), (9, 3072, True),
+                                                (5, 5376, True), (7, 1040, False)])
+def test_modulated_norm_quantize_bit_exact(cuda_device, oracle, rows, width, convrot):
+    from h3tp import ops
+    rng = np.random.default_rng(rows + width)
+    x = (rng.standard_normal((rows, width)) * 3).astype(np.float16)
+    x[0, : width // 3] = 0
+    w = (rng.uniform(0.5, 1.5, width)).astype(np.float32)
+    shift = (rng.standard_normal((3, width)) * .1).astype(np.float32)
+    scale = (rng.standard_normal((3, width)) * .1).astype(np.float32)
+    labels = rng.integers(0, 3, rows).astype(np.int32)
+    h_ref = oracle.modulated_norm(x, w, 1e-6, shift, scale, labels)
+    q_ref, s_ref = oracle.column_quantize(h_ref, convrot)
+    q, s, h = ops.modulated_norm_quantize(_t(x, cuda_device), _t(w, cuda_device), 1e-6,
+                                          _t(shift, cuda_device), _t(scale, cuda_device),
+                                          _t(labels, cuda_device), convrot=convrot, want_h=True)
+    _bits_equal(_np(h), h_ref)
+    _bits_equal(_np(q), q_ref)
+    _bits_equal(_np(s).ravel(), s_ref)
+    _, _, h2 = ops.modulated_norm_quantize(_t(x, cuda_device), _t(w, cuda_device), 1e-6,
+                                           _t(shift, cuda_device), _t(scale, cuda_device),
+                                           _t(labels, cuda_device), quantize=False)
+    _bits_equal(_np(h2), h_ref)
+
+
+def test_modulated_norm_against_reference_golden(cuda_device):
+    """The reference's own torch path (h3_tensor_flow.modulated_norm, tests/golden):
+    within one fp16 ulp, nearly all bit for bit (different sum order, correctly
+    rounded rsqrt)."""
+    from h3tp import ops
+    G = np.load(Path(__file__).parent / "golden" / "reference_golden.npz")
+    _, _, h = ops.modulated_norm_quantize(
+        _t(G["norm_x"], cuda_device), _t(G["norm_w"], cuda_device), float(G["norm_eps"][0]),
+        _t(G["norm_shift"], cuda_device), _t(G["norm_scale"], cuda_device),
+        _t(G["norm_labels"], cuda_device), quantize=False)
+    d = np.abs(_np(h).view(np.int16).astype(np.int32) - G["norm_h"].view(np.int16).astype(np.int32))
+    assert d.max() <= 1 and (d == 0).mean() >= 0.999
+
+
 def test_row_quantize_owned_slice(cuda_device, oracle):
     from h3tp import ops
     rng = np.random.default_rng(5)

@@ -243,6 +243,37 @@ def test_te_row_linear_parts_k12800(cuda_device, oracle):
     _eq(_np(y), ref)
 
 
+def test_fused_norm_then_column_parallel_qkv(cuda_device, oracle):
+    """dit_fusion.modulated_norm_quantize feeding ColumnParallelLinearINT8.forward_quantized
+    gives the bits of the unfused route (norm -> fp16 h -> column linear)."""
+    from types import SimpleNamespace
+    from h3tp.dit_fusion import modulated_norm, modulated_norm_quantize
+    from h3tp.tp_dit import ColumnParallelLinearINT8
+    rng = np.random.default_rng(14)
+    M, hidden = 50, 1024
+    x = (rng.standard_normal((M, hidden)) * 2).astype(np.float16)
+    norm = SimpleNamespace(normalized_shape=(hidden,), eps=1e-6,
+                           weight=_t(rng.uniform(.5, 1.5, hidden).astype(np.float32), cuda_device))
+    shift = (rng.standard_normal((3, hidden)) * .1).astype(np.float32)
+    scale = (rng.standard_normal((3, hidden)) * .1).astype(np.float32)
+    segments = [(0, 20, 0), (20, 50, 2)]
+    w, s = _weights(rng, 3 * 256, hidden)
+    mod = ColumnParallelLinearINT8(hidden, w.shape[0], 0, 1, components=3, device=cuda_device)
+    mod.load_shard_from_full(torch.from_numpy(w), torch.from_numpy(s))
+    xd, sh, sc = _t(x, cuda_device), _t(shift, cuda_device), _t(scale, cuda_device)
+    with torch.no_grad():
+        q, a = modulated_norm_quantize(norm, xd, sh, sc, segments)
+        y = mod.forward_quantized(q, a)
+        h = modulated_norm(norm, xd, sh, sc, segments)
+        y_unfused = mod(h)
+    labels = np.concatenate([np.zeros(20, np.int32), np.full(30, 2, np.int32)])
+    h_ref = oracle.modulated_norm(x, _np(norm.weight), 1e-6, shift, scale, labels)
+    _eq(_np(h), h_ref)
+    ref, _ = oracle.column_linear(h_ref, w, s.ravel(), convrot=True)
+    _eq(_np(y), ref)
+    _eq(_np(y_unfused), ref)
+
+
 def test_unsupported_geometry_raises_before_launch(cuda_device):
     from h3tp import ops
     x = torch.zeros((4, 300), dtype=torch.float16, device=cuda_device)

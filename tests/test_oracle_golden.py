@@ -79,6 +79,34 @@ def test_packed_int8_transport_known_answers(oracle, pattern):
     _eq(oracle.dequantize_i32(restored, a, w, out="f32"), G[f"kat_{pattern}_int8_expected"])
 
 
+def test_modulated_norm_vs_reference_torch_path(oracle):
+    """The fused column producer's modulated RMSNorm against the reference's own torch
+    path (h3_tensor_flow.modulated_norm, F.rms_norm + segment modulation): the same
+    operations in a different summation order and with a correctly rounded rsqrt, so
+    the fp16 outputs agree to within one ulp, nearly all bit for bit."""
+    h = oracle.modulated_norm(G["norm_x"], G["norm_w"], G["norm_eps"][0], G["norm_shift"],
+                              G["norm_scale"], G["norm_labels"])
+    ref = G["norm_h"]
+    assert np.array_equal(np.sign(h.astype(np.float32)), np.sign(ref.astype(np.float32)))
+    d = np.abs(h.view(np.int16).astype(np.int32) - ref.view(np.int16).astype(np.int32))
+    assert d.max() <= 1
+    assert (d == 0).mean() >= 0.999
+
+
+def test_oracle_rsqrt_is_correctly_rounded(oracle):
+    from decimal import Decimal, getcontext
+    getcontext().prec = 60
+    rng = np.random.default_rng(3)
+    vals = np.concatenate([rng.uniform(1e-6, 1e4, 500).astype(np.float32),
+                           np.float32([1, 2, 4, 0.25, 3, 1e-38, 3e38, 1.5e-45])])
+    for v in vals:
+        y = np.float32(oracle.rsqrt_rn(float(v)))
+        t = 1 / Decimal(float(v)).sqrt()
+        best = min((np.nextafter(y, np.float32(0)), y, np.nextafter(y, np.float32(np.inf))),
+                   key=lambda c: abs(Decimal(float(c)) - t))
+        assert best == y, v
+
+
 def test_row_order_contract(oracle):
     """INT32 partial SUM, then f32 * scale * ws, then FP32 LoRA, then one fp16 store
     (benchmarks/test_fp16_fc2_experiment.py:10-30)."""
