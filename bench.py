@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--sweep", action="store_true",
                     help="BASELINE config 5 shape sweep on one GPU: one JSON line per point")
+    ap.add_argument("--max-exchange", choices=["peer", "nccl"], default="peer",
+                    help="FC2 row maxima at TP > 1: in-kernel over peer memory, or NCCL MAX")
     ap.add_argument("--payload", choices=["fp16", "int8_gather"], default="fp16",
                     help="row partial payload at TP > 1 (scaled fp16, or the packed INT8 scheme)")
     return ap.parse_args()
@@ -278,7 +280,8 @@ def run_ours(args):
     h_cpu, x_cpu = make_inputs(M, hidden)
     from h3tp.h3_operator_policy import H3OperatorPolicy
     mlp = TPDiTMLPINT8(hidden, ffn, rank, world, device=dev, comm=comm,
-                       policy=H3OperatorPolicy(row_payload=args.payload))
+                       policy=H3OperatorPolicy(row_payload=args.payload,
+                                               fc2_max_exchange=args.max_exchange))
     mlp.fc1.load_shard_from_full(w1, s1)
     mlp.fc2.load_shard_from_full(w2, s2)
     h = h_cpu.to(dev)
@@ -302,7 +305,8 @@ def run_ours(args):
         sq.row_linear(act, mlp.fc2.weight, mlp.fc2.weight_scale, comm,
                       mode=mlp.fc2.operator_policy.fc2_quantizer, scaled_transport=True,
                       residual=x, transport=mlp.fc2.operator_policy.row_transport,
-                      payload=mlp.fc2.operator_policy.row_payload)
+                      payload=mlp.fc2.operator_policy.row_payload,
+                      peer_max=mlp.fc2.operator_policy.fc2_max_exchange == "peer")
 
     with torch.no_grad():
         for _ in range(max(3, args.warmup)):
@@ -443,6 +447,7 @@ def run_ours(args):
                    "fc2_quantizer": mlp.fc2.operator_policy.fc2_quantizer,
                    "row_transport": mlp.fc2.operator_policy.row_transport,
                    "row_payload": mlp.fc2.operator_policy.row_payload,
+                   "fc2_max_exchange": mlp.fc2.operator_policy.fc2_max_exchange,
                    "l2": "inputs larger than L2 (h = 201 MB per step), no flush"},
         "roofline": {"kernel": "gemm_i8_kernel<EPI_SWIGLU> (FC1)", "bound": "tensor",
                      "achieved": round(achieved, 2), "peak": round(int8_peak, 1), "unit": "TOPS",

@@ -281,6 +281,23 @@ int h3_peer_gather(const void* const* bases, int world, int rank, int64_t flags_
                    int64_t final_off, int64_t rows, int64_t width, void* residual_f16,
                    uint32_t epoch, void* stream);
 
+/* TP>1 producer in one pass: h3_swiglu_rotate_max + the NCCL MAX all-reduce of the row
+ * maxima (tilelang_swiglu_quant.py:86-87) + h3_swiglu_rotate_quantize, with the row
+ * maxima exchanged over peer memory inside the kernel.  bases/world/rank as above;
+ * at slots_off every buffer holds u64 slots [rows][world] (zeroed before the first
+ * call, a region of their own: not the partial or final area); epoch (1, 2, 3, ...
+ * per call, the same on every rank) tags each slot.  The kernel runs a persistent
+ * grid; every rank must launch it for the same rows and width, and no kernel that
+ * waits for other ranks (a collective of another communicator) may run beside it on
+ * any rank: its CTAs could keep one of ours from becoming resident, the rule NCCL
+ * states for concurrent communicators.  Waits are bounded (2 s per CTA in total); a
+ * wait that gives up uses the local maximum and leaves H3_ERR_TIMEOUT in
+ * h3_device_error.  row_max (optional) receives the global maxima. */
+int h3_swiglu_rotate_quantize_peer(const void* x, int input_kind, int64_t rows,
+                                   int64_t width, const void* const* bases, int world,
+                                   int rank, int64_t slots_off, uint32_t epoch, int division,
+                                   int8_t* q, float* scale, float* row_max, void* stream);
+
 /* ----------------------------------------------------------------------------
  * Column linear without allocation.  No counterpart in the reference: added for
  * callers that may not allocate device memory (runtimes that budget all device

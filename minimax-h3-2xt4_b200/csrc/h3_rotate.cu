@@ -17,7 +17,65 @@
 
 namespace h3 {
 
-enum ProducerMode { MODE_MAX = 0, MODE_QUANT = 1, MODE_LOCAL = 2 };
+enum ProducerMode { MODE_MAX = 0, MODE_QUANT = 1, MODE_LOCAL = 2, MODE_PEER = 3 };
+
+// MODE_PEER: the global row maximum is exchanged inside the kernel over NVLink peer
+// memory instead of an NCCL MAX between two passes.  bases[w] is rank w's workspace
+// buffer; at slots_off each holds u64 slots [rows][world]: (epoch << 32) | max bits.
+struct PeerMax {
+  uint64_t bases[8];
+  int64_t slots_off;
+  int world, rank;
+  uint32_t epoch;
+  int* err;
+};
+
+constexpr unsigned long long PEER_TIMEOUT_NS = 2000000000ull;
+
+// Publishes this rank's maximum of `row` into every rank's slot, waits for every rank's,
+// and returns the maximum over ranks (the NCCL MAX all-reduce of the reference,
+// tilelang_swiglu_quant.py:87).  Called by every thread of the CTA.  `deadline` bounds
+// the waiting of the whole CTA: it is set at the first slot that is not ready, and once
+// it has passed every later wait gives up after one look (the local maximum is used and
+// H3_ERR_TIMEOUT is recorded).  A slot is rewritten with the next epoch only after every
+// rank has finished this launch: the row reduce that follows it waits for all ranks.
+H3_DEV float peer_row_max(const PeerMax& pm, int64_t row, float m, float* red,
+                          uint64_t& deadline) {
+  const int tid = threadIdx.x;
+  float got = m;
+  if (tid < pm.world) {
+    const unsigned long long v = ((unsigned long long)pm.epoch << 32) | __float_as_uint(m);
+    unsigned long long* slot =
+        reinterpret_cast<unsigned long long*>(pm.bases[tid] + pm.slots_off) + row * pm.world +
+        pm.rank;
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(slot), "l"(v) : "memory");
+    const unsigned long long* mine =
+        reinterpret_cast<const unsigned long long*>(pm.bases[pm.rank] + pm.slots_off) +
+        row * pm.world + tid;
+    while (true) {
+      unsigned long long w;
+      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(mine) : "memory");
+      if ((uint32_t)(w >> 32) == pm.epoch) {
+        got = __uint_as_float((uint32_t)w);
+        break;
+      }
+      uint64_t now;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+      if (deadline == 0) deadline = now + PEER_TIMEOUT_NS;
+      if (now > deadline) {
+        atomicExch(pm.err, H3_ERR_TIMEOUT);
+        break;
+      }
+      __nanosleep(64);
+    }
+    red[tid] = got;
+  }
+  __syncthreads();
+  float g = red[0];
+  for (int w = 1; w < pm.world; ++w) g = fmaxf(g, red[w]);
+  __syncthreads();
+  return g;
+}
 
 struct RowTeam {
   int threads;  // CTA size, multiple of 32
@@ -153,7 +211,7 @@ template <int KIND, int MODE, int NP>
 __global__ void __launch_bounds__(512) swiglu_rotate_kernel(
     const void* __restrict__ x, int64_t rows, int64_t width, float* __restrict__ rotated,
     float* __restrict__ row_max, const float* __restrict__ row_max_in, int division,
-    int8_t* __restrict__ q, float* __restrict__ scale_out) {
+    int8_t* __restrict__ q, float* __restrict__ scale_out, const PeerMax pm) {
   extern __shared__ f32x2 smem2[];
   const int tid = threadIdx.x;
   const int half = tid >> 4, b = tid & 15;
@@ -169,6 +227,7 @@ __global__ void __launch_bounds__(512) swiglu_rotate_kernel(
       blk[p][e] = tid + (int64_t)(2 * p + e) * blockDim.x;
       ok[p][e] = blk[p][e] < blocks;  // uniform across each half warp
     }
+  uint64_t deadline = 0;  // MODE_PEER: bound of this CTA's waiting for peers
 
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     f32x2 v[NP][16];
@@ -193,19 +252,25 @@ __global__ void __launch_bounds__(512) swiglu_rotate_kernel(
     }
     float scale = 0.0f;
     bool finite = false;
-    if (MODE == MODE_MAX || MODE == MODE_LOCAL) {
+    if (MODE == MODE_MAX || MODE == MODE_LOCAL || MODE == MODE_PEER) {
       float m = block_reduce_max_nan(m_nan, red);
       finite = m < __uint_as_float(0x7f800000u);  // false for +inf and NaN
       if (!finite) m = block_reduce_max(local_max_ignoring_nan<NP>(v, ok), red);
-      if (tid == 0) row_max[row] = m;
+      if (MODE == MODE_PEER) {
+        // The global maximum is >= every local |x|, so a finite local row (no NaN or
+        // inf) keeps the packed quantiser exact when the global maximum is finite too.
+        m = peer_row_max(pm, row, m, red, deadline);
+        finite = finite && m < __uint_as_float(0x7f800000u);
+      }
+      if (tid == 0 && row_max != nullptr) row_max[row] = m;
       scale = row_scale_from_max(m);
     } else {
       scale = row_scale_from_max(__ldg(row_max_in + row));
     }
-    if (MODE == MODE_QUANT || MODE == MODE_LOCAL) {
+    if (MODE == MODE_QUANT || MODE == MODE_LOCAL || MODE == MODE_PEER) {
       const float inv = __fdiv_rn(1.0f, scale);
       // MODE_QUANT's maximum comes from outside and may be below |x|: scalar path
-      quantize_store<NP>(v, ok, blk, MODE == MODE_LOCAL && finite, scale, inv, division,
+      quantize_store<NP>(v, ok, blk, MODE != MODE_QUANT && finite, scale, inv, division,
                          q + row * width);
       if (tid == 0) scale_out[row] = scale;
     }
@@ -424,44 +489,56 @@ static bool allow_smem(K kernel, size_t smem, bool& done) {
 template <int KIND, int MODE, int NP>
 static int launch_producer_np(const void* x, int64_t rows, int64_t width, float* rotated,
                               float* row_max, const float* row_max_in, int division, int8_t* q,
-                              float* scale, int threads, cudaStream_t stream) {
+                              float* scale, int threads, cudaStream_t stream,
+                              const PeerMax& pm) {
   static bool smem_set = false;
   const size_t smem = producer_smem(threads);
   if (!allow_smem(swiglu_rotate_kernel<KIND, MODE, NP>, smem, smem_set)) return H3_ERR_CUDA;
-  const int grid = (int)std::min<int64_t>(rows, 1 << 20);
+  int grid = (int)std::min<int64_t>(rows, 1 << 20);
+  if (MODE == MODE_PEER) {
+    // Persistent: every CTA resident, the same row schedule on every rank, so the CTA
+    // that waits for a peer's row maximum never waits for a CTA that cannot run.
+    int per_sm = 0, dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &per_sm, swiglu_rotate_kernel<KIND, MODE, NP>, threads, smem) != cudaSuccess ||
+        per_sm < 1)
+      return H3_ERR_CUDA;
+    grid = (int)std::min<int64_t>(rows, (int64_t)per_sm * h3host::sm_count(dev));
+  }
   swiglu_rotate_kernel<KIND, MODE, NP><<<grid, threads, smem, stream>>>(
-      x, rows, width, rotated, row_max, row_max_in, division, q, scale);
+      x, rows, width, rotated, row_max, row_max_in, division, q, scale, pm);
   return h3host::check_launch();
 }
 
 template <int KIND, int MODE>
 static int launch_producer(const void* x, int64_t rows, int64_t width, float* rotated,
                            float* row_max, const float* row_max_in, int division, int8_t* q,
-                           float* scale, cudaStream_t stream) {
+                           float* scale, cudaStream_t stream, const PeerMax& pm = PeerMax{}) {
   const RowTeam t = row_team(width);
   if (t.nb == 1)
     return launch_producer_np<KIND, MODE, 1>(x, rows, width, rotated, row_max, row_max_in,
-                                             division, q, scale, t.threads, stream);
+                                             division, q, scale, t.threads, stream, pm);
   if (t.nb == 2)
     return launch_producer_np<KIND, MODE, 2>(x, rows, width, rotated, row_max, row_max_in,
-                                             division, q, scale, t.threads, stream);
+                                             division, q, scale, t.threads, stream, pm);
   return H3_ERR_INVALID;
 }
 
 template <int MODE>
 static int dispatch_kind(int kind, const void* x, int64_t rows, int64_t width, float* rotated,
                          float* row_max, const float* row_max_in, int division, int8_t* q,
-                         float* scale, cudaStream_t stream) {
+                         float* scale, cudaStream_t stream, const PeerMax& pm = PeerMax{}) {
   switch (kind) {
     case H3_IN_GATEUP_F16:
       return launch_producer<H3_IN_GATEUP_F16, MODE>(x, rows, width, rotated, row_max,
-                                                     row_max_in, division, q, scale, stream);
+                                                     row_max_in, division, q, scale, stream, pm);
     case H3_IN_ACT_F32:
       return launch_producer<H3_IN_ACT_F32, MODE>(x, rows, width, rotated, row_max,
-                                                  row_max_in, division, q, scale, stream);
+                                                  row_max_in, division, q, scale, stream, pm);
     case H3_IN_ACT_F16:
       return launch_producer<H3_IN_ACT_F16, MODE>(x, rows, width, rotated, row_max,
-                                                  row_max_in, division, q, scale, stream);
+                                                  row_max_in, division, q, scale, stream, pm);
     default:
       return H3_ERR_INVALID;
   }
@@ -517,6 +594,34 @@ extern "C" int h3_swiglu_rotate_quantize_local(const void* x, int input_kind, in
   if (int s = h3host::bind_device_of(x, &dev)) return s;
   return dispatch_kind<MODE_LOCAL>(input_kind, x, rows, width, nullptr, row_max, nullptr,
                                    division, q, scale, (cudaStream_t)stream);
+}
+
+extern "C" int h3_swiglu_rotate_quantize_peer(const void* x, int input_kind, int64_t rows,
+                                              int64_t width, const void* const* bases, int world,
+                                              int rank, int64_t slots_off, uint32_t epoch,
+                                              int division, int8_t* q, float* scale,
+                                              float* row_max, void* stream) {
+  if (!producer_geometry_ok(x, input_kind, rows, width) || q == nullptr || scale == nullptr ||
+      !h3host::aligned(q, 16) || (division != H3_DIV_RN && division != H3_DIV_FAST) ||
+      bases == nullptr || (world != 2 && world != 4 && world != 8) || rank < 0 ||
+      rank >= world || slots_off < 0 || slots_off % 8 != 0 || epoch == 0)
+    return H3_ERR_INVALID;
+  PeerMax pm{};
+  for (int w = 0; w < world; ++w) {
+    if (bases[w] == nullptr || !h3host::aligned(bases[w], 16)) return H3_ERR_INVALID;
+    pm.bases[w] = reinterpret_cast<uint64_t>(bases[w]);
+  }
+  if (rows == 0) return H3_OK;
+  int dev;
+  if (int s = h3host::bind_device_of(x, &dev)) return s;
+  pm.slots_off = slots_off;
+  pm.world = world;
+  pm.rank = rank;
+  pm.epoch = epoch;
+  pm.err = h3host::error_word(dev);
+  if (pm.err == nullptr) return H3_ERR_CUDA;
+  return dispatch_kind<MODE_PEER>(input_kind, x, rows, width, nullptr, row_max, nullptr,
+                                  division, q, scale, (cudaStream_t)stream, pm);
 }
 
 extern "C" int h3_column_quantize(const void* x_f16, int64_t rows, int64_t k, int convrot,

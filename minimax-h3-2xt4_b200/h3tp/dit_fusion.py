@@ -159,7 +159,8 @@ def row_gated(module, value, residual, gate, segments, comm, input_act=None):
         return row_linear(value, module.weight, ws, comm, mode=policy.fc2_quantizer,
                           scaled_transport=scaled, consume_input=consume, residual=residual,
                           gate=gate, labels=labels, transport=transport, division=division,
-                          payload=payload)
+                          payload=payload,
+                          peer_max=getattr(policy, "fc2_max_exchange", "peer") == "peer")
     if value.dtype not in (torch.float16, torch.float32) or value.shape[1] != kl:
         return None
     from .row_quant import global_row_quantize

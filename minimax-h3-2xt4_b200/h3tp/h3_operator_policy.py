@@ -14,6 +14,10 @@ New B200 fields:
                   or 'allreduce' (NCCL fp16 SUM, the reference's form).  All three give
                   the same bits; 'p2p' needs a torch.distributed NCCL group and the
                   residual form of the row output, and uses 'rowblock' otherwise.
+  fc2_max_exchange 'peer' (default: under 'p2p' the FC2 producer exchanges its row
+                  maxima over the peer workspace inside the kernel, one pass instead
+                  of two and an NCCL MAX) or 'nccl' (the reference's MAX all-reduce
+                  between the two passes).  Same codes either way.
   row_payload     'fp16' (the scaled-FP16 partials, default) or 'int8_gather' (the
                   reference's packed INT8 group-128 payload,
                   tilelang_transport_tradeoffs.py:40-88), with any row_transport
@@ -47,6 +51,7 @@ class H3OperatorPolicy:
     dit_p0_c_local_rotation: bool = True
     row_transport: str = "p2p"
     row_payload: str = "fp16"
+    fc2_max_exchange: str = "peer"
     quant_division: str = "rn"
     fc1_swiglu_epilogue: bool = True
 
@@ -66,6 +71,8 @@ class H3OperatorPolicy:
             raise ValueError("Unknown row transport")
         if self.row_payload not in ("fp16", "int8_gather"):
             raise ValueError("Unknown row payload")
+        if self.fc2_max_exchange not in ("peer", "nccl"):
+            raise ValueError("Unknown FC2 maximum exchange")
         if self.quant_division not in ("rn", "fast"):
             raise ValueError("Unknown quantizer division")
 
@@ -116,7 +123,8 @@ def row_linear(module, x, fallback, comm, input_act=None):
                                     mode=policy.fc2_quantizer,
                                     scaled_transport=policy.scaled_transport,
                                     transport=policy.row_transport, division=division,
-                                    payload=policy.row_payload)
+                                    payload=policy.row_payload,
+                                    peer_max=policy.fc2_max_exchange == "peer")
         _fallback("FC2 fused quantizer", str(x.device), None)
     if input_act is None and x.shape[-1] % 256 == 0 and module.convrot_groupsize == 256:
         # O projection: local ConvRot of owned groups, global row max, quantise.

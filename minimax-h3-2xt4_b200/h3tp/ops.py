@@ -200,6 +200,22 @@ def swiglu_rotate_quantize_local(x, kind="gateup_f16", division="rn"):
     return q, s, m
 
 
+def swiglu_rotate_quantize_peer(x, bases, world: int, rank: int, slots_off: int, epoch: int,
+                                kind="gateup_f16", division="rn", want_max=False):
+    """TP>1 single pass (h3_swiglu_rotate_quantize_peer): the row maxima are exchanged
+    with the other ranks over peer memory inside the kernel.  Returns (q, scale [M, 1],
+    row_max [M, 1] of the global maxima or None)."""
+    x, k, M, W = _producer_input(x, kind)
+    q = torch.empty((M, W), dtype=torch.int8, device=x.device)
+    s = torch.empty((M, 1), dtype=torch.float32, device=x.device)
+    m = torch.empty((M, 1), dtype=torch.float32, device=x.device) if want_max else None
+    arr = (ctypes.c_void_p * world)(*bases)
+    N.call("h3_swiglu_rotate_quantize_peer", x.data_ptr(), k, M, W, arr, world, rank,
+           int(slots_off), int(epoch), DIVISIONS[division], q.data_ptr(), s.data_ptr(), _ptr(m),
+           _stream(x))
+    return q, s, m
+
+
 def row_quantize(rotated, row_max, width=None, start=0, division="rn"):
     """tilelang_row_quant.quantize: codes of rotated[:, start:start+width]."""
     rotated = _need(rotated, torch.float32, "rotated", 2)

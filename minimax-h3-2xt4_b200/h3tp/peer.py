@@ -50,7 +50,8 @@ def available(comm) -> bool:
 
 class PeerWorkspace:
     """One symmetric buffer per rank: flags | partial [rows][width] fp16 | final rows
-    [rows][width] fp16, for up to `rows` rows of `width` columns."""
+    [rows][width] fp16 | row-maximum slots u64 [rows][8], for up to `rows` rows of
+    `width` columns."""
 
     def __init__(self, group, device: torch.device, width: int, rows: int):
         import torch.distributed._symmetric_memory as symm
@@ -62,16 +63,20 @@ class PeerWorkspace:
         region = -(-self.capacity * self.width * 2 // _ALIGN) * _ALIGN
         self.partial_off = FLAGS_BYTES
         self.final_off = FLAGS_BYTES + region
-        nbytes = FLAGS_BYTES + 2 * region
+        self.slots_off = FLAGS_BYTES + 2 * region
+        slots = -(-self.capacity * 8 * 8 // _ALIGN) * _ALIGN
+        nbytes = self.slots_off + slots
         with torch.cuda.device(self.device):
             self.buf = symm.empty(nbytes, dtype=torch.uint8, device=self.device)
             self.buf[:FLAGS_BYTES].zero_()
+            self.buf[self.slots_off:].zero_()
             self.handle = symm.rendezvous(self.buf, _group_name(group))
             torch.cuda.synchronize(self.device)
         self.world = int(self.handle.world_size)
         self.rank = int(self.handle.rank)
         self.bases = [int(p) for p in self.handle.buffer_ptrs]
         self.epoch = 0
+        self.max_epoch = 0
         # every rank's flags are zero before any rank signals
         dist.barrier(group=group if isinstance(group, dist.ProcessGroup) else None)
 
@@ -85,6 +90,21 @@ class PeerWorkspace:
         """The same area as a packed INT8 payload, uint8 [rows, width/128*132]."""
         pitch = ops.pack8_pitch(self.width)
         return self.buf[self.partial_off:self.partial_off + rows * pitch].view(rows, pitch)
+
+    def quantize_rows(self, x, kind: str = "gateup_f16", division: str = "rn"):
+        """The FC2 producer with the row maxima exchanged in the kernel
+        (ops.swiglu_rotate_quantize_peer): returns (codes, row scale [M, 1]).  Every
+        rank calls it with the same rows and width, in the same order as its other
+        workspace calls; a slot is rewritten only after the reduce that follows has
+        synchronised the ranks."""
+        rows = x.shape[0]
+        if rows > self.capacity:
+            raise ValueError(f"{rows} rows exceed the workspace capacity {self.capacity}")
+        self.max_epoch += 1
+        q, s, _ = ops.swiglu_rotate_quantize_peer(x, self.bases, self.world, self.rank,
+                                                  self.slots_off, self.max_epoch, kind=kind,
+                                                  division=division)
+        return q, s
 
     def reduce_and_gather(self, rows: int, shift: int, row_scale, weight_scale, residual,
                           gate=None, labels=None, packed: bool = False):

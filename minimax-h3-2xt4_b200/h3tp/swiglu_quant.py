@@ -46,9 +46,13 @@ def input_kind(x: torch.Tensor, local_k: int | None = None) -> tuple[str, int]:
 
 
 def prepare(x: torch.Tensor, comm, mode: str = "fused_stored", *, consume_input: bool = False,
-            division: str = "rn", local_k: int | None = None):
+            division: str = "rn", local_k: int | None = None, peer_workspace=None):
     """SwiGLU + ConvRot + global row quantisation (tilelang_swiglu_quant.py:67-92).
-    Returns (q int8 [M, Kl], scale fp32 [M, 1])."""
+    Returns (q int8 [M, Kl], scale fp32 [M, 1]).
+
+    With `peer_workspace` (a peer.PeerWorkspace of this group) and TP>1, one kernel
+    rotates, exchanges the row maxima with the other ranks over peer memory and
+    quantises: the same codes as either mode, one pass over x."""
     if mode not in MODES:
         raise ValueError(mode)
     kind, kl = input_kind(x, local_k)
@@ -58,6 +62,11 @@ def prepare(x: torch.Tensor, comm, mode: str = "fused_stored", *, consume_input:
     flat = x.reshape(-1, x.shape[-1]).contiguous()
     if C.world_of(comm) == 1:
         q, s, _ = ops.swiglu_rotate_quantize_local(flat, kind, division)
+        if consume_input:
+            x.set_()
+        return q, s
+    if peer_workspace is not None:
+        q, s = peer_workspace.quantize_rows(flat, kind, division)
         if consume_input:
             x.set_()
         return q, s
@@ -152,20 +161,29 @@ def _finish_quantized(q, scale, weight, weight_scale, comm, scaled_transport=Tru
 def row_linear(x, weight, weight_scale, comm, *, mode="fused_stored", scaled_transport=True,
                finish_fn=None, consume_input=False, p0_b=False, residual=None, gate=None,
                labels=None, transport="rowblock", division="rn", out_dtype=torch.float32,
-               payload="fp16"):
+               payload="fp16", peer_max=True):
     """FC2 row linear (tilelang_swiglu_quant.py:108-128).
 
     Returns FP32 [..., N] (the caller adds LoRA, then stores once), or with
     `residual` the gated residual updated in place.  finish_fn keeps the reference's
     callback form: it receives the all-reduced fp16 payload.
     p0_b (the T4 in-place storage trick) is accepted and ignored: on B200 the FP32
-    SwiGLU lives in the FC1 epilogue's own output instead."""
+    SwiGLU lives in the FC1 epilogue's own output instead.
+    With the p2p transport (residual form, NCCL group) the row maxima are exchanged in
+    the producer kernel over the same peer workspace unless peer_max is False; the
+    peer reduce that follows synchronises the ranks before the slots are reused."""
     if finish_fn is not None and not scaled_transport:
         raise ValueError("Fused row-gate requires scaled FP16 transport")
     shape = x.shape
+    ws = None
+    if (peer_max and transport == "p2p" and scaled_transport and finish_fn is None
+            and residual is not None and residual.is_contiguous()
+            and (payload == "int8_gather" or residual.shape[-1] % 8 == 0)
+            and C.world_of(comm) > 1 and P.available(comm)):
+        ws = P.workspace(comm, x.device, weight.shape[0], x.numel() // x.shape[-1])
     with label("fp32_swiglu_convrot_quantize"):
         q, scale = prepare(x, comm, mode, consume_input=consume_input, division=division,
-                           local_k=weight.shape[1])
+                           local_k=weight.shape[1], peer_workspace=ws)
     del x
     out = _finish_quantized(q, scale, weight, weight_scale.reshape(-1), comm, scaled_transport,
                             transport, residual=residual, gate=gate, labels=labels,

@@ -165,3 +165,82 @@ def test_peer_rejects_bad_geometry(cuda_device):
     with pytest.raises(ValueError):   # width not a multiple of 8
         ops.peer_gather(bases, 2, 0, 0, foff, 4, 252, torch.zeros((4, 252), dtype=torch.float16,
                                                                    device=dev))
+
+
+# ----------------------------------------------------------------------------
+# FC2 producer with the row maxima exchanged over peer memory
+# ----------------------------------------------------------------------------
+def _producer_input(rng, kind, rows, width, special):
+    if kind == "gateup_f16":
+        g = rng.standard_normal((rows, width)).astype(np.float32)
+        u = rng.standard_normal((rows, width)).astype(np.float32)
+        g[::5] *= 40.0  # gates past the packed SiLU's range
+        x = [g, u]
+    else:
+        x = [(rng.standard_normal((rows, width)) * 0.7).astype(np.float32)]
+    if special:  # a NaN row, an inf row, a zero row
+        x[0][0, 5] = np.nan
+        x[0][1, 7] = np.inf
+        x[0][2, :] = 0.0
+    dtype = np.float32 if kind == "act_f32" else np.float16
+    return np.concatenate(x, 1).astype(dtype)
+
+
+def _slots(maxima, epoch):
+    """u64 slots [rows][world] = (epoch << 32) | float bits, as every rank publishes."""
+    bits = np.stack(maxima, 1).astype(np.float32).view(np.uint32).astype(np.uint64)
+    return ((np.uint64(epoch) << np.uint64(32)) | bits).view(np.int64)
+
+
+@pytest.mark.parametrize("world,rows,width,kind", [(2, 37, 1024, "gateup_f16"),
+                                                   (4, 300, 7168, "act_f32"),
+                                                   (8, 64, 2048, "act_f16")])
+def test_peer_producer_bit_exact(cuda_device, oracle, world, rows, width, kind):
+    """Each emulated rank's slots hold every rank's row maximum (the oracle's) before
+    its kernel runs, so no kernel waits for another; the codes and scales must equal
+    the oracle's quantisation with the maximum over ranks, for two epochs in a row."""
+    from h3tp import _native, ops
+    rng = np.random.default_rng(world * 7 + width)
+    xs = [_producer_input(rng, kind, rows, width, special=(r == 0)) for r in range(world)]
+    rot = [oracle.fc2_rotate(x, kind) for x in xs]
+    gmax = np.max(np.stack([m for _, m in rot]), 0)
+    dev = cuda_device
+    bufs = [torch.zeros(256 + rows * world * 8, dtype=torch.uint8, device=dev)
+            for _ in range(world)]
+    bases = [b.data_ptr() for b in bufs]
+    xd = [torch.from_numpy(x).to(dev) for x in xs]
+    for epoch in (1, 2):
+        slots = torch.from_numpy(_slots([m for _, m in rot], epoch)).to(dev)
+        for b in bufs:
+            b[256:].view(torch.int64).view(rows, world).copy_(slots)
+        for r in range(world):
+            q, s, m = ops.swiglu_rotate_quantize_peer(xd[r], bases, world, r, 256, epoch, kind,
+                                                      want_max=True)
+            q_ref, s_ref = oracle.row_quantize(rot[r][0], gmax)
+            got = q.cpu().numpy()
+            assert np.array_equal(got, q_ref), f"rank {r} epoch {epoch}"
+            assert np.array_equal(s.cpu().numpy().ravel().view(np.uint32), s_ref.view(np.uint32))
+            assert np.array_equal(m.cpu().numpy().ravel().view(np.uint32), gmax.view(np.uint32))
+    assert _native.device_error(dev.index or 0) == 0
+
+
+def test_peer_producer_wait_gives_up(cuda_device, oracle):
+    """Rank 1 never publishes: rank 0's CTAs give up after their bounded wait, record
+    H3_ERR_TIMEOUT and quantise with the local maxima."""
+    from h3tp import _native, ops
+    dev = cuda_device
+    rows, width = 6, 512
+    x = _producer_input(np.random.default_rng(3), "gateup_f16", rows, width, special=False)
+    R, m_loc = oracle.fc2_rotate(x, "gateup_f16")
+    bufs = [torch.zeros(256 + rows * 2 * 8, dtype=torch.uint8, device=dev) for _ in range(2)]
+    assert _native.device_error(dev.index or 0) == 0
+    q, s, _ = ops.swiglu_rotate_quantize_peer(torch.from_numpy(x).to(dev),
+                                              [b.data_ptr() for b in bufs], 2, 0, 256, 1)
+    torch.cuda.synchronize()
+    assert _native.device_error(dev.index or 0) == _native.H3_ERR_TIMEOUT
+    q_ref, s_ref = oracle.row_quantize(R, m_loc)
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    # rank 0 published its maxima into rank 1's slots
+    pub = bufs[1][256:].view(torch.int64).view(rows, 2)[:, 0].cpu().numpy().view(np.uint64)
+    assert (pub >> np.uint64(32) == 1).all()
+    assert np.array_equal((pub & np.uint64(0xffffffff)).astype(np.uint32), m_loc.view(np.uint32))
