@@ -17,11 +17,14 @@
 
 namespace h3 {
 
-enum ProducerMode { MODE_MAX = 0, MODE_QUANT = 1, MODE_LOCAL = 2, MODE_PEER = 3 };
+enum ProducerMode { MODE_MAX = 0, MODE_QUANT = 1, MODE_LOCAL = 2 };
 
-// MODE_PEER: the global row maximum is exchanged inside the kernel over NVLink peer
-// memory instead of an NCCL MAX between two passes.  bases[w] is rank w's workspace
-// buffer; at slots_off each holds u64 slots [rows][world]: (epoch << 32) | max bits.
+// Row-maximum exchange over NVLink peer memory, for the TP>1 producer in one pass
+// (it replaces the NCCL MAX all-reduce between the two passes of the reference,
+// tilelang_swiglu_quant.py:86-87).  bases[w] is rank w's workspace buffer; at slots_off
+// each holds u64 slots [rows][world] = (epoch << 32) | max bits.  Value and tag share
+// one aligned 64-bit word, so relaxed system-scope accesses suffice: nothing else is
+// ordered by a slot.
 struct PeerMax {
   uint64_t bases[8];
   int64_t slots_off;
@@ -32,29 +35,35 @@ struct PeerMax {
 
 constexpr unsigned long long PEER_TIMEOUT_NS = 2000000000ull;
 
-// Publishes this rank's maximum of `row` into every rank's slot, waits for every rank's,
-// and returns the maximum over ranks (the NCCL MAX all-reduce of the reference,
-// tilelang_swiglu_quant.py:87).  Called by every thread of the CTA.  `deadline` bounds
-// the waiting of the whole CTA: it is set at the first slot that is not ready, and once
-// it has passed every later wait gives up after one look (the local maximum is used and
-// H3_ERR_TIMEOUT is recorded).  A slot is rewritten with the next epoch only after every
-// rank has finished this launch: the row reduce that follows it waits for all ranks.
-H3_DEV float peer_row_max(const PeerMax& pm, int64_t row, float m, float* red,
-                          uint64_t& deadline) {
+// This rank's maximum of `row` into slot [row][rank] of every rank (threads < world).
+H3_DEV void peer_publish(const PeerMax& pm, int64_t row, float m) {
   const int tid = threadIdx.x;
-  float got = m;
   if (tid < pm.world) {
     const unsigned long long v = ((unsigned long long)pm.epoch << 32) | __float_as_uint(m);
     unsigned long long* slot =
         reinterpret_cast<unsigned long long*>(pm.bases[tid] + pm.slots_off) + row * pm.world +
         pm.rank;
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(slot), "l"(v) : "memory");
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(slot), "l"(v) : "memory");
+  }
+}
+
+// Maximum over ranks of `row`, read from this rank's slots (called by every thread).
+// `deadline` bounds the waiting of the whole CTA: it is set at the first slot that is
+// not ready; once it has passed, every later wait gives up after one look, the rank's
+// own maximum `m` stands in for the missing ones and H3_ERR_TIMEOUT is recorded.  A
+// slot is rewritten with the next epoch only after every rank has finished this
+// launch, since the row reduce that follows it waits for all ranks.
+H3_DEV float peer_wait(const PeerMax& pm, int64_t row, float m, float* red,
+                       uint64_t& deadline) {
+  const int tid = threadIdx.x;
+  if (tid < pm.world) {
     const unsigned long long* mine =
         reinterpret_cast<const unsigned long long*>(pm.bases[pm.rank] + pm.slots_off) +
         row * pm.world + tid;
+    float got = m;
     while (true) {
       unsigned long long w;
-      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(mine) : "memory");
+      asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(mine) : "memory");
       if ((uint32_t)(w >> 32) == pm.epoch) {
         got = __uint_as_float((uint32_t)w);
         break;
@@ -66,7 +75,7 @@ H3_DEV float peer_row_max(const PeerMax& pm, int64_t row, float m, float* red,
         atomicExch(pm.err, H3_ERR_TIMEOUT);
         break;
       }
-      __nanosleep(64);
+      __nanosleep(32);
     }
     red[tid] = got;
   }
@@ -211,7 +220,7 @@ template <int KIND, int MODE, int NP>
 __global__ void __launch_bounds__(512) swiglu_rotate_kernel(
     const void* __restrict__ x, int64_t rows, int64_t width, float* __restrict__ rotated,
     float* __restrict__ row_max, const float* __restrict__ row_max_in, int division,
-    int8_t* __restrict__ q, float* __restrict__ scale_out, const PeerMax pm) {
+    int8_t* __restrict__ q, float* __restrict__ scale_out) {
   extern __shared__ f32x2 smem2[];
   const int tid = threadIdx.x;
   const int half = tid >> 4, b = tid & 15;
@@ -227,7 +236,6 @@ __global__ void __launch_bounds__(512) swiglu_rotate_kernel(
       blk[p][e] = tid + (int64_t)(2 * p + e) * blockDim.x;
       ok[p][e] = blk[p][e] < blocks;  // uniform across each half warp
     }
-  uint64_t deadline = 0;  // MODE_PEER: bound of this CTA's waiting for peers
 
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     f32x2 v[NP][16];
@@ -252,28 +260,108 @@ __global__ void __launch_bounds__(512) swiglu_rotate_kernel(
     }
     float scale = 0.0f;
     bool finite = false;
-    if (MODE == MODE_MAX || MODE == MODE_LOCAL || MODE == MODE_PEER) {
+    if (MODE == MODE_MAX || MODE == MODE_LOCAL) {
       float m = block_reduce_max_nan(m_nan, red);
       finite = m < __uint_as_float(0x7f800000u);  // false for +inf and NaN
       if (!finite) m = block_reduce_max(local_max_ignoring_nan<NP>(v, ok), red);
-      if (MODE == MODE_PEER) {
-        // The global maximum is >= every local |x|, so a finite local row (no NaN or
-        // inf) keeps the packed quantiser exact when the global maximum is finite too.
-        m = peer_row_max(pm, row, m, red, deadline);
-        finite = finite && m < __uint_as_float(0x7f800000u);
-      }
-      if (tid == 0 && row_max != nullptr) row_max[row] = m;
+      if (tid == 0) row_max[row] = m;
       scale = row_scale_from_max(m);
     } else {
       scale = row_scale_from_max(__ldg(row_max_in + row));
     }
-    if (MODE == MODE_QUANT || MODE == MODE_LOCAL || MODE == MODE_PEER) {
+    if (MODE == MODE_QUANT || MODE == MODE_LOCAL) {
       const float inv = __fdiv_rn(1.0f, scale);
       // MODE_QUANT's maximum comes from outside and may be below |x|: scalar path
-      quantize_store<NP>(v, ok, blk, MODE != MODE_QUANT && finite, scale, inv, division,
+      quantize_store<NP>(v, ok, blk, MODE == MODE_LOCAL && finite, scale, inv, division,
                          q + row * width);
       if (tid == 0) scale_out[row] = scale;
     }
+  }
+}
+
+// FC2 producer at TP>1 in one pass.  The row loop is pipelined by one row: a CTA
+// rotates row i, publishes its local maximum to every rank, stashes the rotated values
+// in shared memory, and only then waits for the global maximum of its previous row and
+// quantises that row from the stash, so the NVLink round trip of a maximum overlaps
+// the next row's loads and rotation.  Each thread reads back only what it stashed, so
+// the stash needs no barrier; two stash buffers alternate between rows.  Launched as a
+// persistent grid (every CTA resident), so a CTA waiting for a peer's row never waits
+// for a CTA that cannot run.
+template <int KIND, int NP>
+__global__ void __launch_bounds__(512) swiglu_rotate_peer_kernel(
+    const void* __restrict__ x, int64_t rows, int64_t width, float* __restrict__ row_max,
+    int division, int8_t* __restrict__ q, float* __restrict__ scale_out, const PeerMax pm) {
+  extern __shared__ f32x2 smem2[];
+  const int tid = threadIdx.x;
+  const int T = blockDim.x;
+  const int half = tid >> 4, b = tid & 15;
+  f32x2* tile = smem2 + half * (16 * 17);
+  float* red = reinterpret_cast<float*>(smem2 + (T / 16) * (16 * 17));
+  f32x2* stash = reinterpret_cast<f32x2*>(red + 32);  // [2][NP * 16][T]
+  const int64_t blocks = width / 16;
+  int64_t blk[NP][2];
+  bool ok[NP][2];
+#pragma unroll
+  for (int p = 0; p < NP; ++p)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      blk[p][e] = tid + (int64_t)(2 * p + e) * T;
+      ok[p][e] = blk[p][e] < blocks;
+    }
+  uint64_t deadline = 0;
+  int64_t prev = -1;
+  bool prev_finite = false;
+  float prev_local = 0.0f;
+  int buf = 0;
+
+  for (int64_t row = blockIdx.x;; row += gridDim.x) {
+    const bool have = row < rows;
+    bool finite = false;
+    float m = 0.0f;
+    if (have) {
+      f32x2 v[NP][16];
+      float m_nan = 0.0f;
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        load_activation2<KIND>(x, row, width, blk[p][0], blk[p][1], ok[p][0], ok[p][1], v[p]);
+        convrot256_halfwarp2(v[p], tile, b);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) m_nan = max_abs2_nan(m_nan, lo2(v[p][i]), hi2(v[p][i]));
+      }
+      m = block_reduce_max_nan(m_nan, red);
+      finite = m < __uint_as_float(0x7f800000u);  // false for +inf and NaN
+      if (!finite) m = block_reduce_max(local_max_ignoring_nan<NP>(v, ok), red);
+      peer_publish(pm, row, m);
+      f32x2* st = stash + (size_t)buf * NP * 16 * T;
+#pragma unroll
+      for (int p = 0; p < NP; ++p)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) st[(p * 16 + i) * T + tid] = v[p][i];
+    }
+    if (prev >= 0) {
+      const float g = peer_wait(pm, prev, prev_local, red, deadline);
+      // g >= every local |x|: a finite local row keeps the packed quantiser exact when
+      // the global maximum is finite too
+      const bool fin = prev_finite && g < __uint_as_float(0x7f800000u);
+      const float scale = row_scale_from_max(g);
+      const float inv = __fdiv_rn(1.0f, scale);
+      const f32x2* st = stash + (size_t)(buf ^ 1) * NP * 16 * T;
+      f32x2 w[NP][16];
+#pragma unroll
+      for (int p = 0; p < NP; ++p)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w[p][i] = st[(p * 16 + i) * T + tid];
+      quantize_store<NP>(w, ok, blk, fin, scale, inv, division, q + prev * width);
+      if (tid == 0) {
+        scale_out[prev] = scale;
+        if (row_max != nullptr) row_max[prev] = g;
+      }
+    }
+    if (!have) break;
+    prev = row;
+    prev_finite = finite;
+    prev_local = m;
+    buf ^= 1;
   }
 }
 
@@ -489,59 +577,81 @@ static bool allow_smem(K kernel, size_t smem, bool& done) {
 template <int KIND, int MODE, int NP>
 static int launch_producer_np(const void* x, int64_t rows, int64_t width, float* rotated,
                               float* row_max, const float* row_max_in, int division, int8_t* q,
-                              float* scale, int threads, cudaStream_t stream,
-                              const PeerMax& pm) {
+                              float* scale, int threads, cudaStream_t stream) {
   static bool smem_set = false;
   const size_t smem = producer_smem(threads);
   if (!allow_smem(swiglu_rotate_kernel<KIND, MODE, NP>, smem, smem_set)) return H3_ERR_CUDA;
-  int grid = (int)std::min<int64_t>(rows, 1 << 20);
-  if (MODE == MODE_PEER) {
-    // Persistent: every CTA resident, the same row schedule on every rank, so the CTA
-    // that waits for a peer's row maximum never waits for a CTA that cannot run.
-    int per_sm = 0, dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-            &per_sm, swiglu_rotate_kernel<KIND, MODE, NP>, threads, smem) != cudaSuccess ||
-        per_sm < 1)
-      return H3_ERR_CUDA;
-    grid = (int)std::min<int64_t>(rows, (int64_t)per_sm * h3host::sm_count(dev));
-  }
+  const int grid = (int)std::min<int64_t>(rows, 1 << 20);
   swiglu_rotate_kernel<KIND, MODE, NP><<<grid, threads, smem, stream>>>(
-      x, rows, width, rotated, row_max, row_max_in, division, q, scale, pm);
+      x, rows, width, rotated, row_max, row_max_in, division, q, scale);
   return h3host::check_launch();
 }
 
 template <int KIND, int MODE>
 static int launch_producer(const void* x, int64_t rows, int64_t width, float* rotated,
                            float* row_max, const float* row_max_in, int division, int8_t* q,
-                           float* scale, cudaStream_t stream, const PeerMax& pm = PeerMax{}) {
+                           float* scale, cudaStream_t stream) {
   const RowTeam t = row_team(width);
   if (t.nb == 1)
     return launch_producer_np<KIND, MODE, 1>(x, rows, width, rotated, row_max, row_max_in,
-                                             division, q, scale, t.threads, stream, pm);
+                                             division, q, scale, t.threads, stream);
   if (t.nb == 2)
     return launch_producer_np<KIND, MODE, 2>(x, rows, width, rotated, row_max, row_max_in,
-                                             division, q, scale, t.threads, stream, pm);
+                                             division, q, scale, t.threads, stream);
   return H3_ERR_INVALID;
 }
 
 template <int MODE>
 static int dispatch_kind(int kind, const void* x, int64_t rows, int64_t width, float* rotated,
                          float* row_max, const float* row_max_in, int division, int8_t* q,
-                         float* scale, cudaStream_t stream, const PeerMax& pm = PeerMax{}) {
+                         float* scale, cudaStream_t stream) {
   switch (kind) {
     case H3_IN_GATEUP_F16:
       return launch_producer<H3_IN_GATEUP_F16, MODE>(x, rows, width, rotated, row_max,
-                                                     row_max_in, division, q, scale, stream, pm);
+                                                     row_max_in, division, q, scale, stream);
     case H3_IN_ACT_F32:
       return launch_producer<H3_IN_ACT_F32, MODE>(x, rows, width, rotated, row_max,
-                                                  row_max_in, division, q, scale, stream, pm);
+                                                  row_max_in, division, q, scale, stream);
     case H3_IN_ACT_F16:
       return launch_producer<H3_IN_ACT_F16, MODE>(x, rows, width, rotated, row_max,
-                                                  row_max_in, division, q, scale, stream, pm);
+                                                  row_max_in, division, q, scale, stream);
     default:
       return H3_ERR_INVALID;
   }
+}
+
+// The peer producer's shared memory: the producer's plus two stashes of one row.
+static size_t peer_producer_smem(int threads, int np) {
+  return producer_smem(threads) + 2 * (size_t)np * 16 * threads * sizeof(unsigned long long);
+}
+
+template <int KIND, int NP>
+static int launch_peer_np(const void* x, int64_t rows, int64_t width, float* row_max,
+                          int division, int8_t* q, float* scale, int threads,
+                          const PeerMax& pm, cudaStream_t stream) {
+  static bool smem_set = false;
+  const size_t smem = peer_producer_smem(threads, NP);
+  if (!allow_smem(swiglu_rotate_peer_kernel<KIND, NP>, smem, smem_set)) return H3_ERR_CUDA;
+  int per_sm = 0, dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+          &per_sm, swiglu_rotate_peer_kernel<KIND, NP>, threads, smem) != cudaSuccess ||
+      per_sm < 1)
+    return H3_ERR_CUDA;
+  const int grid = (int)std::min<int64_t>(rows, (int64_t)per_sm * h3host::sm_count(dev));
+  swiglu_rotate_peer_kernel<KIND, NP><<<grid, threads, smem, stream>>>(
+      x, rows, width, row_max, division, q, scale, pm);
+  return h3host::check_launch();
+}
+
+template <int KIND>
+static int launch_peer(const void* x, int64_t rows, int64_t width, float* row_max,
+                       int division, int8_t* q, float* scale, const PeerMax& pm,
+                       cudaStream_t stream) {
+  const RowTeam t = row_team(width);
+  if (t.nb != 1 || peer_producer_smem(t.threads, 1) > 227 * 1024) return H3_ERR_INVALID;
+  return launch_peer_np<KIND, 1>(x, rows, width, row_max, division, q, scale, t.threads, pm,
+                                 stream);
 }
 
 static bool producer_geometry_ok(const void* x, int kind, int64_t rows, int64_t width) {
@@ -601,10 +711,11 @@ extern "C" int h3_swiglu_rotate_quantize_peer(const void* x, int input_kind, int
                                               int rank, int64_t slots_off, uint32_t epoch,
                                               int division, int8_t* q, float* scale,
                                               float* row_max, void* stream) {
-  if (!producer_geometry_ok(x, input_kind, rows, width) || q == nullptr || scale == nullptr ||
-      !h3host::aligned(q, 16) || (division != H3_DIV_RN && division != H3_DIV_FAST) ||
-      bases == nullptr || (world != 2 && world != 4 && world != 8) || rank < 0 ||
-      rank >= world || slots_off < 0 || slots_off % 8 != 0 || epoch == 0)
+  if (!producer_geometry_ok(x, input_kind, rows, width) || width > H3_PEER_PRODUCER_MAX_WIDTH ||
+      q == nullptr || scale == nullptr || !h3host::aligned(q, 16) ||
+      (division != H3_DIV_RN && division != H3_DIV_FAST) || bases == nullptr ||
+      (world != 2 && world != 4 && world != 8) || rank < 0 || rank >= world || slots_off < 0 ||
+      slots_off % 8 != 0 || epoch == 0)
     return H3_ERR_INVALID;
   PeerMax pm{};
   for (int w = 0; w < world; ++w) {
@@ -620,8 +731,15 @@ extern "C" int h3_swiglu_rotate_quantize_peer(const void* x, int input_kind, int
   pm.epoch = epoch;
   pm.err = h3host::error_word(dev);
   if (pm.err == nullptr) return H3_ERR_CUDA;
-  return dispatch_kind<MODE_PEER>(input_kind, x, rows, width, nullptr, row_max, nullptr,
-                                  division, q, scale, (cudaStream_t)stream, pm);
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (input_kind) {
+    case H3_IN_GATEUP_F16:
+      return launch_peer<H3_IN_GATEUP_F16>(x, rows, width, row_max, division, q, scale, pm, st);
+    case H3_IN_ACT_F32:
+      return launch_peer<H3_IN_ACT_F32>(x, rows, width, row_max, division, q, scale, pm, st);
+    default:
+      return launch_peer<H3_IN_ACT_F16>(x, rows, width, row_max, division, q, scale, pm, st);
+  }
 }
 
 extern "C" int h3_column_quantize(const void* x_f16, int64_t rows, int64_t k, int convrot,

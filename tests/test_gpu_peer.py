@@ -165,6 +165,10 @@ def test_peer_rejects_bad_geometry(cuda_device):
     with pytest.raises(ValueError):   # width not a multiple of 8
         ops.peer_gather(bases, 2, 0, 0, foff, 4, 252, torch.zeros((4, 252), dtype=torch.float16,
                                                                    device=dev))
+    with pytest.raises(ValueError):   # rows wider than the peer producer stages
+        ops.swiglu_rotate_quantize_peer(
+            torch.zeros((1, 2 * (ops.PEER_PRODUCER_MAX_WIDTH + 256)), dtype=torch.float16,
+                        device=dev), bases, 2, 0, FLAGS, 1)
 
 
 # ----------------------------------------------------------------------------
