@@ -289,6 +289,7 @@ def run_ours(args):
     stream = torch.cuda.current_stream(dev)
 
     fc1_events = []
+    fc2_events = []
 
     def step(record=False):
         # TPDiTMLPINT8.forward, unrolled so the FC1 GEMM can be bracketed by events.
@@ -307,6 +308,10 @@ def run_ours(args):
                       residual=x, transport=mlp.fc2.operator_policy.row_transport,
                       payload=mlp.fc2.operator_policy.row_payload,
                       peer_max=mlp.fc2.operator_policy.fc2_max_exchange == "peer")
+        if record:
+            e2 = torch.cuda.Event(enable_timing=True)
+            e2.record(stream)
+            fc2_events.append((e1, e2))
 
     with torch.no_grad():
         for _ in range(max(3, args.warmup)):
@@ -330,10 +335,11 @@ def run_ours(args):
         launches = ops.launch_count() - calls0
         elapsed_ms = start.elapsed_time(end)
         fc1_ms = statistics.mean(a.elapsed_time(b) for a, b in fc1_events)
-        t = torch.tensor([elapsed_ms, fc1_ms], device=dev, dtype=torch.float64)
+        fc2_ms = statistics.mean(a.elapsed_time(b) for a, b in fc2_events)
+        t = torch.tensor([elapsed_ms, fc1_ms, fc2_ms], device=dev, dtype=torch.float64)
         if comm:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms, fc1_ms = float(t[0]), float(t[1])
+        elapsed_ms, fc1_ms, fc2_ms = float(t[0]), float(t[1]), float(t[2])
         ms_per_step = elapsed_ms / args.steps
 
         # e2e through the public module API with host buffers: every step uploads its
@@ -456,6 +462,8 @@ def run_ours(args):
                      "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({pk['source']}); "
                                     "INT8 dense peak estimate"},
         "gpu_launches": int(launches),
+        "phases_ms": {"fc1_gemm": round(fc1_ms, 4), "fc2_chain": round(fc2_ms, 4),
+                      "column_quantize_and_rest": round(ms_per_step - fc1_ms - fc2_ms, 4)},
         "device_error": err,
     }
     clk = clocks.summary()
