@@ -224,53 +224,27 @@ __global__ void __launch_bounds__(THREADS) reduce_kernel(const Args a) {
     const int64_t total = (a.row_end - a.row_begin) * chunks;
     const int64_t first = a.row_begin * chunks;  // uint4 index of the block's first chunk
     uint4* res = reinterpret_cast<uint4*>(a.residual);
-    const int64_t stride = (int64_t)gridDim.x * THREADS;
-    if (PACKED) {
-      for (int64_t i = blockIdx.x * (int64_t)THREADS + threadIdx.x; i < total; i += stride) {
-        const int64_t e = first + i;  // uint4 index of the chunk in [rows][width]
-        const int64_t r = e / chunks;
-        const int64_t c0 = (e - r * chunks) << 3;
-        int32_t q[8];
+    for (int64_t i = blockIdx.x * (int64_t)THREADS + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * THREADS) {
+      const int64_t e = first + i;  // uint4 index of the chunk in [rows][width]
+      const int64_t r = e / chunks;
+      const int64_t c0 = (e - r * chunks) << 3;
+      int32_t q[8];
+      if (PACKED) {
         load_restore_int8<W>(a, r, c0, q);
-        const uint4 y = epilogue_chunk(a, q, r, c0, res[e]);
-        res[e] = y;
+      } else {
+        uint4 u[W];
 #pragma unroll
         for (int w = 0; w < W; ++w)
-          if (w != a.rank) reinterpret_cast<uint4*>(a.bases[w] + a.final_off)[e] = y;
+          u[w] = w == a.rank ? load_received(a.bases[w], a.partial_off + e * 16)
+                             : load_peer(a.bases[w], a.partial_off + e * 16);
+        restore_fp16<W>(a, u, q);
       }
-    } else {
-      // Two chunks per thread and step, every load of both issued before either is
-      // used: twice the NVLink bytes in flight per thread.
-      for (int64_t i = blockIdx.x * (int64_t)THREADS + threadIdx.x; i < total;
-           i += 2 * stride) {
-        const bool two = i + stride < total;
-        const int64_t e0 = first + i;
-        const int64_t e1 = two ? e0 + stride : e0;  // a repeat of chunk 0 when alone
-        uint4 u0[W], u1[W];
+      const uint4 y = epilogue_chunk(a, q, r, c0, res[e]);
+      res[e] = y;
 #pragma unroll
-        for (int w = 0; w < W; ++w) {
-          u0[w] = w == a.rank ? load_received(a.bases[w], a.partial_off + e0 * 16)
-                              : load_peer(a.bases[w], a.partial_off + e0 * 16);
-          u1[w] = w == a.rank ? load_received(a.bases[w], a.partial_off + e1 * 16)
-                              : load_peer(a.bases[w], a.partial_off + e1 * 16);
-        }
-        const uint4 x0 = res[e0], x1 = res[e1];
-        int32_t q0[8], q1[8];
-        restore_fp16<W>(a, u0, q0);
-        restore_fp16<W>(a, u1, q1);
-        const int64_t r0 = e0 / chunks, r1 = e1 / chunks;
-        const uint4 y0 = epilogue_chunk(a, q0, r0, (e0 - r0 * chunks) << 3, x0);
-        const uint4 y1 = epilogue_chunk(a, q1, r1, (e1 - r1 * chunks) << 3, x1);
-        res[e0] = y0;
-        if (two) res[e1] = y1;
-#pragma unroll
-        for (int w = 0; w < W; ++w)
-          if (w != a.rank) {
-            uint4* fin = reinterpret_cast<uint4*>(a.bases[w] + a.final_off);
-            fin[e0] = y0;
-            if (two) fin[e1] = y1;
-          }
-      }
+      for (int w = 0; w < W; ++w)
+        if (w != a.rank) reinterpret_cast<uint4*>(a.bases[w] + a.final_off)[e] = y;
     }
   } else if (threadIdx.x == 0) {
     atomicExch(a.err, H3_ERR_TIMEOUT);
