@@ -53,9 +53,7 @@ constexpr int BM2 = 256;
 constexpr int B_HALF = (BN / 2) * BK;          // 16 KiB
 constexpr int STAGES2 = 6;
 constexpr int STAGE2_BYTES = A_STAGE + B_HALF;  // 32 KiB per CTA
-// per epilogue warp: a 32-row x 8-column fp32 staging block for its TMA stores
-constexpr int EPI_STAGE = EPI_WARPS * 32 * 8 * 4;
-constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + EPI_STAGE + 256 + EPI_SMEM;
+constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 256 + EPI_SMEM;
 
 // Instruction descriptor, kind::i8: D = S32 (bits 4-5 = 2), A = B = signed 8-bit
 // (bits 7-9 and 10-12 = 1), both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
@@ -90,7 +88,6 @@ struct Args {
   RowOut row;
   int res_vec;    // residual / gate rows may use 128-bit accesses
   int scale_vec;  // weight scales / bias may use 128-bit loads
-  int tma_out;    // SWIGLU, FP32 output: stores go through shared memory and TMA
   int* err;
 };
 
@@ -208,33 +205,6 @@ H3_DEV void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int32_t c0, i
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
       "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(cluster_bar)
       : "memory");
-}
-
-// TMA store of a shared-memory block into the tensor of `map` at (c0, c1), as one
-// bulk group, with an L2 evict-first policy (the output streams past the operands).
-H3_DEV void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t c0, int32_t c1,
-                         uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint"
-      " [%0, {%2, %3}], [%1], %4;" ::"l"((uint64_t)map),
-      "r"(src), "r"(c0), "r"(c1), "l"(policy)
-      : "memory");
-}
-
-H3_DEV uint64_t l2_evict_first_policy() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
-
-H3_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// the shared-memory sources of this thread's bulk groups have been read
-H3_DEV void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-// this thread's bulk groups are complete
-H3_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-// generic-proxy writes to shared memory become visible to the TMA (async proxy)
-H3_DEV void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 H3_DEV void tc_commit_pair(uint32_t cluster_bar) {
@@ -446,12 +416,9 @@ H3_DEV void load_scales(const float* w, int64_t n0, int64_t N, int scalar, float
 // Epilogue of one output tile: this warp's 32 TMEM lanes (`row` is the lane's output
 // row) and one EPI_PARTS-th of the tile's 256 accumulator columns.
 // ---------------------------------------------------------------------------
-// stg / tmC / policy: the warp's TMA staging block, the output tensor map and the L2
-// policy of its stores (args.tma_out, CTA-pair kernel only).
 template <int EPI>
 H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool row_ok, int nb,
-                          int part, float* wsm, float* stg = nullptr,
-                          const CUtensorMap* tmC = nullptr, uint64_t policy = 0) {
+                          int part, float* wsm) {
   const int64_t N = args.N;
   if (EPI == EPI_SWIGLU) {
     // accumulator columns [0,128) = gate rows, [128,256) = up rows of this tile
@@ -504,22 +471,7 @@ H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool ro
         const float u = __half2float(__float2half_rn(vu));
         y[j] = swiglu_f32(g, u);
       }
-      if (tmC != nullptr) {
-        // lane = row of a 32 x 8 block in shared memory, written to the output by one
-        // TMA store (rows >= M and columns >= N are clipped by the copy)
-        if (lane == 0) bulk_wait_read();  // the previous block has been read
-        __syncwarp();
-        float4* st = reinterpret_cast<float4*>(stg + lane * SW);
-        st[0] = make_float4(y[0], y[1], y[2], y[3]);
-        st[1] = make_float4(y[4], y[5], y[6], y[7]);
-        fence_proxy_async_smem();
-        __syncwarp();
-        const int64_t row0 = row - lane;
-        if (lane == 0 && row0 < args.M) {
-          tma_store_2d(tmC, smem_u32(stg), (int32_t)n0, (int32_t)row0, policy);
-          bulk_commit();
-        }
-      } else if (row_ok) {
+      if (row_ok) {
         if (args.out_kind == H3_OUT_F32)
           store_f32_chunk<SW>(reinterpret_cast<float*>(args.out) + row * N + n0, n0, N, y,
                               (N & 3) == 0, true);
@@ -821,17 +773,13 @@ template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmB2,
-                        const __grid_constant__ CUtensorMap tmC, const Args args) {
+                        const __grid_constant__ CUtensorMap tmB2, const Args args) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES2 * A_STAGE;
-  // TMA staging blocks: 1024-byte aligned, one per epilogue warp
-  float* stg = reinterpret_cast<float*>(smem + STAGES2 * STAGE2_BYTES) +
-               (threadIdx.x / 32 >= 2 ? (threadIdx.x / 32 - 2) * 32 * 8 : 0);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES2 * STAGE2_BYTES + EPI_STAGE);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES2 * STAGE2_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES2;
   uint64_t* tfull = bars + 2 * STAGES2;
@@ -839,7 +787,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* wsm = reinterpret_cast<float*>(smem + STAGES2 * STAGE2_BYTES + EPI_STAGE + 256) +
+  float* wsm = reinterpret_cast<float*>(smem + STAGES2 * STAGE2_BYTES + 256) +
                (threadIdx.x / 32 >= 2 ? (threadIdx.x / 32 - 2) * 64 : 0);
 
   const int warp = threadIdx.x >> 5;
@@ -971,8 +919,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const int part = (warp - 2) >> 2;
     int acc = 0;
     uint32_t acc_phase = 0;
-    const bool tma_out = EPI == EPI_SWIGLU && args.tma_out != 0;
-    const uint64_t policy = tma_out ? l2_evict_first_policy() : 0;
     for (int tile = cluster_id; tile < total_tiles; tile += clusters) {
       int mb, nb;
       tile_coords(tile, args, mb, nb);
@@ -980,16 +926,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const int64_t row = (int64_t)mb * BM2 + (int64_t)rank * BM + quad * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-      epilogue_tile<EPI>(args, tbase, row, row < args.M, nb, part, wsm, stg,
-                         tma_out ? &tmC : nullptr, policy);
+      epilogue_tile<EPI>(args, tbase, row, row < args.M, nb, part, wsm);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(cluster_addr(smem_u32(tempty + acc), 0));
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
-    // the output stores of this warp are complete before the CTA leaves
-    if (tma_out && lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -1030,21 +973,6 @@ static bool make_map(CUtensorMap* map, const int8_t* base, int64_t rows, int64_t
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
-// Row-major fp32 [rows, cols] output with a 32-row x 8-column box (32 bytes inner, no
-// swizzle), for the epilogue's TMA stores.
-static bool make_out_map(CUtensorMap* map, float* base, int64_t rows, int64_t cols) {
-  auto fn = encode_fn();
-  if (fn == nullptr) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)cols * sizeof(float)};
-  cuuint32_t box[2] = {8, 32};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -1099,14 +1027,6 @@ static int launch(const int8_t* q, const int8_t* w, int64_t M, int64_t N, int64_
     if (!make_map(&tB, w, N, K, bn_rows)) return H3_ERR_INVALID;
     tB2 = tB;
   }
-  // FP32 SwiGLU output of the pair kernel: TMA stores of 32 x 8 blocks
-  CUtensorMap tC = tA;
-  args.tma_out = 0;
-  if (EPI == EPI_SWIGLU && pair && args.out_kind == H3_OUT_F32 && N % 4 == 0 &&
-      h3host::aligned(args.out, 16)) {
-    if (!make_out_map(&tC, reinterpret_cast<float*>(args.out), M, N)) return H3_ERR_INVALID;
-    args.tma_out = 1;
-  }
   const int tile_n = EPI == EPI_SWIGLU ? BN / 2 : BN;
   args.M = M;
   args.N = N;
@@ -1130,7 +1050,7 @@ static int launch(const int8_t* q, const int8_t* w, int64_t M, int64_t N, int64_
       attr_set[dev][1] = true;
     }
     const int grid = 2 * (int)std::min<int64_t>(tiles, sms / 2);
-    gemm_i8_pair_kernel<EPI><<<grid, THREADS, SMEM2_BYTES, stream>>>(tA, tB, tB2, tC, args);
+    gemm_i8_pair_kernel<EPI><<<grid, THREADS, SMEM2_BYTES, stream>>>(tA, tB, tB2, args);
   } else {
     if (!attr_set[dev][0]) {
       if (cudaFuncSetAttribute(gemm_i8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1345,7 +1265,7 @@ extern "C" int h3_column_linear_noalloc(const void* x_f16, int64_t m, int64_t k,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES) != cudaSuccess)
       return H3_ERR_CUDA;
     const int grid = 2 * (int)std::min<int64_t>(tiles, sms / 2);
-    gemm_i8_pair_kernel<EPI_COLUMN><<<grid, THREADS, SMEM2_BYTES, st>>>(tA, tB, tB, tA, args);
+    gemm_i8_pair_kernel<EPI_COLUMN><<<grid, THREADS, SMEM2_BYTES, st>>>(tA, tB, tB, args);
   } else {
     if (cudaFuncSetAttribute(gemm_i8_kernel<EPI_COLUMN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              SMEM_BYTES) != cudaSuccess)
