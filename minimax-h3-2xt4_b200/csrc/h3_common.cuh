@@ -157,11 +157,13 @@ H3_DEV f32x2 dup2(float v) { return pk2(v, v); }
 H3_DEV float lo2(f32x2 v) {
   float a, b;
   asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+  (void)b;
   return a;
 }
 H3_DEV float hi2(f32x2 v) {
   float a, b;
   asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+  (void)a;
   return b;
 }
 H3_DEV f32x2 add2(f32x2 a, f32x2 b) {

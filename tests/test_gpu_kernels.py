@@ -380,10 +380,13 @@ def test_gemm_column_scalar_weight_scale(cuda_device, oracle):
     _bits_equal(_np(y), oracle.column_epilogue(oracle.int8_gemm(A, W), a, w))
 
 
-@pytest.mark.parametrize("M,Nh,K", [(1, 128, 128), (33, 96, 256), (300, 256, 3072), (129, 384, 1024)])
+@pytest.mark.parametrize("M,Nh,K", [(1, 128, 128), (33, 96, 256), (300, 256, 3072), (129, 384, 1024),
+                                    (260, 100, 512), (200, 98, 256)])
 @pytest.mark.parametrize("out", ["f32", "f16"])
 @pytest.mark.parametrize("bias", [False, True])
 def test_gemm_swiglu_bit_exact(cuda_device, oracle, M, Nh, K, out, bias):
+    """Ragged rows (M = 129, 200, 260, 300 on CTA pairs) and ragged columns (Nh = 100,
+    98: a partial 8-column chunk, a width that is not a multiple of 4)."""
     from h3tp import ops
     rng = np.random.default_rng(M + Nh + K)
     A, W = _operands(rng, M, 2 * Nh, K)
