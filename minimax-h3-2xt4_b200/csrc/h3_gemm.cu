@@ -37,10 +37,12 @@ constexpr int STAGES = 4;
 constexpr int A_STAGE = BM * BK;  // 16 KiB
 constexpr int B_STAGE = BN * BK;  // 32 KiB
 constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
-constexpr int MAX_EPI_WARPS = 32;            // the SwiGLU epilogue's; 16 for the others
+constexpr int EPI_WARPS = 16;                // four warps per 32-lane TMEM quadrant
+constexpr int EPI_PARTS = EPI_WARPS / 4;     // column slices of a tile, one per warp
+constexpr int THREADS = 64 + 32 * EPI_WARPS;  // warp 0 TMA, warp 1 MMA, warps 2.. epilogue
 constexpr int TMEM_COLS = 512;
 // per epilogue warp: 64 floats of staged weight scales (EPI_SWIGLU)
-constexpr int EPI_SMEM = MAX_EPI_WARPS * 64 * 4;
+constexpr int EPI_SMEM = EPI_WARPS * 64 * 4;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + EPI_SMEM;
 constexpr unsigned long long TIMEOUT_NS = 2000000000ull;
 
@@ -68,17 +70,6 @@ enum Epi {
   EPI_ROW_ENCODE = 3,
   EPI_ROW_DEQUANT = 4,
   EPI_ROW_PACK8 = 5
-};
-
-// Epilogue warps per CTA (warps 2.., the same number per 32-lane TMEM quadrant) and
-// CTA size (warp 0 TMA, warp 1 MMA).  The SwiGLU epilogue is the heaviest per output
-// and latency-bound: it runs eight warps per quadrant (two per scheduler at every
-// instant more than the others) on 4-column steps, within 56 registers.
-template <int EPI>
-struct EpiShape {
-  static constexpr int warps = EPI == EPI_SWIGLU ? 32 : 16;
-  static constexpr int parts = warps / 4;  // column slices of a tile, one per warp
-  static constexpr int threads = 64 + 32 * warps;
 };
 
 struct Args {
@@ -269,13 +260,7 @@ H3_DEV void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 
-H3_DEV void tmem_ld_nowait(uint32_t taddr, uint32_t (&r)[4]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(taddr));
-}
-
-H3_DEV void tmem_ld_nowait(uint32_t taddr, uint32_t (&r)[8]) {
+H3_DEV void tmem_ld8_nowait(uint32_t taddr, uint32_t (&r)[8]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
                  "=r"(r[6]), "=r"(r[7])
@@ -290,14 +275,6 @@ H3_DEV void tmem_wait_ld(uint32_t (&r)[16]) {
                : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
                  "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
                  "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
-               :
-               : "memory");
-}
-
-H3_DEV void tmem_wait_ld(uint32_t (&a)[4], uint32_t (&b)[4]) {
-  asm volatile("tcgen05.wait::ld.sync.aligned;"
-               : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(b[0]), "+r"(b[1]),
-                 "+r"(b[2]), "+r"(b[3])
                :
                : "memory");
 }
@@ -341,13 +318,7 @@ H3_DEV void tile_coords(int tile, const Args& a, int& mb, int& nb) {
 // ---------------------------------------------------------------------------
 template <int C>
 H3_DEV void store_f16_chunk(__half* dst, int64_t n0, int64_t N, const float (&v)[C], bool vec) {
-  if (vec && n0 + C <= N && C % 8 != 0) {
-    static_assert(C % 8 == 0 || C == 4, "4 or a multiple of 8 columns");
-    __half2 h[2];
-    h[0] = __floats2half2_rn(v[0], v[1]);
-    h[1] = __floats2half2_rn(v[2], v[3]);
-    *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<uint2*>(h);
-  } else if (vec && n0 + C <= N) {
+  if (vec && n0 + C <= N) {
     uint4* p = reinterpret_cast<uint4*>(dst);
 #pragma unroll
     for (int i = 0; i < C / 8; ++i) {
@@ -443,7 +414,7 @@ H3_DEV void load_scales(const float* w, int64_t n0, int64_t N, int scalar, float
 
 // ---------------------------------------------------------------------------
 // Epilogue of one output tile: this warp's 32 TMEM lanes (`row` is the lane's output
-// row) and one EpiShape<EPI>::parts-th of the tile's 256 accumulator columns.
+// row) and one EPI_PARTS-th of the tile's 256 accumulator columns.
 // ---------------------------------------------------------------------------
 template <int EPI>
 H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool row_ok, int nb,
@@ -451,16 +422,16 @@ H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool ro
   const int64_t N = args.N;
   if (EPI == EPI_SWIGLU) {
     // accumulator columns [0,128) = gate rows, [128,256) = up rows of this tile
-    constexpr int GCOLS = (BN / 2) / EpiShape<EPI>::parts;  // gate columns of this warp
+    constexpr int GCOLS = (BN / 2) / EPI_PARTS;  // gate columns of this warp
     const int64_t n_base = (int64_t)nb * (BN / 2) + part * GCOLS;
     const float a = row_ok ? __ldg(args.row_scale + row) : 0.0f;
     const bool vec4 = args.scale_vec != 0;
-    constexpr int SW = GCOLS >= 32 ? 8 : 4;  // columns per step (register budget)
-    // This warp's GCOLS gate and GCOLS up weight scales, staged in shared memory once
-    // per tile (one coalesced load per lane) and read back as broadcasts.
+    constexpr int SW = 8;  // columns per step: keeps the SwiGLU epilogue within 96 registers
+    // This warp's 32 gate and 32 up weight scales, staged in shared memory once per
+    // tile (one coalesced load per lane) and read back as broadcasts.
     const int lane = threadIdx.x & 31;
     __syncwarp();
-    if (lane < GCOLS) {
+    {
       const int64_t nl = n_base + lane;
       wsm[lane] = nl < N ? __ldg(args.weight_scale + nl) : 0.0f;
       wsm[32 + lane] = nl < N ? __ldg(args.weight_scale + N + nl) : 0.0f;
@@ -471,8 +442,8 @@ H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool ro
       const int64_t n0 = n_base + c * SW;
       if (n0 >= N) break;  // warp-uniform
       uint32_t rg[SW], ru[SW];
-      tmem_ld_nowait(tbase + part * GCOLS + c * SW, rg);
-      tmem_ld_nowait(tbase + BN / 2 + part * GCOLS + c * SW, ru);
+      tmem_ld8_nowait(tbase + part * GCOLS + c * SW, rg);
+      tmem_ld8_nowait(tbase + BN / 2 + part * GCOLS + c * SW, ru);
       float wg[SW], wu[SW];
 #pragma unroll
       for (int i = 0; i < SW / 4; ++i) {
@@ -515,9 +486,8 @@ H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool ro
     // q = clamp(rint(f32(P) /rn scale), -127, 127).  A group is the columns of two warps
     // of the same TMEM lane quadrant (parts 2g', 2g'+1); each warp reads the whole group
     // from TMEM for the maximum (no exchange between warps) and codes its own 64.
-    constexpr int COLS = BN / EpiShape<EPI>::parts;  // 64
-    static_assert(EPI != EPI_ROW_PACK8 || COLS == 64, "two warps per 128-column group");
-    const int gl = part >> 1;                        // group within the tile
+    constexpr int COLS = BN / EPI_PARTS;  // 64
+    const int gl = part >> 1;             // group within the tile
     const int64_t g = (int64_t)nb * (BN / 128) + gl;
     if (g * 128 >= N) return;  // warp-uniform: the whole group is past the last column
     float m = 0.0f;
@@ -559,7 +529,7 @@ H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool ro
     }
     if (row_ok && (part & 1) == 0) *reinterpret_cast<float*>(dst + 128) = scale;
   } else {
-    constexpr int COLS = BN / EpiShape<EPI>::parts;  // accumulator columns of this warp
+    constexpr int COLS = BN / EPI_PARTS;  // accumulator columns of this warp
     const int64_t n_base = (int64_t)nb * BN + part * COLS;
     const float a = (row_ok && args.row_scale != nullptr) ? __ldg(args.row_scale + row) : 0.0f;
     int64_t lab = 0;
@@ -630,7 +600,7 @@ H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool ro
 }
 
 template <int EPI>
-__global__ void __launch_bounds__(EpiShape<EPI>::threads, 1)
+__global__ void __launch_bounds__(THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmB2, const Args args) {
   extern __shared__ uint8_t smem_raw[];
@@ -659,7 +629,7 @@ __global__ void __launch_bounds__(EpiShape<EPI>::threads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(tfull + a), 1);
-      mbar_init(smem_u32(tempty + a), 32 * EpiShape<EPI>::warps);
+      mbar_init(smem_u32(tempty + a), 32 * EPI_WARPS);
     }
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
@@ -800,7 +770,7 @@ __global__ void __launch_bounds__(EpiShape<EPI>::threads, 1)
 //   tempty[a] leader only: one arrive per epilogue warp of both CTAs
 // ---------------------------------------------------------------------------
 template <int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(EpiShape<EPI>::threads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmB2, const Args args) {
@@ -832,7 +802,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(EpiShape<EPI>::threa
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(tfull + a), 1);
-      mbar_init(smem_u32(tempty + a), 2 * EpiShape<EPI>::warps);
+      mbar_init(smem_u32(tempty + a), 2 * EPI_WARPS);
     }
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
@@ -1080,8 +1050,7 @@ static int launch(const int8_t* q, const int8_t* w, int64_t M, int64_t N, int64_
       attr_set[dev][1] = true;
     }
     const int grid = 2 * (int)std::min<int64_t>(tiles, sms / 2);
-    gemm_i8_pair_kernel<EPI><<<grid, EpiShape<EPI>::threads, SMEM2_BYTES, stream>>>(tA, tB, tB2,
-                                                                                 args);
+    gemm_i8_pair_kernel<EPI><<<grid, THREADS, SMEM2_BYTES, stream>>>(tA, tB, tB2, args);
   } else {
     if (!attr_set[dev][0]) {
       if (cudaFuncSetAttribute(gemm_i8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1090,7 +1059,7 @@ static int launch(const int8_t* q, const int8_t* w, int64_t M, int64_t N, int64_
       attr_set[dev][0] = true;
     }
     const int grid = (int)std::min<int64_t>(tiles, sms);
-    gemm_i8_kernel<EPI><<<grid, EpiShape<EPI>::threads, SMEM_BYTES, stream>>>(tA, tB, tB2, args);
+    gemm_i8_kernel<EPI><<<grid, THREADS, SMEM_BYTES, stream>>>(tA, tB, tB2, args);
   }
   return h3host::check_launch();
 }
@@ -1296,15 +1265,13 @@ extern "C" int h3_column_linear_noalloc(const void* x_f16, int64_t m, int64_t k,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES) != cudaSuccess)
       return H3_ERR_CUDA;
     const int grid = 2 * (int)std::min<int64_t>(tiles, sms / 2);
-    gemm_i8_pair_kernel<EPI_COLUMN>
-        <<<grid, EpiShape<EPI_COLUMN>::threads, SMEM2_BYTES, st>>>(tA, tB, tB, args);
+    gemm_i8_pair_kernel<EPI_COLUMN><<<grid, THREADS, SMEM2_BYTES, st>>>(tA, tB, tB, args);
   } else {
     if (cudaFuncSetAttribute(gemm_i8_kernel<EPI_COLUMN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              SMEM_BYTES) != cudaSuccess)
       return H3_ERR_CUDA;
     const int grid = (int)std::min<int64_t>(tiles, sms);
-    gemm_i8_kernel<EPI_COLUMN><<<grid, EpiShape<EPI_COLUMN>::threads, SMEM_BYTES, st>>>(tA, tB,
-                                                                                       tB, args);
+    gemm_i8_kernel<EPI_COLUMN><<<grid, THREADS, SMEM_BYTES, st>>>(tA, tB, tB, args);
   }
   return h3host::check_launch();
 }
