@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--sweep", action="store_true",
                     help="BASELINE config 5 shape sweep on one GPU: one JSON line per point")
+    ap.add_argument("--sweep-producers", action="store_true",
+                    help="only the activation-producer lines of the sweep")
     ap.add_argument("--max-exchange", choices=["peer", "nccl"], default="peer",
                     help="FC2 row maxima at TP > 1: in-kernel over peer memory, or NCCL MAX")
     ap.add_argument("--payload", choices=["fp16", "int8_gather"], default="fp16",
@@ -510,7 +512,8 @@ def run_sweep(args):
         return statistics.median(ts)
 
     with torch.no_grad():
-        for K, N in ((3072, 3072), (3072, 16384), (8192, 3072), (5120, 13824)):
+        for K, N in (() if args.sweep_producers else
+                     ((3072, 3072), (3072, 16384), (8192, 3072), (5120, 13824))):
             w = torch.randint(-127, 128, (N, K), generator=g, device=dev, dtype=torch.int8)
             s = torch.rand((N, 1), generator=g, device=dev) * 9e-3 + 1e-3
             for M in (256, 1024, 4096, 16384, 65536):
@@ -550,6 +553,37 @@ def run_sweep(args):
                               "frac_of_hbm": round(nbytes / (fused * 1e-3) / 1e9 / hbm, 4)}),
                   flush=True)
             del x
+        # TP > 1 FC2 producer (BASELINE config 4 at TP 2/4/8, Kl = 8192 / t): the
+        # in-kernel row-maximum exchange against the two passes of the NCCL route (the
+        # MAX all-reduce between them not included) and the TP1 single pass, one GPU
+        # emulating `world` ranks whose slots are all published before the launch.
+        for world in (2, 4, 8):
+            kl = 8192 // world
+            act = torch.randn((M, kl), generator=g, device=dev) * 0.7
+            _, mx = ops.swiglu_rotate_max(act, "act_f32", store=False)
+            bits = mx.reshape(-1).view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+            slots = ((1 << 32) | bits).reshape(M, 1).expand(M, world).contiguous()
+            bufs = [torch.zeros(256 + M * world * 8, dtype=torch.uint8, device=dev)
+                    for _ in range(world)]
+            for b in bufs:
+                b[256:].view(torch.int64).view(M, world).copy_(slots)
+            bases = [b.data_ptr() for b in bufs]
+            peer = timed(lambda: ops.swiglu_rotate_quantize_peer(act, bases, world, 0, 256, 1,
+                                                                 "act_f32"))
+
+            def two_pass():
+                _, m = ops.swiglu_rotate_max(act, "act_f32", store=False)
+                ops.swiglu_rotate_quantize(act, m, "act_f32")
+
+            two = timed(two_pass)
+            local = timed(lambda: ops.swiglu_rotate_quantize_local(act, "act_f32"))
+            nbytes = M * kl * 4 + M * kl + 4 * M  # read the activation, write codes, scales
+            print(json.dumps({"sweep": "fc2_producer_tp", "tp": world, "M": M, "Kl": kl,
+                              "ms_peer": round(peer, 4), "ms_two_pass": round(two, 4),
+                              "ms_tp1_single_pass": round(local, 4),
+                              "frac_of_hbm_peer": round(nbytes / (peer * 1e-3) / 1e9 / hbm, 4)}),
+                  flush=True)
+            del act, bufs
     return 0
 
 
@@ -557,7 +591,7 @@ def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
-    if args.sweep:
+    if args.sweep or args.sweep_producers:
         return run_sweep(args)
     return run_ours(args)
 
