@@ -279,13 +279,14 @@ __global__ void __launch_bounds__(512) swiglu_rotate_kernel(
   }
 }
 
-// FC2 producer at TP>1 in one pass over HBM.  The row loop is pipelined by one row: a
-// CTA rotates row i and publishes its local maximum to every rank, and only then waits
-// for the global maximum of its previous row, reloads that row (an L2 hit: the grid
-// read it one iteration earlier, a few MB ago) and rotates and quantises it, so the
-// NVLink round trip of a maximum overlaps the next row's loads and rotation.  Launched
-// as a persistent grid (every CTA resident), so a CTA waiting for a peer's row never
-// waits for a CTA that cannot run.
+// FC2 producer at TP>1 in one pass.  The row loop is pipelined by one row: a CTA
+// rotates row i, publishes its local maximum to every rank, stashes the rotated values
+// in shared memory, and only then waits for the global maximum of its previous row and
+// quantises that row from the stash, so the NVLink round trip of a maximum overlaps
+// the next row's loads and rotation.  Each thread reads back only what it stashed, so
+// the stash needs no barrier; two stash buffers alternate between rows.  Launched as a
+// persistent grid (every CTA resident), so a CTA waiting for a peer's row never waits
+// for a CTA that cannot run.
 template <int KIND, int NP>
 __global__ void __launch_bounds__(512) swiglu_rotate_peer_kernel(
     const void* __restrict__ x, int64_t rows, int64_t width, float* __restrict__ row_max,
@@ -296,6 +297,7 @@ __global__ void __launch_bounds__(512) swiglu_rotate_peer_kernel(
   const int half = tid >> 4, b = tid & 15;
   f32x2* tile = smem2 + half * (16 * 17);
   float* red = reinterpret_cast<float*>(smem2 + (T / 16) * (16 * 17));
+  f32x2* stash = reinterpret_cast<f32x2*>(red + 32);  // [2][NP * 16][T]
   const int64_t blocks = width / 16;
   int64_t blk[NP][2];
   bool ok[NP][2];
@@ -310,6 +312,7 @@ __global__ void __launch_bounds__(512) swiglu_rotate_peer_kernel(
   int64_t prev = -1;
   bool prev_finite = false;
   float prev_local = 0.0f;
+  int buf = 0;
 
   for (int64_t row = blockIdx.x;; row += gridDim.x) {
     const bool have = row < rows;
@@ -329,6 +332,11 @@ __global__ void __launch_bounds__(512) swiglu_rotate_peer_kernel(
       finite = m < __uint_as_float(0x7f800000u);  // false for +inf and NaN
       if (!finite) m = block_reduce_max(local_max_ignoring_nan<NP>(v, ok), red);
       peer_publish(pm, row, m);
+      f32x2* st = stash + (size_t)buf * NP * 16 * T;
+#pragma unroll
+      for (int p = 0; p < NP; ++p)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) st[(p * 16 + i) * T + tid] = v[p][i];
     }
     if (prev >= 0) {
       const float g = peer_wait(pm, prev, prev_local, red, deadline);
@@ -337,12 +345,12 @@ __global__ void __launch_bounds__(512) swiglu_rotate_peer_kernel(
       const bool fin = prev_finite && g < __uint_as_float(0x7f800000u);
       const float scale = row_scale_from_max(g);
       const float inv = __fdiv_rn(1.0f, scale);
+      const f32x2* st = stash + (size_t)(buf ^ 1) * NP * 16 * T;
       f32x2 w[NP][16];
 #pragma unroll
-      for (int p = 0; p < NP; ++p) {
-        load_activation2<KIND>(x, prev, width, blk[p][0], blk[p][1], ok[p][0], ok[p][1], w[p]);
-        convrot256_halfwarp2(w[p], tile, b);
-      }
+      for (int p = 0; p < NP; ++p)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w[p][i] = st[(p * 16 + i) * T + tid];
       quantize_store<NP>(w, ok, blk, fin, scale, inv, division, q + prev * width);
       if (tid == 0) {
         scale_out[prev] = scale;
@@ -353,6 +361,7 @@ __global__ void __launch_bounds__(512) swiglu_rotate_peer_kernel(
     prev = row;
     prev_finite = finite;
     prev_local = m;
+    buf ^= 1;
   }
 }
 
@@ -611,12 +620,17 @@ static int dispatch_kind(int kind, const void* x, int64_t rows, int64_t width, f
   }
 }
 
+// The peer producer's shared memory: the producer's plus two stashes of one row.
+static size_t peer_producer_smem(int threads, int np) {
+  return producer_smem(threads) + 2 * (size_t)np * 16 * threads * sizeof(unsigned long long);
+}
+
 template <int KIND, int NP>
 static int launch_peer_np(const void* x, int64_t rows, int64_t width, float* row_max,
                           int division, int8_t* q, float* scale, int threads,
                           const PeerMax& pm, cudaStream_t stream) {
   static bool smem_set = false;
-  const size_t smem = producer_smem(threads);
+  const size_t smem = peer_producer_smem(threads, NP);
   if (!allow_smem(swiglu_rotate_peer_kernel<KIND, NP>, smem, smem_set)) return H3_ERR_CUDA;
   int per_sm = 0, dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
@@ -635,13 +649,9 @@ static int launch_peer(const void* x, int64_t rows, int64_t width, float* row_ma
                        int division, int8_t* q, float* scale, const PeerMax& pm,
                        cudaStream_t stream) {
   const RowTeam t = row_team(width);
-  if (t.nb == 1)
-    return launch_peer_np<KIND, 1>(x, rows, width, row_max, division, q, scale, t.threads, pm,
-                                   stream);
-  if (t.nb == 2)
-    return launch_peer_np<KIND, 2>(x, rows, width, row_max, division, q, scale, t.threads, pm,
-                                   stream);
-  return H3_ERR_INVALID;
+  if (t.nb != 1 || peer_producer_smem(t.threads, 1) > 227 * 1024) return H3_ERR_INVALID;
+  return launch_peer_np<KIND, 1>(x, rows, width, row_max, division, q, scale, t.threads, pm,
+                                 stream);
 }
 
 static bool producer_geometry_ok(const void* x, int kind, int64_t rows, int64_t width) {
@@ -701,7 +711,8 @@ extern "C" int h3_swiglu_rotate_quantize_peer(const void* x, int input_kind, int
                                               int rank, int64_t slots_off, uint32_t epoch,
                                               int division, int8_t* q, float* scale,
                                               float* row_max, void* stream) {
-  if (!producer_geometry_ok(x, input_kind, rows, width) || q == nullptr || scale == nullptr || !h3host::aligned(q, 16) ||
+  if (!producer_geometry_ok(x, input_kind, rows, width) || width > H3_PEER_PRODUCER_MAX_WIDTH ||
+      q == nullptr || scale == nullptr || !h3host::aligned(q, 16) ||
       (division != H3_DIV_RN && division != H3_DIV_FAST) || bases == nullptr ||
       (world != 2 && world != 4 && world != 8) || rank < 0 || rank >= world || slots_off < 0 ||
       slots_off % 8 != 0 || epoch == 0)

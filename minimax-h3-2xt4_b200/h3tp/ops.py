@@ -200,6 +200,9 @@ def swiglu_rotate_quantize_local(x, kind="gateup_f16", division="rn"):
     return q, s, m
 
 
+PEER_PRODUCER_MAX_WIDTH = 16384  # H3_PEER_PRODUCER_MAX_WIDTH
+
+
 def swiglu_rotate_quantize_peer(x, bases, world: int, rank: int, slots_off: int, epoch: int,
                                 kind="gateup_f16", division="rn", want_max=False):
     """TP>1 single pass (h3_swiglu_rotate_quantize_peer): the row maxima are exchanged

@@ -179,7 +179,8 @@ def row_linear(x, weight, weight_scale, comm, *, mode="fused_stored", scaled_tra
     if (peer_max and transport == "p2p" and scaled_transport and finish_fn is None
             and residual is not None and residual.is_contiguous()
             and (payload == "int8_gather" or residual.shape[-1] % 8 == 0)
-            and C.world_of(comm) > 1 and P.available(comm)):
+            and C.world_of(comm) > 1 and weight.shape[1] <= ops.PEER_PRODUCER_MAX_WIDTH
+            and P.available(comm)):
         ws = P.workspace(comm, x.device, weight.shape[0], x.numel() // x.shape[-1])
     with label("fp32_swiglu_convrot_quantize"):
         q, scale = prepare(x, comm, mode, consume_input=consume_input, division=division,
