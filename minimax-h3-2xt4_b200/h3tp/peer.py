@@ -48,6 +48,17 @@ def available(comm) -> bool:
         return False
 
 
+def layout(width: int, rows: int) -> dict:
+    """Byte offsets of one rank's workspace buffer for up to `rows` rows of `width`
+    columns: flags | partial (fp16 [rows][width], or the packed INT8 rows, which are
+    smaller) | final rows (fp16 [rows][width]) | row-maximum slots (u64 [rows][8]).
+    Every area starts on a 256-byte boundary."""
+    region = -(-rows * width * 2 // _ALIGN) * _ALIGN
+    slots = -(-rows * 8 * 8 // _ALIGN) * _ALIGN
+    return {"partial_off": FLAGS_BYTES, "final_off": FLAGS_BYTES + region,
+            "slots_off": FLAGS_BYTES + 2 * region, "nbytes": FLAGS_BYTES + 2 * region + slots}
+
+
 class PeerWorkspace:
     """One symmetric buffer per rank: flags | partial [rows][width] fp16 | final rows
     [rows][width] fp16 | row-maximum slots u64 [rows][8], for up to `rows` rows of
@@ -60,12 +71,11 @@ class PeerWorkspace:
         self.device = torch.device(device)
         self.width = int(width)
         self.capacity = int(rows)
-        region = -(-self.capacity * self.width * 2 // _ALIGN) * _ALIGN
-        self.partial_off = FLAGS_BYTES
-        self.final_off = FLAGS_BYTES + region
-        self.slots_off = FLAGS_BYTES + 2 * region
-        slots = -(-self.capacity * 8 * 8 // _ALIGN) * _ALIGN
-        nbytes = self.slots_off + slots
+        lay = layout(self.width, self.capacity)
+        self.partial_off = lay["partial_off"]
+        self.final_off = lay["final_off"]
+        self.slots_off = lay["slots_off"]
+        nbytes = lay["nbytes"]
         with torch.cuda.device(self.device):
             self.buf = symm.empty(nbytes, dtype=torch.uint8, device=self.device)
             self.buf[:FLAGS_BYTES].zero_()

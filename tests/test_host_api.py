@@ -19,11 +19,38 @@ def test_policy_defaults_and_validation():
     assert ref.scaled_transport
     assert not H3OperatorPolicy(row_linear_backend="native").scaled_transport
     for bad in (dict(row_linear_backend="x"), dict(fc2_quantizer="x"), dict(column_linear_backend="x"),
-                dict(row_transport="ring"), dict(quant_division="approx"), dict(dit_fused_row_gate=1)):
+                dict(row_transport="ring"), dict(quant_division="approx"), dict(dit_fused_row_gate=1),
+                dict(row_payload="int4"), dict(fc2_max_exchange="ring")):
         with pytest.raises(ValueError):
             H3OperatorPolicy(**bad)
     with pytest.raises(dataclasses.FrozenInstanceError):
         p.fc2_quantizer = "native"
+
+
+def test_policy_max_exchange_default():
+    from h3tp.h3_operator_policy import H3OperatorPolicy
+    p = H3OperatorPolicy()
+    assert p.row_transport == "p2p" and p.fc2_max_exchange == "peer"
+    assert H3OperatorPolicy(fc2_max_exchange="nccl").fc2_max_exchange == "nccl"
+
+
+@pytest.mark.parametrize("width,rows", [(3072, 32768), (512, 1), (264, 77), (13824, 4099)])
+def test_peer_workspace_layout(width, rows):
+    """Flags, partial, final rows and row-maximum slots of the peer workspace: disjoint,
+    256-byte aligned, and large enough for the fp16 partial, the packed INT8 rows
+    (width / 128 groups of 132 bytes) and 8 slots of 8 bytes per row."""
+    from h3tp import peer
+    lay = peer.layout(width, rows)
+    areas = [(0, peer.FLAGS_BYTES), (lay["partial_off"], lay["final_off"]),
+             (lay["final_off"], lay["slots_off"]), (lay["slots_off"], lay["nbytes"])]
+    for (a0, a1), (b0, _) in zip(areas, areas[1:]):
+        assert a1 <= b0
+    for off in (lay["partial_off"], lay["final_off"], lay["slots_off"]):
+        assert off % 256 == 0
+    assert lay["final_off"] - lay["partial_off"] >= rows * width * 2
+    assert lay["final_off"] - lay["partial_off"] >= rows * (width // 128) * 132
+    assert lay["slots_off"] - lay["final_off"] >= rows * width * 2
+    assert lay["nbytes"] - lay["slots_off"] >= rows * 8 * 8
 
 
 def test_tensor_flow_policy():
