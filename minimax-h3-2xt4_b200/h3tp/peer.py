@@ -48,6 +48,12 @@ def available(comm) -> bool:
         return False
 
 
+def next_epoch(epoch: int) -> int:
+    """The epoch after `epoch` in 1 .. 2^32 - 1: the kernels take u32 epochs, and 0 is
+    the tag of the zeroed flags and slots, so it is never used."""
+    return epoch % 0xFFFFFFFF + 1
+
+
 def layout(width: int, rows: int) -> dict:
     """Byte offsets of one rank's workspace buffer for up to `rows` rows of `width`
     columns: flags | partial (fp16 [rows][width], or the packed INT8 rows, which are
@@ -110,7 +116,7 @@ class PeerWorkspace:
         rows = x.shape[0]
         if rows > self.capacity:
             raise ValueError(f"{rows} rows exceed the workspace capacity {self.capacity}")
-        self.max_epoch += 1
+        self.max_epoch = next_epoch(self.max_epoch)
         q, s, _ = ops.swiglu_rotate_quantize_peer(x, self.bases, self.world, self.rank,
                                                   self.slots_off, self.max_epoch, kind=kind,
                                                   division=division)
@@ -120,7 +126,7 @@ class PeerWorkspace:
                           gate=None, labels=None, packed: bool = False):
         """Sums the partials every rank wrote into partial() (or, packed, partial_u8())
         into `residual` (fp16 [rows, width], updated in place on every rank)."""
-        self.epoch += 1
+        self.epoch = next_epoch(self.epoch)
         if packed:
             ops.peer_reduce_int8(self.bases, self.world, self.rank, 0, self.partial_off,
                                  self.final_off, rows, self.width, row_scale, weight_scale,

@@ -34,6 +34,13 @@ def test_policy_max_exchange_default():
     assert H3OperatorPolicy(fc2_max_exchange="nccl").fc2_max_exchange == "nccl"
 
 
+def test_peer_epochs_skip_zero():
+    from h3tp import peer
+    assert peer.next_epoch(0) == 1 and peer.next_epoch(1) == 2
+    assert peer.next_epoch(0xFFFFFFFE) == 0xFFFFFFFF
+    assert peer.next_epoch(0xFFFFFFFF) == 1  # wraps past the zeroed flags' tag
+
+
 @pytest.mark.parametrize("width,rows", [(3072, 32768), (512, 1), (264, 77), (13824, 4099)])
 def test_peer_workspace_layout(width, rows):
     """Flags, partial, final rows and row-maximum slots of the peer workspace: disjoint,
