@@ -45,6 +45,17 @@ def input_kind(x: torch.Tensor, local_k: int | None = None) -> tuple[str, int]:
     return "gateup_f16", width // 2
 
 
+def _checked_input(x: torch.Tensor, mode: str, local_k: int | None):
+    """(kind, local_k) of a valid FC2 input; ValueError otherwise, raised on every rank
+    before any collective (tilelang_swiglu_quant.py:16)."""
+    if mode not in MODES:
+        raise ValueError(mode)
+    kind, kl = input_kind(x, local_k)
+    if kl % 256 or kl == 0:
+        raise ValueError("Whole regular ConvRot256 groups required")
+    return kind, kl
+
+
 def prepare(x: torch.Tensor, comm, mode: str = "fused_stored", *, consume_input: bool = False,
             division: str = "rn", local_k: int | None = None, peer_workspace=None):
     """SwiGLU + ConvRot + global row quantisation (tilelang_swiglu_quant.py:67-92).
@@ -53,12 +64,7 @@ def prepare(x: torch.Tensor, comm, mode: str = "fused_stored", *, consume_input:
     With `peer_workspace` (a peer.PeerWorkspace of this group) and TP>1, one kernel
     rotates, exchanges the row maxima with the other ranks over peer memory and
     quantises: the same codes as either mode, one pass over x."""
-    if mode not in MODES:
-        raise ValueError(mode)
-    kind, kl = input_kind(x, local_k)
-    if kl % 256 or kl == 0:
-        # checked on every rank before the MAX collective (tilelang_swiglu_quant.py:16)
-        raise ValueError("Whole regular ConvRot256 groups required")
+    kind, kl = _checked_input(x, mode, local_k)
     flat = x.reshape(-1, x.shape[-1]).contiguous()
     if C.world_of(comm) == 1:
         q, s, _ = ops.swiglu_rotate_quantize_local(flat, kind, division)
@@ -176,6 +182,7 @@ def row_linear(x, weight, weight_scale, comm, *, mode="fused_stored", scaled_tra
         raise ValueError("Fused row-gate requires scaled FP16 transport")
     shape = x.shape
     ws = None
+    _checked_input(x, mode, weight.shape[1])  # before the workspace's collective steps
     if (peer_max and transport == "p2p" and scaled_transport and finish_fn is None
             and residual is not None and residual.is_contiguous()
             and (payload == "int8_gather" or residual.shape[-1] % 8 == 0)
