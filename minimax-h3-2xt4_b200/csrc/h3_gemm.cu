@@ -416,27 +416,22 @@ H3_DEV void load_scales(const float* w, int64_t n0, int64_t N, int scalar, float
 // Epilogue of one output tile: this warp's 32 TMEM lanes (`row` is the lane's output
 // row) and one EPI_PARTS-th of the tile's 256 accumulator columns.
 // ---------------------------------------------------------------------------
-// have_pre: `pre` holds this lane's row scale and its gate / up weight scales for the
-// tile (SWIGLU), loaded during the previous tile so no epilogue waits for them.
 template <int EPI>
 H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool row_ok, int nb,
-                          int part, float* wsm, float3 pre = float3{}, bool have_pre = false) {
+                          int part, float* wsm) {
   const int64_t N = args.N;
   if (EPI == EPI_SWIGLU) {
     // accumulator columns [0,128) = gate rows, [128,256) = up rows of this tile
     constexpr int GCOLS = (BN / 2) / EPI_PARTS;  // gate columns of this warp
     const int64_t n_base = (int64_t)nb * (BN / 2) + part * GCOLS;
-    const float a = have_pre ? pre.x : (row_ok ? __ldg(args.row_scale + row) : 0.0f);
+    const float a = row_ok ? __ldg(args.row_scale + row) : 0.0f;
     const bool vec4 = args.scale_vec != 0;
     constexpr int SW = 8;  // columns per step: keeps the SwiGLU epilogue within 96 registers
     // This warp's 32 gate and 32 up weight scales, staged in shared memory once per
     // tile (one coalesced load per lane) and read back as broadcasts.
     const int lane = threadIdx.x & 31;
     __syncwarp();
-    if (have_pre) {
-      wsm[lane] = pre.y;
-      wsm[32 + lane] = pre.z;
-    } else {
+    {
       const int64_t nl = n_base + lane;
       wsm[lane] = nl < N ? __ldg(args.weight_scale + nl) : 0.0f;
       wsm[32 + lane] = nl < N ? __ldg(args.weight_scale + N + nl) : 0.0f;
@@ -924,21 +919,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const int part = (warp - 2) >> 2;
     int acc = 0;
     uint32_t acc_phase = 0;
-    // SWIGLU: this lane's row scale and gate / up weight scales of a tile, loaded one
-    // tile ahead (the loads are in flight while the current tile's epilogue runs)
-    auto swiglu_scales = [&](int t) {
-      int mb2, nb2;
-      tile_coords(t, args, mb2, nb2);
-      const int64_t r2 = (int64_t)mb2 * BM2 + (int64_t)rank * BM + quad * 32 + lane;
-      const int64_t nl = (int64_t)nb2 * (BN / 2) + part * ((BN / 2) / EPI_PARTS) + lane;
-      float3 v;
-      v.x = r2 < args.M ? __ldg(args.row_scale + r2) : 0.0f;
-      v.y = nl < args.N ? __ldg(args.weight_scale + nl) : 0.0f;
-      v.z = nl < args.N ? __ldg(args.weight_scale + args.N + nl) : 0.0f;
-      return v;
-    };
-    float3 pre = float3{};
-    if (EPI == EPI_SWIGLU && cluster_id < total_tiles) pre = swiglu_scales(cluster_id);
     for (int tile = cluster_id; tile < total_tiles; tile += clusters) {
       int mb, nb;
       tile_coords(tile, args, mb, nb);
@@ -946,9 +926,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const int64_t row = (int64_t)mb * BM2 + (int64_t)rank * BM + quad * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-      const float3 cur = pre;
-      if (EPI == EPI_SWIGLU && tile + clusters < total_tiles) pre = swiglu_scales(tile + clusters);
-      epilogue_tile<EPI>(args, tbase, row, row < args.M, nb, part, wsm, cur, EPI == EPI_SWIGLU);
+      epilogue_tile<EPI>(args, tbase, row, row < args.M, nb, part, wsm);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(cluster_addr(smem_u32(tempty + acc), 0));
