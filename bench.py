@@ -56,6 +56,9 @@ def parse():
                     help="BASELINE config 5 shape sweep on one GPU: one JSON line per point")
     ap.add_argument("--sweep-producers", action="store_true",
                     help="only the activation-producer lines of the sweep")
+    ap.add_argument("--fc1-epilogue", choices=["swiglu", "fp16"], default="swiglu",
+                    help="FC1 writes the FP32 SwiGLU activation, or fp16 [gate|up] with the "
+                         "SwiGLU applied in the FC2 producer (the reference's form)")
     ap.add_argument("--max-exchange", choices=["peer", "nccl"], default="peer",
                     help="FC2 row maxima at TP > 1: in-kernel over peer memory, or NCCL MAX")
     ap.add_argument("--payload", choices=["fp16", "int8_gather"], default="fp16",
@@ -283,7 +286,8 @@ def run_ours(args):
     from h3tp.h3_operator_policy import H3OperatorPolicy
     mlp = TPDiTMLPINT8(hidden, ffn, rank, world, device=dev, comm=comm,
                        policy=H3OperatorPolicy(row_payload=args.payload,
-                                               fc2_max_exchange=args.max_exchange))
+                                               fc2_max_exchange=args.max_exchange,
+                                               fc1_swiglu_epilogue=args.fc1_epilogue == "swiglu"))
     mlp.fc1.load_shard_from_full(w1, s1)
     mlp.fc2.load_shard_from_full(w2, s2)
     h = h_cpu.to(dev)
@@ -300,8 +304,12 @@ def run_ours(args):
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-        act = ops.int8_gemm_swiglu(codes, mlp.fc1.weight, row_scale,
-                                   mlp.fc1.weight_scale.reshape(-1), None, torch.float32)
+        if args.fc1_epilogue == "swiglu":
+            act = ops.int8_gemm_swiglu(codes, mlp.fc1.weight, row_scale,
+                                       mlp.fc1.weight_scale.reshape(-1), None, torch.float32)
+        else:
+            act = ops.int8_gemm_column(codes, mlp.fc1.weight, row_scale,
+                                       mlp.fc1.weight_scale.reshape(-1))
         if record:
             e1.record(stream)
             fc1_events.append((e0, e1))
@@ -440,7 +448,8 @@ def run_ours(args):
     tfile = ROOT / "profiles" / "roofline_traffic.json"
     if tfile.exists():
         try:
-            traffic = json.loads(tfile.read_text()).get(f"fc1_swiglu_gemm_tp{world}")
+            traffic = json.loads(tfile.read_text()).get(f"fc1_swiglu_gemm_tp{world}") \
+                if args.fc1_epilogue == "swiglu" else None
         except ValueError:
             traffic = None
     line = {
@@ -456,8 +465,10 @@ def run_ours(args):
                    "row_transport": mlp.fc2.operator_policy.row_transport,
                    "row_payload": mlp.fc2.operator_policy.row_payload,
                    "fc2_max_exchange": mlp.fc2.operator_policy.fc2_max_exchange,
+                   "fc1_epilogue": args.fc1_epilogue,
                    "l2": "inputs larger than L2 (h = 201 MB per step), no flush"},
-        "roofline": {"kernel": "gemm_i8_kernel<EPI_SWIGLU> (FC1)", "bound": "tensor",
+        "roofline": {"kernel": ("gemm_i8_pair_kernel<EPI_SWIGLU> (FC1)" if args.fc1_epilogue == "swiglu"
+                               else "gemm_i8_pair_kernel<EPI_COLUMN> (FC1)"), "bound": "tensor",
                      "achieved": round(achieved, 2), "peak": round(int8_peak, 1), "unit": "TOPS",
                      "frac": round(achieved / int8_peak, 4), "traffic": traffic,
                      "ms_per_launch": round(fc1_ms, 4), "ops_per_launch": fc1_ops,
