@@ -132,3 +132,58 @@ def test_transport_shift_generalisation():
     assert transport.shift_for(7168) == 12 and transport.shift_for(3584) == 11
     assert transport.shift_for(8192 // 8, 8) == transport.shift_for(8192 // 2, 2) == 12
     assert ops.transport_shift(3072) == 10
+
+
+class _FakeComm:
+    """Duck-typed torch.distributed of world 2 that records collective calls."""
+    def __init__(self):
+        self.calls = []
+
+    def is_initialized(self):
+        return True
+
+    def get_world_size(self):
+        return 2
+
+    def get_rank(self):
+        return 0
+
+    def all_reduce(self, t, op=None):
+        self.calls.append("all_reduce")
+
+
+class _FakeWorkspace:
+    def __init__(self):
+        self.seen = []
+
+    def quantize_rows(self, x, kind, division):
+        self.seen.append((tuple(x.shape), kind, division))
+        rows, width = x.shape[0], (x.shape[1] // 2 if kind == "gateup_f16" else x.shape[1])
+        return (torch.zeros((rows, width), dtype=torch.int8),
+                torch.ones((rows, 1), dtype=torch.float32))
+
+
+@pytest.mark.parametrize("dtype,width,kind", [(torch.float16, 1024, "gateup_f16"),
+                                              (torch.float32, 512, "act_f32")])
+def test_prepare_with_peer_workspace_takes_one_pass(dtype, width, kind):
+    """At TP > 1 with a peer workspace, prepare() hands the whole activation to the
+    workspace's single-pass producer and issues no NCCL MAX; consume_input releases the
+    caller's storage afterwards (tilelang_swiglu_quant.py:81-85)."""
+    from h3tp import swiglu_quant
+    comm, ws = _FakeComm(), _FakeWorkspace()
+    x = torch.zeros((3, 5, width), dtype=dtype)
+    q, s = swiglu_quant.prepare(x, comm, "fused_recompute", consume_input=True, division="rn",
+                                local_k=512, peer_workspace=ws)
+    assert ws.seen == [((15, width), kind, "rn")]
+    assert comm.calls == []
+    assert q.shape == (15, 512) and s.shape == (15, 1)
+    assert x.numel() == 0  # storage released
+
+
+def test_prepare_rejects_partial_groups_before_the_workspace():
+    from h3tp import swiglu_quant
+    comm, ws = _FakeComm(), _FakeWorkspace()
+    with pytest.raises(ValueError):
+        swiglu_quant.prepare(torch.zeros((4, 2 * 384), dtype=torch.float16), comm,
+                             peer_workspace=ws)
+    assert ws.seen == [] and comm.calls == []
