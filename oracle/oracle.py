@@ -11,7 +11,6 @@ passed as numpy.float16 (bit-compatible with torch.float16).
 from __future__ import annotations
 
 import ctypes
-from pathlib import Path
 
 import numpy as np
 
