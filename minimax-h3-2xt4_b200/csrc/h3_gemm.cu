@@ -467,9 +467,9 @@ H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool ro
           vg = __fadd_rn(vg, bg[j]);
           vu = __fadd_rn(vu, bu[j]);
         }
-        // both fp16 roundings in one packed conversion (each half rounds on its own)
-        const float2 gu = __half22float2(__floats2half2_rn(vg, vu));
-        y[j] = swiglu_f32(gu.x, gu.y);
+        const float g = __half2float(__float2half_rn(vg));
+        const float u = __half2float(__float2half_rn(vu));
+        y[j] = swiglu_f32(g, u);
       }
       if (row_ok) {
         if (args.out_kind == H3_OUT_F32)
