@@ -3,8 +3,10 @@
  *
  * Every entry point takes raw device pointers, element counts and a cudaStream_t
  * (passed as void*), enqueues its kernels on that stream and returns an int status
- * (H3_OK or an H3_ERR_* code).  Nothing here allocates the caller's tensors:
- * outputs are written into caller-provided device buffers, the way the reference's
+ * (H3_OK or an H3_ERR_* code).  It runs on the device that owns its first device
+ * pointer and leaves the calling thread's current device as it found it.  Nothing
+ * here allocates the caller's tensors: outputs are written into caller-provided
+ * device buffers, the way the reference's
  * native extension (comfy_kitchen._C.cublas_gemm_int8 / dequantize_int8_linear,
  * called from patches/optimized_tp.py:34-43 and patches/parallel_int8.py:53-65)
  * receives DLPack tensors plus a raw stream.  Geometry is checked before any launch
@@ -60,8 +62,14 @@ enum {
 int h3_abi_version(void);
 const char* h3_status_string(int status);
 /* Reads, then clears, the device-side error word that bounded waits set when
- * they give up.  Synchronises the device.  *code = 0 when nothing failed. */
+ * they give up.  Synchronises the device (not during stream capture).  *code = 0
+ * when nothing failed. */
 int h3_device_error(int device, int* code);
+/* The same word as it stands, without synchronising or clearing: the word lives in
+ * host-mapped page-locked memory that kernels write with a system-scope store, so the
+ * host can poll it once per operator call at no device cost.  *code = 0 when nothing
+ * has failed (or nothing has run yet on that device). */
+int h3_device_error_peek(int device, int* code);
 
 /* ----------------------------------------------------------------------------
  * Column path (QKV / FC1): ColumnParallelLinearINT8.forward, tp_dit.py:69-96
@@ -320,7 +328,8 @@ int h3_swiglu_rotate_quantize_peer(const void* x, int input_kind, int64_t rows,
  * capture.  All calls on a device share the array: calls whose GPU work overlaps race
  * and must be serialised by the caller (one stream, or events).
  * h3_column_linear_noalloc_error reads (without clearing) the error word of the last
- * call; the next call clears it. */
+ * call; the next call clears it.  It synchronises the device, so it must not be called
+ * while a stream of that device is being captured. */
 int h3_column_linear_noalloc(const void* x_f16, int64_t m, int64_t k, int convrot,
                              const int8_t* w, int64_t n, const float* weight_scale,
                              int64_t weight_scale_len, const float* bias, void* out_f16,

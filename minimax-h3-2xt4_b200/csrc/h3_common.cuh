@@ -358,6 +358,14 @@ H3_DEV float warp_max(float v) {
   return v;
 }
 
+// Records an error code in the library's error word.  The word sits in host-mapped
+// pinned memory (the no-allocation entry keeps its own in static device memory), so
+// this is a plain system-scope store rather than an atomic: any non-zero code means a
+// failure, and the host can read it while kernels are still running.
+H3_DEV void report_error(int* err, int code) {
+  asm volatile("st.relaxed.sys.global.s32 [%0], %1;" ::"l"(err), "r"(code) : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // Output stage shared by the row epilogues.
 //   y: FP32 dequantised row output of one element
@@ -376,7 +384,7 @@ H3_DEV float gate_value(const RowOut& o, int64_t r, int64_t c, int64_t width) {
   if (o.gate == nullptr) return 1.0f;
   int64_t lab = o.labels ? (int64_t)__ldg(o.labels + r) : 0;
   if (lab < 0 || lab >= o.gate_rows) {
-    atomicExch(o.err, H3_ERR_INVALID);
+    report_error(o.err, H3_ERR_INVALID);
     lab = 0;
   }
   return __ldg(o.gate + lab * width + c);
@@ -404,9 +412,24 @@ H3_DEV void row_store(const RowOut& o, int64_t r, int64_t c, int64_t width, floa
 // ---------------------------------------------------------------------------
 namespace h3host {
 
-int bind_device_of(const void* ptr, int* device);  // cudaSetDevice to the pointer's device
+// Makes a device current for the lifetime of the object and, when it goes out of
+// scope, makes the caller's previous device current again: an entry point never leaves
+// the calling thread on another GPU.
+class DeviceScope {
+ public:
+  DeviceScope() = default;
+  DeviceScope(const DeviceScope&) = delete;
+  DeviceScope& operator=(const DeviceScope&) = delete;
+  ~DeviceScope();
+  int bind(const void* ptr, int* device);  // the device owning ptr (host pointers: INVALID)
+  int bind_index(int device);              // a device by ordinal
+
+ private:
+  int prev_ = -1;
+};
 int sm_count(int device);
-int* error_word(int device);                         // lazily created device word
+int* error_word(int device);       // device view of the lazily created mapped error word
+int* error_word_host(int device);  // host view of it (nullptr before its first use)
 int check_launch();                                  // maps cudaGetLastError to a status
 
 inline bool aligned(const void* p, unsigned a) { return ((uintptr_t)p % a) == 0; }

@@ -131,7 +131,7 @@ H3_DEV bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, i
       if (honour_abort && *abort_flag) return false;
       if (globaltimer() - t0 > TIMEOUT_NS) {
         *abort_flag = 1;
-        atomicExch(err, H3_ERR_TIMEOUT);
+        report_error(err, H3_ERR_TIMEOUT);
         return false;
       }
     }
@@ -537,7 +537,7 @@ H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool ro
         args.row.gate != nullptr && args.row.labels != nullptr) {
       lab = __ldg(args.row.labels + row);
       if (lab < 0 || lab >= args.row.gate_rows) {
-        atomicExch(args.row.err, H3_ERR_INVALID);
+        report_error(args.row.err, H3_ERR_INVALID);
         lab = 0;
       }
     }
@@ -1003,16 +1003,28 @@ static void set_raster(Args& a, int64_t a_block_bytes, int64_t b_block_bytes) {
   a.group_n = n_cost < m_cost ? (int)gn : 0;
 }
 
+// Geometry every GEMM launch accepts: K a multiple of 16, M < 2^31, N <= 2^24,
+// K <= 2^20, 16-byte aligned operands and a tile count that fits an int.
+template <int EPI>
+static bool gemm_geometry_ok(const int8_t* q, const int8_t* w, int64_t M, int64_t N, int64_t K) {
+  if (q == nullptr || w == nullptr || M < 0 || N <= 0 || K <= 0 || K % 16 != 0) return false;
+  if (!h3host::aligned(q, 16) || !h3host::aligned(w, 16)) return false;
+  if (M > (int64_t)1 << 31 || N > (int64_t)1 << 24 || K > (int64_t)1 << 20) return false;
+  const bool pair = M > BM;
+  const int64_t tile_m = pair ? BM2 : BM, tile_n = EPI == EPI_SWIGLU ? BN / 2 : BN;
+  return ((M + tile_m - 1) / tile_m) * ((N + tile_n - 1) / tile_n) <= INT32_MAX;
+}
+
+// Enqueues one GEMM.  args.err, when the caller set it, replaces the library's device
+// error word (the no-allocation entry keeps its own in static memory).
 template <int EPI>
 static int launch(const int8_t* q, const int8_t* w, int64_t M, int64_t N, int64_t K, Args args,
                   cudaStream_t stream) {
-  if (q == nullptr || w == nullptr || M < 0 || N <= 0 || K <= 0 || K % 16 != 0)
-    return H3_ERR_INVALID;
-  if (!h3host::aligned(q, 16) || !h3host::aligned(w, 16)) return H3_ERR_INVALID;
-  if (M > (int64_t)1 << 31 || N > (int64_t)1 << 24 || K > (int64_t)1 << 20) return H3_ERR_INVALID;
+  if (!gemm_geometry_ok<EPI>(q, w, M, N, K)) return H3_ERR_INVALID;
   if (M == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(q, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(q, &dev)) return s;
   if (!device_is_sm100(dev)) return H3_ERR_UNSUPPORTED;
   // CTA pairs (256-row tiles) once there is more than one 128-row block; a single
   // CTA per tile below that.
@@ -1035,11 +1047,10 @@ static int launch(const int8_t* q, const int8_t* w, int64_t M, int64_t N, int64_
   args.tiles_n = (int)((N + tile_n - 1) / tile_n);
   args.num_kb = (int)((K + BK - 1) / BK);
   set_raster(args, (pair ? BM2 : BM) * K, (EPI == EPI_SWIGLU ? 2 * tile_n : tile_n) * K);
-  args.err = h3host::error_word(dev);
+  if (args.err == nullptr) args.err = h3host::error_word(dev);
   if (args.err == nullptr) return H3_ERR_CUDA;
   if (args.row.err == nullptr) args.row.err = args.err;
   const int64_t tiles = (int64_t)args.tiles_m * args.tiles_n;
-  if (tiles > INT32_MAX) return H3_ERR_INVALID;
   const int sms = h3host::sm_count(dev);
   static bool attr_set[64][2] = {{false}};
   if (pair) {
@@ -1212,19 +1223,24 @@ extern "C" int h3_column_linear_noalloc(const void* x_f16, int64_t m, int64_t k,
                                         int64_t weight_scale_len, const float* bias,
                                         void* out_f16, void* stream) {
   using namespace h3::noalloc;
-  if (x_f16 == nullptr || w == nullptr || weight_scale == nullptr || out_f16 == nullptr ||
-      m < 0 || k <= 0 || n <= 0 || k % 16 != 0 ||
-      (weight_scale_len != 1 && weight_scale_len != n) || !h3host::aligned(out_f16, 16) ||
-      !h3host::aligned(w, 16))
-    return H3_ERR_INVALID;
   // layout: [error word | row scales | codes], each 256-byte aligned
   const int64_t scale_off = 256;
-  const int64_t code_off = scale_off + align256(m * 4);
-  if (m > ((int64_t)1 << 31) || code_off + m * k > (int64_t)H3_NOALLOC_SCRATCH_BYTES)
+  const int64_t code_off = m >= 0 ? scale_off + align256(m * 4) : 0;
+  // Everything the two launches below would refuse is refused here, before either runs:
+  // the GEMM's geometry (checked on the codes' future address), the quantiser's width
+  // rules, and the size of the static scratch.
+  if (x_f16 == nullptr || w == nullptr || weight_scale == nullptr || out_f16 == nullptr ||
+      m < 0 || m > ((int64_t)1 << 31) || (weight_scale_len != 1 && weight_scale_len != n) ||
+      !h3host::aligned(x_f16, 16) || !h3host::aligned(out_f16, 16) ||
+      !gemm_geometry_ok<EPI_COLUMN>(reinterpret_cast<const int8_t*>(256), w, m, n, k) ||
+      (convrot ? k % 256 != 0 : k % 16 != 0) || k > 4 * 512 * 16)
+    return H3_ERR_INVALID;
+  if (code_off + m * k > (int64_t)H3_NOALLOC_SCRATCH_BYTES)
     return H3_ERR_INVALID;  // beyond the static scratch: use h3_column_quantize + h3_int8_gemm_column
   if (m == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(x_f16, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(x_f16, &dev)) return s;
   if (!device_is_sm100(dev)) return H3_ERR_UNSUPPORTED;
   uint8_t* base = scratch_ptr(dev);
   if (base == nullptr) return H3_ERR_CUDA;
@@ -1245,43 +1261,15 @@ extern "C" int h3_column_linear_noalloc(const void* x_f16, int64_t m, int64_t k,
   args.scalar_w = weight_scale_len == 1;
   args.bias = bias;
   args.scale_vec = n % 4 == 0 && h3host::aligned(weight_scale, 16);
-  const bool pair = m > BM;
-  CUtensorMap tA, tB;
-  if (!make_map(&tA, q, m, k, BM)) return H3_ERR_INVALID;
-  if (!make_map(&tB, w, n, k, pair ? BN / 2 : BN)) return H3_ERR_INVALID;
-  args.M = m;
-  args.N = n;
-  args.K = k;
-  args.tiles_m = (int)((m + (pair ? BM2 : BM) - 1) / (pair ? BM2 : BM));
-  args.tiles_n = (int)((n + BN - 1) / BN);
-  args.num_kb = (int)((k + BK - 1) / BK);
-  set_raster(args, (pair ? BM2 : BM) * k, BN * k);
   args.err = err;
-  args.row.err = err;
-  const int64_t tiles = (int64_t)args.tiles_m * args.tiles_n;
-  const int sms = h3host::sm_count(dev);
-  if (pair) {
-    if (cudaFuncSetAttribute(gemm_i8_pair_kernel<EPI_COLUMN>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES) != cudaSuccess)
-      return H3_ERR_CUDA;
-    const int grid = 2 * (int)std::min<int64_t>(tiles, sms / 2);
-    gemm_i8_pair_kernel<EPI_COLUMN><<<grid, THREADS, SMEM2_BYTES, st>>>(tA, tB, tB, args);
-  } else {
-    if (cudaFuncSetAttribute(gemm_i8_kernel<EPI_COLUMN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             SMEM_BYTES) != cudaSuccess)
-      return H3_ERR_CUDA;
-    const int grid = (int)std::min<int64_t>(tiles, sms);
-    gemm_i8_kernel<EPI_COLUMN><<<grid, THREADS, SMEM_BYTES, st>>>(tA, tB, tB, args);
-  }
-  return h3host::check_launch();
+  return launch<EPI_COLUMN>(q, w, m, n, k, args, st);
 }
 
 extern "C" int h3_column_linear_noalloc_error(int device, int* code) {
   if (code == nullptr) return H3_ERR_INVALID;
   *code = 0;
-  int cur = -1;
-  cudaGetDevice(&cur);
-  if (cur != device && cudaSetDevice(device) != cudaSuccess) return H3_ERR_CUDA;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind_index(device)) return s;
   uint8_t* base = h3::noalloc::scratch_ptr(device);
   if (base == nullptr) return H3_ERR_CUDA;
   if (cudaDeviceSynchronize() != cudaSuccess) return H3_ERR_CUDA;

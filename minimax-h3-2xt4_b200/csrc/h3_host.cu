@@ -10,10 +10,29 @@ namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_mutex;
 int g_sm_count[kMaxDevices] = {0};
-int* g_error_word[kMaxDevices] = {nullptr};
+int* g_error_word[kMaxDevices] = {nullptr};  // device view of the mapped word
+int* g_error_host[kMaxDevices] = {nullptr};  // host view of the same word
 }  // namespace
 
-int bind_device_of(const void* ptr, int* device) {
+DeviceScope::~DeviceScope() {
+  if (prev_ >= 0) cudaSetDevice(prev_);
+}
+
+int DeviceScope::bind_index(int device) {
+  if (device < 0 || device >= kMaxDevices) return H3_ERR_INVALID;
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess) {
+    cudaGetLastError();
+    return H3_ERR_CUDA;
+  }
+  if (cur != device) {
+    if (cudaSetDevice(device) != cudaSuccess) return H3_ERR_CUDA;
+    if (prev_ < 0) prev_ = cur;
+  }
+  return H3_OK;
+}
+
+int DeviceScope::bind(const void* ptr, int* device) {
   cudaPointerAttributes attr;
   cudaError_t e = cudaPointerGetAttributes(&attr, ptr);
   if (e != cudaSuccess) {
@@ -22,11 +41,7 @@ int bind_device_of(const void* ptr, int* device) {
   }
   if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged)
     return H3_ERR_INVALID;  // host pointers are rejected: the path has no CPU fallback
-  if (attr.device < 0 || attr.device >= kMaxDevices) return H3_ERR_INVALID;
-  int cur = -1;
-  if (cudaGetDevice(&cur) != cudaSuccess || cur != attr.device) {
-    if (cudaSetDevice(attr.device) != cudaSuccess) return H3_ERR_CUDA;
-  }
+  if (int s = bind_index(attr.device)) return s;
   *device = attr.device;
   return H3_OK;
 }
@@ -41,16 +56,36 @@ int sm_count(int device) {
   return g_sm_count[device];
 }
 
+// The error word of a device: one int of host-mapped, page-locked memory, written by
+// kernels with a system-scope store and read by the host directly (h3_device_error_peek
+// needs no synchronisation).  Created on first use with the device current.
 int* error_word(int device) {
   if (device < 0 || device >= kMaxDevices) return nullptr;
   std::lock_guard<std::mutex> lock(g_mutex);
   if (g_error_word[device] == nullptr) {
-    int* p = nullptr;
-    if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
-    if (cudaMemset(p, 0, sizeof(int)) != cudaSuccess) return nullptr;
-    g_error_word[device] = p;
+    int* host = nullptr;
+    if (cudaHostAlloc(reinterpret_cast<void**>(&host), sizeof(int),
+                      cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    *reinterpret_cast<volatile int*>(host) = 0;
+    int* dev = nullptr;
+    if (cudaHostGetDevicePointer(reinterpret_cast<void**>(&dev), host, 0) != cudaSuccess) {
+      cudaGetLastError();
+      cudaFreeHost(host);
+      return nullptr;
+    }
+    g_error_host[device] = host;
+    g_error_word[device] = dev;
   }
   return g_error_word[device];
+}
+
+int* error_word_host(int device) {
+  if (device < 0 || device >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  return g_error_host[device];
 }
 
 int check_launch() {
@@ -76,15 +111,19 @@ extern "C" const char* h3_status_string(int status) {
 extern "C" int h3_device_error(int device, int* code) {
   if (code == nullptr) return H3_ERR_INVALID;
   *code = 0;
-  int cur = -1;
-  cudaGetDevice(&cur);
-  if (cur != device && cudaSetDevice(device) != cudaSuccess) return H3_ERR_CUDA;
-  int* w = h3host::error_word(device);
-  if (w == nullptr) return H3_ERR_CUDA;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind_index(device)) return s;
+  if (h3host::error_word(device) == nullptr) return H3_ERR_CUDA;
+  volatile int* w = h3host::error_word_host(device);
   if (cudaDeviceSynchronize() != cudaSuccess) return H3_ERR_CUDA;
-  int v = 0;
-  if (cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return H3_ERR_CUDA;
-  if (cudaMemset(w, 0, sizeof(int)) != cudaSuccess) return H3_ERR_CUDA;
-  *code = v;
+  *code = *w;
+  *w = 0;
+  return H3_OK;
+}
+
+extern "C" int h3_device_error_peek(int device, int* code) {
+  if (code == nullptr || device < 0) return H3_ERR_INVALID;
+  volatile int* w = h3host::error_word_host(device);
+  *code = w == nullptr ? 0 : *w;
   return H3_OK;
 }

@@ -183,7 +183,7 @@ H3_DEV uint4 epilogue_chunk(const Args& a, const int32_t (&q)[8], int64_t r, int
   if (a.gate != nullptr) {
     int64_t lab = a.labels ? (int64_t)__ldg(a.labels + r) : 0;
     if (lab < 0 || lab >= a.gate_rows) {
-      atomicExch(a.err, H3_ERR_INVALID);
+      report_error(a.err, H3_ERR_INVALID);
       lab = 0;
     }
     const float4* gp = reinterpret_cast<const float4*>(a.gate + lab * a.width + c0);
@@ -247,7 +247,7 @@ __global__ void __launch_bounds__(THREADS) reduce_kernel(const Args a) {
         if (w != a.rank) reinterpret_cast<uint4*>(a.bases[w] + a.final_off)[e] = y;
     }
   } else if (threadIdx.x == 0) {
-    atomicExch(a.err, H3_ERR_TIMEOUT);
+    report_error(a.err, H3_ERR_TIMEOUT);
   }
   // Every thread fences its stores to the peers; then count this CTA (failures in the
   // high half-word); the last one resets the counter and, when every CTA succeeded,
@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(THREADS) reduce_kernel(const Args a) {
 template <int W>
 __global__ void __launch_bounds__(THREADS) gather_kernel(const Args a) {
   if (!wait_all(a, DONE, true)) {
-    if (threadIdx.x == 0) atomicExch(a.err, H3_ERR_TIMEOUT);
+    if (threadIdx.x == 0) report_error(a.err, H3_ERR_TIMEOUT);
     return;
   }
   const int64_t chunks = a.width >> 3;
@@ -324,7 +324,8 @@ int run(const void* const* bases, int world, int rank, int64_t flags_off, int64_
     a.bases[w] = reinterpret_cast<uint64_t>(bases[w]);
   }
   int dev;
-  if (int s = h3host::bind_device_of(residual_f16, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(residual_f16, &dev)) return s;
   a.flags_off = flags_off;
   a.partial_off = partial_off;
   a.final_off = final_off;

@@ -72,7 +72,7 @@ H3_DEV float peer_wait(const PeerMax& pm, int64_t row, float m, float* red,
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
       if (deadline == 0) deadline = now + PEER_TIMEOUT_NS;
       if (now > deadline) {
-        atomicExch(pm.err, H3_ERR_TIMEOUT);
+        report_error(pm.err, H3_ERR_TIMEOUT);
         break;
       }
       __nanosleep(32);
@@ -419,7 +419,7 @@ H3_DEV void modulated_norm_pairs(f32x2 (&v)[NP][16], const int64_t (&blk)[NP][2]
   const float inv = __frsqrt_rn(__fadd_rn(__fmul_rn(total, na.inv_width), na.eps));
   int64_t lab = na.labels ? (int64_t)__ldg(na.labels + row) : 0;
   if (lab < 0 || lab >= na.mod_rows) {
-    atomicExch(na.err, H3_ERR_INVALID);
+    report_error(na.err, H3_ERR_INVALID);
     lab = 0;
   }
   const float* sh = na.shift + lab * width;
@@ -673,7 +673,8 @@ extern "C" int h3_swiglu_rotate_max(const void* x, int input_kind, int64_t rows,
   if (rotated != nullptr && !h3host::aligned(rotated, 16)) return H3_ERR_INVALID;
   if (rows == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(x, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(x, &dev)) return s;
   return dispatch_kind<MODE_MAX>(input_kind, x, rows, width, rotated, row_max, nullptr, 0,
                                  nullptr, nullptr, (cudaStream_t)stream);
 }
@@ -687,7 +688,8 @@ extern "C" int h3_swiglu_rotate_quantize(const void* x, int input_kind, int64_t 
     return H3_ERR_INVALID;
   if (rows == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(x, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(x, &dev)) return s;
   return dispatch_kind<MODE_QUANT>(input_kind, x, rows, width, nullptr, nullptr, row_max,
                                    division, q, scale, (cudaStream_t)stream);
 }
@@ -701,7 +703,8 @@ extern "C" int h3_swiglu_rotate_quantize_local(const void* x, int input_kind, in
     return H3_ERR_INVALID;
   if (rows == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(x, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(x, &dev)) return s;
   return dispatch_kind<MODE_LOCAL>(input_kind, x, rows, width, nullptr, row_max, nullptr,
                                    division, q, scale, (cudaStream_t)stream);
 }
@@ -724,7 +727,8 @@ extern "C" int h3_swiglu_rotate_quantize_peer(const void* x, int input_kind, int
   }
   if (rows == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(x, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(x, &dev)) return s;
   pm.slots_off = slots_off;
   pm.world = world;
   pm.rank = rank;
@@ -751,7 +755,8 @@ extern "C" int h3_column_quantize(const void* x_f16, int64_t rows, int64_t k, in
   if (!h3host::aligned(x_f16, 16) || !h3host::aligned(q, 16)) return H3_ERR_INVALID;
   if (rows == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(x_f16, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(x_f16, &dev)) return s;
   const RowTeam t = row_team(k);
   const size_t smem = producer_smem(t.threads);
   const int grid = (int)std::min<int64_t>(rows, 1 << 20);
@@ -786,7 +791,8 @@ extern "C" int h3_row_quantize(const float* rotated, int64_t rows, int64_t width
     return H3_ERR_INVALID;
   if (rows == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(rotated, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(rotated, &dev)) return s;
   const int64_t total = rows * width;
   const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)h3host::sm_count(dev) * 16);
   row_quantize_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(rotated, rows, width, stride,
@@ -799,7 +805,8 @@ extern "C" int h3_expf_compare(const float* x, int64_t n, float* ours, float* cu
   if (x == nullptr || ours == nullptr || cuda == nullptr || n < 0) return H3_ERR_INVALID;
   if (n == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(x, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(x, &dev)) return s;
   const int grid = (int)std::min<int64_t>((n + 255) / 256, 4096);
   expf_compare_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(x, n, ours, cuda);
   return h3host::check_launch();
@@ -810,7 +817,8 @@ extern "C" int h3_silu_compare(const float* g, int64_t n, float* fast, float* ie
   if (g == nullptr || fast == nullptr || ieee == nullptr || n < 0) return H3_ERR_INVALID;
   if (n == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(g, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(g, &dev)) return s;
   const int grid = (int)std::min<int64_t>((n + 255) / 256, 4096);
   silu_compare_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(g, n, fast, ieee, cuda);
   return h3host::check_launch();
@@ -822,7 +830,8 @@ extern "C" int h3_quant_compare(const float* x, const float* scale, int64_t n, i
     return H3_ERR_INVALID;
   if (n == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(x, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(x, &dev)) return s;
   const int grid = (int)std::min<int64_t>((n + 255) / 256, (int64_t)h3host::sm_count(dev) * 16);
   quant_compare_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(x, scale, n, fast, ieee);
   return h3host::check_launch();
@@ -846,7 +855,8 @@ extern "C" int h3_modulated_norm_quantize(const void* x_f16, int64_t rows, int64
     return H3_ERR_INVALID;
   if (rows == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(x_f16, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(x_f16, &dev)) return s;
   NormArgs na{norm_weight, shift, scale, labels, mod_rows, eps,
               (float)(1.0 / (double)width), reinterpret_cast<__half*>(h_f16),
               h3host::error_word(dev)};

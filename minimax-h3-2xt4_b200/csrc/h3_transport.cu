@@ -221,7 +221,8 @@ extern "C" int h3_fp16_encode(const int32_t* partial, int64_t n, int shift, void
     return H3_ERR_INVALID;
   if (n == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(partial, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(partial, &dev)) return s;
   const float factor = ldexpf(1.0f, -shift);
   fp16_encode_kernel<<<elementwise_grid(n, dev), 256, 0, (cudaStream_t)stream>>>(
       partial, n, factor, reinterpret_cast<__half*>(out_f16));
@@ -234,7 +235,8 @@ extern "C" int h3_fp16_decode(const void* payload_f16, int64_t n, int shift, int
     return H3_ERR_INVALID;
   if (n == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(payload_f16, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(payload_f16, &dev)) return s;
   const float factor = ldexpf(1.0f, shift);
   fp16_decode_kernel<<<elementwise_grid(n, dev), 256, 0, (cudaStream_t)stream>>>(
       reinterpret_cast<const __half*>(payload_f16), n, factor, out);
@@ -262,7 +264,8 @@ extern "C" int h3_row_reduce_finish(const void* parts_f16, int world, int64_t pa
   }
   if (rows == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(parts_f16, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(parts_f16, &dev)) return s;
   RowOut o{out_kind, out, reinterpret_cast<__half*>(residual_f16), gate, gate_rows, labels,
            h3host::error_word(dev)};
   if (o.err == nullptr) return H3_ERR_CUDA;
@@ -289,7 +292,8 @@ extern "C" int h3_column_dequantize(const int32_t* acc, int64_t rows, int64_t wi
     return H3_ERR_INVALID;
   if (rows == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(acc, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(acc, &dev)) return s;
   column_dequantize_kernel<<<elementwise_grid(rows * width, dev), 256, 0,
                              (cudaStream_t)stream>>>(acc, rows, width, row_scale, weight_scale,
                                                      weight_scale_len == 1,
@@ -307,7 +311,8 @@ extern "C" int h3_dequantize_i32(const int32_t* acc, int64_t rows, int64_t width
     return H3_ERR_INVALID;
   if (rows == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(acc, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(acc, &dev)) return s;
   dequantize_i32_kernel<<<elementwise_grid(rows * width, dev), 256, 0, (cudaStream_t)stream>>>(
       acc, rows, width, row_scale, weight_scale, weight_scale_len == 1, bias, out_kind, out);
   return h3host::check_launch();
@@ -323,7 +328,8 @@ extern "C" int h3_gated_add(const void* branch, int branch_kind, int64_t rows, i
     return H3_ERR_INVALID;
   if (rows == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(branch, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(branch, &dev)) return s;
   RowOut o{H3_OUT_RESIDUAL, nullptr, reinterpret_cast<__half*>(residual_f16), gate, gate_rows,
            labels, h3host::error_word(dev)};
   if (o.err == nullptr) return H3_ERR_CUDA;
@@ -339,7 +345,8 @@ extern "C" int h3_pack8(const int32_t* partial, int64_t rows, int64_t width, voi
     return H3_ERR_INVALID;
   if (rows == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(partial, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(partial, &dev)) return s;
   pack8_kernel<<<elementwise_grid(rows * (width / 128) * 32, dev), 256, 0, (cudaStream_t)stream>>>(
       partial, rows, width, reinterpret_cast<uint8_t*>(out_u8));
   return h3host::check_launch();
@@ -369,7 +376,8 @@ extern "C" int h3_unpack8_finish(const void* parts_u8, int world, int64_t part_s
   }
   if (rows == 0) return H3_OK;
   int dev;
-  if (int s = h3host::bind_device_of(parts_u8, &dev)) return s;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(parts_u8, &dev)) return s;
   RowOut o{out_kind, out, reinterpret_cast<__half*>(residual_f16), gate, gate_rows, labels,
            h3host::error_word(dev)};
   if (o.err == nullptr) return H3_ERR_CUDA;

@@ -39,6 +39,7 @@ SIGNATURES = {
     "h3_abi_version": [],
     "h3_status_string": [_I],
     "h3_device_error": [_I, _P],
+    "h3_device_error_peek": [_I, _P],
     "h3_column_quantize": [_P, _I64, _I64, _I, _P, _P, _P],
     "h3_int8_gemm_i32": [_P, _P, _I64, _I64, _I64, _P, _P],
     "h3_int8_gemm_column": [_P, _P, _I64, _I64, _I64, _P, _P, _I64, _P, _P, _P],
@@ -116,8 +117,8 @@ def check(status: int, name: str) -> None:
 
 # Entry points that enqueue exactly one kernel per successful call.
 _LAUNCHING = {n for n in SIGNATURES if n not in (
-    "h3_abi_version", "h3_status_string", "h3_device_error", "h3_transport_shift",
-    "h3_column_linear_noalloc_error")}
+    "h3_abi_version", "h3_status_string", "h3_device_error", "h3_device_error_peek",
+    "h3_transport_shift", "h3_column_linear_noalloc_error")}
 _launches = 0
 
 
@@ -138,3 +139,23 @@ def device_error(device: int) -> int:
     code = ctypes.c_int(0)
     check(load().h3_device_error(int(device), ctypes.byref(code)), "h3_device_error")
     return code.value
+
+
+def device_error_peek(device: int) -> int:
+    """The device-side error word as it stands, read from host-mapped memory without
+    synchronising or clearing it (0 when nothing failed so far)."""
+    code = ctypes.c_int(0)
+    check(load().h3_device_error_peek(int(device), ctypes.byref(code)), "h3_device_error_peek")
+    return code.value
+
+
+def raise_on_device_error(device: int, where: str) -> None:
+    """Raises H3Error when a kernel enqueued earlier on `device` has recorded a failure
+    (a bounded wait that gave up, an out-of-range label).  The word is read without a
+    device synchronisation, so a failure shows up at the first check after the kernel
+    that recorded it has run; h3_device_error clears it."""
+    code = device_error_peek(device)
+    if code:
+        msg = load().h3_status_string(code).decode()
+        raise H3Error(f"{where}: an earlier kernel on cuda:{device} reported: {msg} "
+                      f"(status {code}); read and clear it with h3_device_error")

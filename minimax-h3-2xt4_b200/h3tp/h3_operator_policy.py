@@ -22,7 +22,11 @@ New B200 fields:
                   reference's packed INT8 group-128 payload,
                   tilelang_transport_tradeoffs.py:40-88), with any row_transport
   quant_division  'rn' (IEEE, bit-exact with the CPU oracle) or 'fast' (__fdividef)
-  fc1_swiglu_epilogue  FC1 stores the FP32 SwiGLU activation instead of fp16 [gate|up]
+  fc1_swiglu_epilogue  off (default): FC1 returns the reference's fp16 [S, 2*ffn/t]
+                  [gate|up]; on: FC1 applies the FP32 SwiGLU in its GEMM epilogue and
+                  returns fp32 [S, ffn/t] (same bytes, the same FC2 codes).  Turn it on
+                  where FC1's output goes only to FC2 (TPDiTBlockINT8.forward,
+                  tp_dit.py:356-360): FC2's producer then skips the SwiGLU
 """
 from __future__ import annotations
 
@@ -40,7 +44,7 @@ COLUMN_BACKENDS = ("preallocated", "cuda_int8_tilelang", "b200")
 @dataclass(frozen=True)
 class H3OperatorPolicy:
     row_linear_backend: str = "b200_scaled_fp16"
-    fc2_quantizer: str = "fused_recompute"
+    fc2_quantizer: str = "fused_stored"
     column_linear_backend: str = "b200"
     dit_fused_gate: bool = True
     dit_fused_row_gate: bool = True
@@ -53,7 +57,7 @@ class H3OperatorPolicy:
     row_payload: str = "fp16"
     fc2_max_exchange: str = "peer"
     quant_division: str = "rn"
-    fc1_swiglu_epilogue: bool = True
+    fc1_swiglu_epilogue: bool = False
 
     def __post_init__(self):
         for name in ("dit_fused_gate", "dit_fused_row_gate", "dit_p0_2_lifetime",

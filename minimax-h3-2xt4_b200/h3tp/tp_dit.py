@@ -27,6 +27,16 @@ def default_comm():
     return dist if dist.is_available() and dist.is_initialized() else None
 
 
+def _check_device_error(x: torch.Tensor) -> None:
+    """Raises if a kernel enqueued earlier on x's GPU recorded a failure (a bounded
+    wait that gave up, a label out of range).  One read of host-mapped memory, no
+    device synchronisation."""
+    if x.is_cuda:
+        from ._native import raise_on_device_error
+        raise_on_device_error(x.device.index if x.device.index is not None
+                              else torch.cuda.current_device(), "INT8 linear")
+
+
 def run_int8_linear_forward(x, weight, weight_scale, convrot=True, convrot_groupsize=256,
                             out_dtype=torch.float16, backend="b200", p0_a1=False, **kw):
     from .dit_column_linear import column_linear
@@ -37,8 +47,14 @@ def run_int8_linear_forward(x, weight, weight_scale, convrot=True, convrot_group
 class ColumnParallelLinearINT8(nn.Module):
     """Column-parallel INT8 linear: output features split across TP ranks, no
     communication.  Input [S, in_features] fp16 -> output [S, out_features // world]
-    fp16; with the FC1 SwiGLU epilogue (components == 2 and `_swiglu_epilogue`), the
-    FP32 SwiGLU activation [S, out_features // world // 2] instead."""
+    fp16, the reference's layout (for FC1 the component-packed [gate_r | up_r]).
+
+    Opt-in change of output: when the operator policy sets `fc1_swiglu_epilogue`
+    (configure_block copies it into `_swiglu_epilogue`) and components == 2, FC1 returns
+    the FP32 SwiGLU activation silu(f16 gate) * f16 up, shape [S, out_features // world
+    // 2] and dtype float32 - the same bytes as the fp16 [gate|up] it replaces, and the
+    same INT8 codes in FC2, whose producer then skips the SwiGLU.  Only callers that hand
+    FC1's output straight to RowParallelLinearINT8(input_act='swiglu') should turn it on."""
 
     def __init__(self, in_features: int, out_features: int, rank: int = 0, world_size: int = 2,
                  convrot: bool = True, convrot_groupsize: int = 256,
@@ -67,6 +83,7 @@ class ColumnParallelLinearINT8(nn.Module):
         self.weight_scale.data.copy_(scale.reshape(-1, 1))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        _check_device_error(x)
         orig_shape = x.shape
         x_2d = x.reshape(-1, self.in_features)
         policy = getattr(self, "operator_policy", None)
@@ -138,6 +155,7 @@ class RowParallelLinearINT8(nn.Module):
                 residual=None, gate=None, segments=None) -> torch.Tensor:
         if not reduce_sum and self.world_size > 1:
             raise ValueError("Quantization-preserving projection requires reduction")
+        _check_device_error(x)
         comm = self._comm()
         if residual is not None:
             from .dit_fusion import row_gated
@@ -174,7 +192,9 @@ class TPDiTMLPINT8(nn.Module):
                                             device=device)
         self.fc2 = RowParallelLinearINT8(ffn, hidden, rank, world_size, device=device)
         self.fc2.comm = comm
-        configure_block(self, "dit", policy or H3OperatorPolicy())
+        # FC1's output feeds FC2 only, so the FP32 SwiGLU epilogue is on unless the
+        # caller's policy says otherwise
+        configure_block(self, "dit", policy or H3OperatorPolicy(fc1_swiglu_epilogue=True))
 
     def forward(self, x: torch.Tensor, h: torch.Tensor, gate=None, segments=None) -> torch.Tensor:
         """x: fp16 residual [S, hidden] (updated in place); h: fp16 normed input."""
@@ -202,7 +222,7 @@ class TPDiTLinearBlockINT8(nn.Module):
         self.fc2 = RowParallelLinearINT8(ffn, hidden, rank, world_size, device=device)
         self.out_proj.comm = comm
         self.fc2.comm = comm
-        configure_block(self, "dit", policy or H3OperatorPolicy())
+        configure_block(self, "dit", policy or H3OperatorPolicy(fc1_swiglu_epilogue=True))
 
     def forward(self, x: torch.Tensor, gate_msa=None, gate_mlp=None, segments=None) -> torch.Tensor:
         inner = self.hidden // self.world_size

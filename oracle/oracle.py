@@ -132,8 +132,8 @@ def column_quantize(x: np.ndarray, convrot: bool = True):
     return q, s
 
 
-def int8_gemm(A: np.ndarray, W: np.ndarray) -> np.ndarray:
-    """Exact INT32 GEMM, C = A @ W.T (parallel_int8.int_mm / torch._int_mm)."""
+def int8_gemm_loop(A: np.ndarray, W: np.ndarray) -> np.ndarray:
+    """Exact INT32 GEMM, C = A @ W.T, as a plain C loop (the oracle's own statement)."""
     A = _c(A, np.int8)
     W = _c(W, np.int8)
     M, K = A.shape
@@ -142,6 +142,22 @@ def int8_gemm(A: np.ndarray, W: np.ndarray) -> np.ndarray:
     C = np.empty((M, N), np.int32)
     lib().h3o_int8_gemm(_p(A), _p(W), M, N, K, _p(C))
     return C
+
+
+def int8_gemm(A: np.ndarray, W: np.ndarray) -> np.ndarray:
+    """Exact INT32 GEMM, C = A @ W.T.  Large products run through torch._int_mm on the
+    CPU, which is what the reference's own parallel_int8.int_mm calls there
+    (patches/parallel_int8.py:46-50); small ones through the C loop.  The two agree bit
+    for bit (tests/test_oracle_golden.py pins both against the reference's int_mm)."""
+    A = _c(A, np.int8)
+    W = _c(W, np.int8)
+    M, K = A.shape
+    N = W.shape[0]
+    assert W.shape[1] == K
+    if M * N * K < (1 << 24):
+        return int8_gemm_loop(A, W)
+    import torch
+    return torch._int_mm(torch.from_numpy(A), torch.from_numpy(W).t()).numpy()
 
 
 # ----------------------------------------------------------------------------

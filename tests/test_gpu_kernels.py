@@ -438,6 +438,100 @@ def test_gemm_row_dequant_bit_exact(cuda_device, oracle, out):
 
 
 # ----------------------------------------------------------------------------
+# persistent multi-tile GEMM: every CTA (pair) walks many tiles, so both TMEM
+# accumulator buffers, their phase flips, the shared-memory ring wrapping across tiles
+# and the grouped raster are exercised.  The pair kernel runs 74 clusters on 256 x 256
+# tiles (256 x 128 output columns for SwiGLU); the single-CTA kernel 148 CTAs.
+# ----------------------------------------------------------------------------
+def _scales(rng, n, lo=1e-3, hi=1e-2):
+    return rng.uniform(lo, hi, n).astype(np.float32)
+
+
+def test_gemm_multitile_swiglu(cuda_device, oracle):
+    """FC1 shape class: M = 4096, 2 x 8192 packed rows -> 16 x 64 = 1024 pair tiles."""
+    from h3tp import ops
+    rng = np.random.default_rng(401)
+    M, Nh, K = 4096, 8192, 512
+    A, W = _operands(rng, M, 2 * Nh, K)
+    a, w = _scales(rng, M, 1e-3, 5e-2), _scales(rng, 2 * Nh)
+    y = ops.int8_gemm_swiglu(_t(A, cuda_device), _t(W, cuda_device), _t(a, cuda_device),
+                             _t(w, cuda_device), None, torch.float32)
+    _bits_equal(_np(y), oracle.swiglu_epilogue(oracle.int8_gemm(A, W), a, w, None, "f32"))
+
+
+def test_gemm_multitile_column_m_raster_groups(cuda_device, oracle):
+    """A = 16384 x 3072 (50 MB) is larger than the 32 MB L2 slab, so the raster keeps
+    groups of 42 M-blocks resident (two groups); 64 x 48 = 3072 pair tiles; bias on."""
+    from h3tp import ops
+    rng = np.random.default_rng(402)
+    M, N, K = 16384, 12288, 3072
+    A, W = _operands(rng, M, N, K)
+    a, w = _scales(rng, M, 1e-3, 5e-2), _scales(rng, N)
+    b = (rng.standard_normal(N) * 0.02).astype(np.float32)
+    y = ops.int8_gemm_column(_t(A, cuda_device), _t(W, cuda_device), _t(a, cuda_device),
+                             _t(w, cuda_device), _t(b, cuda_device))
+    got = _np(y)
+    del y
+    _bits_equal(got, oracle.column_epilogue(oracle.int8_gemm(A, W), a, w, b))
+
+
+def test_gemm_multitile_row_encode_n_raster_groups(cuda_device, oracle):
+    """W = 16384 x 3072 is the larger operand: groups of 42 N-blocks (two groups) sweep
+    all 48 M-blocks; 3072 pair tiles with the scaled-FP16 encode."""
+    from h3tp import ops
+    rng = np.random.default_rng(403)
+    M, N, K = 12288, 16384, 3072
+    A, W = _operands(rng, M, N, K)
+    shift = oracle.transport_shift(2 * K)
+    y = ops.int8_gemm_row_encode(_t(A, cuda_device), _t(W, cuda_device), shift)
+    got = _np(y)
+    del y
+    _bits_equal(got, oracle.fp16_encode(oracle.int8_gemm(A, W), shift))
+
+
+def test_gemm_multitile_row_dequant_residual(cuda_device, oracle):
+    """FC2 shape class: M = 8192, N = 3072 -> 32 x 12 = 384 pair tiles, gated residual
+    with per-row labels."""
+    from h3tp import ops
+    rng = np.random.default_rng(404)
+    M, N, K = 8192, 3072, 1024
+    A, W = _operands(rng, M, N, K)
+    a, w = _scales(rng, M, 1e-3, 5e-2), (_scales(rng, N) / 512).astype(np.float32)
+    X = rng.standard_normal((M, N)).astype(np.float16)
+    gate = rng.standard_normal((9, N)).astype(np.float32)
+    labels = rng.integers(0, 9, M).astype(np.int32)
+    Xd = _t(X, cuda_device)
+    ops.int8_gemm_row_dequant(_t(A, cuda_device), _t(W, cuda_device), _t(a, cuda_device),
+                              _t(w, cuda_device), residual=Xd, gate=_t(gate, cuda_device),
+                              labels=_t(labels, cuda_device))
+    ref = X.copy()
+    oracle.dequantize_i32(oracle.int8_gemm(A, W), a, w, out="residual", residual=ref,
+                          gate=gate, labels=labels)
+    _bits_equal(_np(Xd), ref)
+
+
+def test_gemm_multitile_pack8(cuda_device, oracle):
+    """Packed INT8 group-128 payload on 384 pair tiles."""
+    from h3tp import ops
+    rng = np.random.default_rng(405)
+    M, N, K = 8192, 3072, 512
+    A, W = _operands(rng, M, N, K)
+    y = ops.int8_gemm_row_pack8(_t(A, cuda_device), _t(W, cuda_device))
+    _bits_equal(_np(y), oracle.pack8(oracle.int8_gemm(A, W)))
+
+
+def test_gemm_multitile_single_cta_kernel(cuda_device, oracle):
+    """M <= 128 runs the single-CTA kernel: N = 80000 gives 313 tiles (a ragged last
+    one) over 148 CTAs, so every CTA takes two or three tiles."""
+    from h3tp import ops
+    rng = np.random.default_rng(406)
+    M, N, K = 100, 80000, 256
+    A, W = _operands(rng, M, N, K)
+    C = ops.int8_gemm_i32(_t(A, cuda_device), _t(W, cuda_device))
+    _bits_equal(_np(C), oracle.int8_gemm(A, W))
+
+
+# ----------------------------------------------------------------------------
 # transport codec and reduction epilogue
 # ----------------------------------------------------------------------------
 # ----------------------------------------------------------------------------

@@ -69,6 +69,42 @@ def test_column_linear_no_rotation_with_bias(cuda_device, oracle):
     _eq(_np(y), oracle.column_epilogue(oracle.int8_gemm(q, w), a, s.ravel(), b))
 
 
+def _baseline_config1(seed=0):
+    """BASELINE config 1 exactly: X fp16 [1024, 3072] ~ N(0, 1) with 1% of the columns
+    (a seeded randperm, 30 columns) scaled x20; W int8 [3072, 3072] uniform in
+    [-127, 127]; per-output-channel fp32 scales uniform in [1e-3, 1e-2]; bias
+    ~ N(0, 0.02); seed 0."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn((1024, 3072), generator=g)
+    cols = torch.randperm(3072, generator=g)[:30]
+    x[:, cols] *= 20.0
+    w = torch.randint(-127, 128, (3072, 3072), generator=g, dtype=torch.int8)
+    s = (torch.rand((3072, 1), generator=g) * 9e-3 + 1e-3).float()
+    b = (torch.randn(3072, generator=g) * 0.02).float()
+    return x.half().numpy(), w.numpy(), s.numpy(), b.numpy()
+
+
+@pytest.mark.parametrize("bias", [False, True])
+def test_baseline_config1_column_linear(cuda_device, oracle, bias):
+    """The single W8A8 linear of BASELINE config 1 (M = 1024, K = N = 3072, no
+    rotation, dynamic per-row quant, INT32 accumulate, FP32 dequant, fp16 out) through
+    the public column_linear: codes, row scales, INT32 accumulators and the fp16 output
+    all bit-exact against the oracle."""
+    from h3tp import ops
+    from h3tp.dit_column_linear import column_linear
+    x, w, s, b = _baseline_config1()
+    b = b if bias else None
+    xd, wd, sd = _t(x, cuda_device), _t(w, cuda_device), _t(s, cuda_device)
+    q_ref, a_ref = oracle.column_quantize(x, False)
+    q, a = ops.column_quantize(xd, False)
+    _eq(_np(q), q_ref)
+    _eq(_np(a).ravel(), a_ref.ravel())
+    acc_ref = oracle.int8_gemm(q_ref, w)
+    _eq(_np(ops.int8_gemm_i32(q, wd)), acc_ref)
+    y = column_linear(xd, wd, sd, convrot=False, bias=None if b is None else _t(b, cuda_device))
+    _eq(_np(y), oracle.column_epilogue(acc_ref, a_ref, s.ravel(), b))
+
+
 @pytest.mark.parametrize("world", [1, 2, 4])
 @pytest.mark.parametrize("mode", ["fused_stored", "fused_recompute"])
 def test_fc2_chain_emulated_tp(cuda_device, oracle, world, mode):

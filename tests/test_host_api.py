@@ -11,7 +11,9 @@ def test_policy_defaults_and_validation():
     from h3tp.h3_operator_policy import H3OperatorPolicy
     p = H3OperatorPolicy()
     assert p.row_linear_backend == "b200_scaled_fp16" and p.scaled_transport
-    assert p.fc2_quantizer in ("fused_stored", "fused_recompute")
+    # the reference's defaults (patches/h3_operator_policy.py:14): fused_stored, and FC1
+    # returning fp16 [gate|up] unless the FP32 SwiGLU epilogue is asked for
+    assert p.fc2_quantizer == "fused_stored" and not p.fc1_swiglu_epilogue
     assert p.column_linear_backend == "b200"
     # the reference's own values stay accepted (h3_operator_policy.py:9-41)
     ref = H3OperatorPolicy(row_linear_backend="tilelang_scaled_fp16", fc2_quantizer="fused_stored",

@@ -28,6 +28,19 @@ def test_transport_shift_matches_shift_for(oracle):
 
 def test_int_mm_exact(oracle):
     _eq(oracle.int8_gemm(G["int_mm_q"], G["int_mm_w"]), G["int_mm_out"])
+    _eq(oracle.int8_gemm_loop(G["int_mm_q"], G["int_mm_w"]), G["int_mm_out"])
+
+
+def test_int8_gemm_routes_agree(oracle):
+    """The C loop and the CPU int_mm route of the oracle's GEMM give the same INT32 bits,
+    saturating operands included."""
+    rng = np.random.default_rng(11)
+    A = rng.integers(-128, 128, size=(300, 2048), dtype=np.int8)
+    W = rng.integers(-127, 128, size=(96, 2048), dtype=np.int8)
+    A[:4] = -128
+    W[:3] = -127
+    big = oracle.int8_gemm(A, W)  # above the size at which the int_mm route takes over
+    _eq(big, oracle.int8_gemm_loop(A, W))
 
 
 def test_dequantize_cpu_branch(oracle):

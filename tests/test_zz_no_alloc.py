@@ -9,6 +9,8 @@ one left behind - and must refuse a problem larger than its static scratch witho
 launching anything.  This file is collected last so a failure here cannot hide
 another test."""
 import ctypes
+import re
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -17,7 +19,19 @@ import torch
 pytestmark = pytest.mark.gpu
 
 H3_ERR_INVALID = 1
-SCRATCH_BYTES = 32 << 20
+
+
+def _scratch_bytes() -> int:
+    """H3_NOALLOC_SCRATCH_BYTES as the library's header defines it."""
+    header = (Path(__file__).resolve().parents[1] / "include" / "h3b200.h").read_text()
+    m = re.search(r"#define\s+H3_NOALLOC_SCRATCH_BYTES\s+\((\d+)u\s*<<\s*(\d+)\)", header)
+    assert m, "H3_NOALLOC_SCRATCH_BYTES not found in include/h3b200.h"
+    return int(m.group(1)) << int(m.group(2))
+
+
+def _fits(m: int, k: int, limit: int) -> bool:
+    """The header's size rule: 256 + roundup256(4 m) + m k <= limit."""
+    return 256 + -(-4 * m // 256) * 256 + m * k <= limit
 
 
 def _noalloc(x, w, ws, bias, convrot):
@@ -70,16 +84,19 @@ def test_noalloc_column_linear_matches_existing_path(cuda_device):
 def test_noalloc_rejects_problems_beyond_the_static_scratch(cuda_device):
     from h3tp import _native
     lib = _native.load()
+    limit = _scratch_bytes()
     k = 4096
-    m = SCRATCH_BYTES // k  # codes alone fill the array; scales and error word do not fit
-    x = torch.zeros((m, k), dtype=torch.float16, device=cuda_device)
+    m_max = limit // k
+    while not _fits(m_max, k, limit):
+        m_max -= 1
+    x = torch.zeros((m_max + 1, k), dtype=torch.float16, device=cuda_device)
     w = torch.zeros((256, k), dtype=torch.int8, device=cuda_device)
     ws = torch.ones((256, 1), dtype=torch.float32, device=cuda_device)
+    # one row beyond the rule is refused, launching nothing
     st, out = _noalloc(x, w, ws, None, True)
     assert st == H3_ERR_INVALID
-    # just inside the limit still runs
-    m_ok = (SCRATCH_BYTES - 256 - 4 * 8192) // k
-    st, out = _noalloc(x[:m_ok], w, ws, None, True)
-    assert st == 0
+    # the largest problem inside the rule still runs
+    st, out = _noalloc(x[:m_max], w, ws, None, True)
+    assert st == 0, lib.h3_status_string(st)
     torch.cuda.synchronize()
     assert torch.count_nonzero(out) == 0
