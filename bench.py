@@ -237,7 +237,7 @@ def cpu_block_sample(rows, w1, s1, w2, s2, h, x, threads, start=0):
     return dt, block_ops(rows, w2.shape[0], w2.shape[1])
 
 
-def cpu_baseline(w1, s1, w2, s2, h, x, budget_s=12.0, rows=512):
+def cpu_baseline(w1, s1, w2, s2, h, x, budget_s=12.0, rows=4096):
     import torch
     threads = os.cpu_count() or 1
     cpu_block_sample(64, w1, s1, w2, s2, h, x, threads)  # warm-up
@@ -663,7 +663,7 @@ def run_ours(args):
     if e2e is not None:
         line["e2e"] = e2e
     if world == 1 and not args.no_cpu:
-        line["cpu_baseline"] = cpu_baseline(w1, s1, w2, s2, h_cpu, x_cpu)
+        line["cpu_baseline"] = cpu_baseline(w1, s1, w2, s2, h_cpu, x_cpu, rows=min(args.ref_rows, M))
     if comm:
         from h3tp import peer
         peer.release()

@@ -10,9 +10,9 @@ the reference (tilelang_dit_fusion.py:153-168).
 """
 from __future__ import annotations
 
-import threading
-from functools import lru_cache
+from collections import OrderedDict
 
+import numpy as np
 import torch
 
 from . import comm as C
@@ -20,30 +20,65 @@ from . import ops
 
 
 def segment_key(rows, segments, modulation_rows=9):
-    """Validated, hashable segments: [(a, b, row)] tiling [0, rows) exactly
-    (tilelang_dit_fusion.py:93-100)."""
-    key = tuple(tuple(s) for s in segments)
-    cursor = 0
-    for a, b, row in sorted(key):
-        if (any(type(v) is not int for v in (a, b, row)) or a != cursor
-                or not a < b <= rows or not 0 <= row < modulation_rows):
-            return None
-        cursor = b
-    return key if cursor == rows else None
+    """The segment layout as a hashable, validated tuple, or None when it is not one.
+
+    A layout is a list of (start, end, modulation_row) triples of plain ints that,
+    taken in order of their starts, tile [0, rows) without gap or overlap, each with
+    start < end and a modulation row in [0, modulation_rows) - the contract of the
+    reference's segment check (tilelang_dit_fusion.py:93-100)."""
+    triples = [tuple(seg) for seg in segments]
+    if any(len(t) != 3 for t in triples):
+        raise ValueError("segments are (start, end, modulation_row) triples")
+    if any(type(v) is not int for t in triples for v in t):
+        return None
+    ordered = sorted(triples)
+    bounds = [0] + [t[1] for t in ordered]
+    if any(t[0] != b for t, b in zip(ordered, bounds)) or bounds[-1] != rows:
+        return None
+    if any(not (t[0] < t[1] and 0 <= t[2] < modulation_rows) for t in ordered):
+        return None
+    return tuple(triples)
 
 
-_label_lock = threading.RLock()
+class _LabelCache:
+    """Per-row modulation labels (int32, one per row) on each device, built once per
+    segment layout and kept in a small least-recently-used table per device.
+
+    A label vector is built from the layout on the host, copied to the device and
+    waited for before it is cached, so it is complete for every stream that reads it
+    later; a reader on a stream other than the one that built it is recorded on the
+    tensor, so the allocator keeps the memory until that stream's work is done even if
+    the entry is evicted meanwhile."""
+
+    def __init__(self, capacity: int = 8):
+        self.capacity = capacity
+        self.tables: dict = {}
+
+    def get(self, device: torch.device, rows: int, key: tuple) -> torch.Tensor:
+        table = self.tables.setdefault(device, OrderedDict())
+        entry = table.get((rows, key))
+        if entry is None:
+            ordered = sorted(key)
+            labels = np.repeat(np.array([t[2] for t in ordered], dtype=np.int32),
+                               [t[1] - t[0] for t in ordered])
+            with torch.cuda.device(device):
+                built_on = torch.cuda.current_stream(device)
+                tensor = torch.from_numpy(labels).to(device)
+                built_on.synchronize()
+            entry = (tensor, built_on)
+            table[(rows, key)] = entry
+            while len(table) > self.capacity:
+                table.popitem(last=False)
+        else:
+            table.move_to_end((rows, key))
+        tensor, built_on = entry
+        reader = torch.cuda.current_stream(device)
+        if reader != built_on:
+            tensor.record_stream(reader)
+        return tensor
 
 
-@lru_cache(maxsize=4)
-def _labels(rows, segments, device):
-    labels = torch.empty(rows, dtype=torch.int32)
-    for a, b, row in segments:
-        labels[a:b] = row
-    labels = labels.to(device)
-    ready = torch.cuda.Event()
-    ready.record(torch.cuda.current_stream(device))
-    return labels, ready
+_LABELS = _LabelCache()
 
 
 def _norm_supported(norm, x, shift, scale):
@@ -86,18 +121,14 @@ def modulated_norm_quantize(norm, x, shift, scale, segments, convrot=True):
 
 
 def labels_for(x, segments, modulation_rows=9):
-    """Per-row modulation labels on x's device, cached (tilelang_dit_fusion.py:115-124)."""
+    """Per-row modulation labels for x's rows on x's device, or None when `segments` is
+    None or not a valid layout (tilelang_dit_fusion.py:107-124)."""
     if segments is None:
         return None
     key = segment_key(x.shape[0], segments, modulation_rows)
     if key is None:
         return None
-    with _label_lock:
-        labels, ready = _labels(x.shape[0], key, str(x.device))
-    stream = torch.cuda.current_stream(x.device)
-    stream.wait_event(ready)
-    labels.record_stream(stream)
-    return labels
+    return _LABELS.get(x.device, x.shape[0], key)
 
 
 def _table(value, x, rows=None):
