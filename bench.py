@@ -69,6 +69,9 @@ def parse():
                     help="FC2 row maxima at TP > 1: in-kernel over peer memory, or NCCL MAX")
     ap.add_argument("--payload", choices=["fp16", "int8_gather"], default="fp16",
                     help="row partial payload at TP > 1 (scaled fp16, or the packed INT8 scheme)")
+    ap.add_argument("--transport", choices=["p2p", "nvls", "rowblock", "allreduce"], default="p2p",
+                    help="row partial exchange at TP > 1 (peer memory, in-switch NVLS reduction, "
+                         "NCCL row blocks or NCCL all-reduce)")
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the sampled-row bit-exactness check after the timed region")
     ap.add_argument("--int8-peak", action="store_true",
@@ -83,7 +86,7 @@ def workload_config(args, world):
     return {"workload": "dit_mlp_block", "M": args.tokens, "hidden": args.hidden,
             "ffn": args.ffn, "tp": world, "parallelism": f"tp{world}",
             "fc2_quantizer": "fused_stored",
-            "row_transport": "p2p", "row_payload": args.payload,
+            "row_transport": args.transport, "row_payload": args.payload,
             "fc2_max_exchange": args.max_exchange, "fc1_epilogue": args.fc1_epilogue,
             "l2": "inputs larger than L2 (h = 201 MB per step), no flush"}
 
@@ -433,6 +436,7 @@ def run_ours(args):
     from h3tp.h3_operator_policy import H3OperatorPolicy
     mlp = TPDiTMLPINT8(hidden, ffn, rank, world, device=dev, comm=comm,
                        policy=H3OperatorPolicy(row_payload=args.payload,
+                                               row_transport=args.transport,
                                                fc2_max_exchange=args.max_exchange,
                                                fc1_swiglu_epilogue=args.fc1_epilogue == "swiglu"))
     mlp.fc1.load_shard_from_full(w1, s1)
@@ -444,6 +448,32 @@ def run_ours(args):
 
     fc1_events = []
     fc2_events = []
+    sub_events = []  # TP > 1 peer route: (producer, FC2 GEMM, reduce, gather) boundaries
+    from h3tp import peer as P, transport as T
+    peer_route = (world > 1 and args.transport in ("p2p", "nvls") and args.payload == "fp16"
+                  and args.max_exchange == "peer")
+
+    def row_chain_peer(act, xres, record):
+        # sq.row_linear's peer route, unrolled so each launch can be bracketed by events
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
+        ws = P.workspace(comm, dev, hidden, M)
+        q, scale = ws.quantize_rows(act, sq.input_kind(act, ffn // world)[0], "rn")
+        if record:
+            ev[0].record(stream)
+        shift = T.shift_for(ffn // world, world)
+        ops.int8_gemm_row_encode(q, mlp.fc2.weight, shift, out=ws.partial(M))
+        if record:
+            ev[1].record(stream)
+        ws.epoch = P.next_epoch(ws.epoch)
+        ops.peer_reduce(ws.bases, ws.world, ws.rank, 0, ws.partial_off, ws.final_off, M, hidden,
+                        shift, scale, mlp.fc2.weight_scale.reshape(-1), xres, None, None, ws.epoch,
+                        multicast=ws.multicast if args.transport == "nvls" else 0)
+        if record:
+            ev[2].record(stream)
+        ops.peer_gather(ws.bases, ws.world, ws.rank, 0, ws.final_off, M, hidden, xres, ws.epoch)
+        if record:
+            ev[3].record(stream)
+            sub_events.append(ev)
 
     def step(xres, record=False):
         # TPDiTMLPINT8.forward, unrolled so the FC1 GEMM can be bracketed by events.
@@ -461,10 +491,13 @@ def run_ours(args):
         if record:
             e1.record(stream)
             fc1_events.append((e0, e1))
-        sq.row_linear(act, mlp.fc2.weight, mlp.fc2.weight_scale, comm,
-                      mode=pol.fc2_quantizer, scaled_transport=True, residual=xres,
-                      transport=pol.row_transport, payload=pol.row_payload,
-                      peer_max=pol.fc2_max_exchange == "peer")
+        if peer_route:
+            row_chain_peer(act, xres, record)
+        else:
+            sq.row_linear(act, mlp.fc2.weight, mlp.fc2.weight_scale, comm,
+                          mode=pol.fc2_quantizer, scaled_transport=True, residual=xres,
+                          transport=pol.row_transport, payload=pol.row_payload,
+                          peer_max=pol.fc2_max_exchange == "peer")
         if record:
             e2 = torch.cuda.Event(enable_timing=True)
             e2.record(stream)
@@ -493,10 +526,19 @@ def run_ours(args):
         elapsed_ms = start.elapsed_time(end)
         fc1_ms = statistics.mean(a.elapsed_time(b) for a, b in fc1_events)
         fc2_ms = statistics.mean(a.elapsed_time(b) for a, b in fc2_events)
-        t = torch.tensor([elapsed_ms, fc1_ms, fc2_ms], device=dev, dtype=torch.float64)
+        sub = [0.0] * 4
+        if sub_events:
+            starts = [b for _, b in fc1_events]
+            for k in range(4):
+                sub[k] = statistics.mean((ev[k - 1] if k else s0).elapsed_time(ev[k])
+                                         for s0, ev in zip(starts, sub_events))
+        t = torch.tensor([elapsed_ms, fc1_ms, fc2_ms] + sub, device=dev, dtype=torch.float64)
+        t_min = t.clone()
         if comm:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dist.all_reduce(t_min, op=dist.ReduceOp.MIN)
         elapsed_ms, fc1_ms, fc2_ms = float(t[0]), float(t[1]), float(t[2])
+        sub_max, sub_min = [float(v) for v in t[3:]], [float(v) for v in t_min[3:]]
         ms_per_step = elapsed_ms / args.steps
 
         # Parity of the timed code path: one more step on a copy of the residual.
@@ -653,6 +695,12 @@ def run_ours(args):
         "gpu_launches": int(launches),
         "phases_ms": {"fc1_gemm": round(fc1_ms, 4), "fc2_chain": round(fc2_ms, 4),
                       "column_quantize_and_rest": round(ms_per_step - fc1_ms - fc2_ms, 4)},
+        **({"fc2_chain_ms": {k: [round(sub_min[i], 4), round(sub_max[i], 4)] for i, k in
+                             enumerate(("peer_producer", "gemm_encode", "reduce_incl_ready_wait",
+                                        "gather"))},
+            "fc2_chain_note": "[min, max] over ranks of the mean per step; the reduce includes "
+                              "the wait for the slowest rank's ready flag"}
+           if sub_events else {}),
         "device_error": err,
     }
     if parity is not None:

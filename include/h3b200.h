@@ -277,6 +277,20 @@ int h3_peer_reduce(const void* const* bases, int world, int rank, int64_t flags_
                    int shift, const float* row_scale, const float* weight_scale,
                    void* residual_f16, const float* gate, int64_t gate_rows,
                    const int32_t* labels, uint32_t epoch, void* stream);
+/* h3_peer_reduce with the reduction done in the NVSwitch (NVLS): `multicast` is the
+ * multicast address of the same workspace buffers (an NVLS multicast object bound to
+ * every rank's buffer, e.g. torch symmetric memory's multicast_ptr).  Each 16-byte
+ * chunk of the owned rows is read with one multimem.ld_reduce (the switch sums the
+ * `world` fp16 partials, fp32 accumulation, one fp16 rounding) and each finished chunk is
+ * stored into every rank's final area with one multimem.st; the epilogue, flags and
+ * h3_peer_gather are those of h3_peer_reduce.  Bit-identical to h3_peer_reduce at
+ * world 2; at world 4 and 8 the switch's summation order is its own (rare last-bit
+ * differences of the fp16 sum where the fp32 partial sums are inexact). */
+int h3_peer_reduce_nvls(const void* const* bases, const void* multicast, int world, int rank,
+                        int64_t flags_off, int64_t partial_off, int64_t final_off, int64_t rows,
+                        int64_t width, int shift, const float* row_scale,
+                        const float* weight_scale, void* residual_f16, const float* gate,
+                        int64_t gate_rows, const int32_t* labels, uint32_t epoch, void* stream);
 /* h3_peer_reduce for packed INT8 payloads (h3_int8_gemm_row_pack8 output at
  * partial_off): restored = rint(rank-order sum of f32(q_w) *rn s_w), then the same
  * epilogue, final-row stores and flags.  width % 128 == 0. */

@@ -25,6 +25,19 @@
 //   gather kernel  waits until done[w] >= e for every peer w and copies the peers'
 //                  finished rows from its own final area into the residual (local).
 //
+// The NVLS form of the reduce kernel (h3_peer_reduce_nvls) takes the multicast address
+// of the same buffers (an NVLink SHARP / NVLS multicast object bound to every rank's
+// allocation): each 16-byte chunk of the owned rows is read with one
+// multimem.ld_reduce, which makes the NVSwitch fetch the chunk from every rank and
+// return the lane-wise sum (fp32 accumulation, one fp16 rounding), and each finished
+// chunk is written with one multimem.st, which the switch replicates into every rank's
+// final area.  Per rank the links then carry about 2*rows*width bytes each way instead
+// of 2 * (world-1)/world * 2*rows*width.  At world 2 the switch's sum of two fp16
+// values is the single RN addition (the fp32 sum of two fp16 values rounds once to
+// fp16 correctly); at world 4 and 8 the switch's summation order is its own, so the
+// result can differ from the rank-order sum in the last fp16 bit where the fp32
+// partial sums are inexact.  Flags, waits and buffer reuse are those of the p2p form.
+//
 // Reuse across calls is ordered by the flags: a rank rewrites its partial only in its
 // next row GEMM, after its gather of this call, which waited for every peer's done
 // (so every peer has finished loading it); and a rank stores into a peer's final area
@@ -46,6 +59,7 @@ constexpr int THREADS = 256;
 
 struct Args {
   uint64_t bases[MAX_WORLD];
+  uint64_t mc;  // multicast (NVLS) address of the same buffer, 0 when unused
   int64_t flags_off, partial_off, final_off;
   int world, rank;
   int64_t rows, width, row_begin, row_end, per;
@@ -108,6 +122,36 @@ H3_DEV uint4 load_received(uint64_t base, int64_t off) {
 // Reads another GPU's memory over NVLink (not cached).
 H3_DEV uint4 load_peer(uint64_t base, int64_t off) {
   return __ldcv(reinterpret_cast<const uint4*>(base + off));
+}
+
+// In-switch reduction (NVLS): the NVSwitch loads this 16-byte chunk from every rank's
+// buffer and returns their sum, accumulated in fp32 and rounded once to fp16 per lane.
+H3_DEV uint4 load_reduce_nvls(uint64_t mc, int64_t off) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.f16x2 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(mc + off)
+               : "memory");
+  return v;
+}
+
+// One store through the multicast address: the switch writes the chunk into every
+// rank's buffer.
+H3_DEV void store_all_nvls(uint64_t mc, int64_t off, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(mc + off),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Decode of an already reduced fp16 chunk: restored = (int32) trunc(f32(t) *rn 2^s).
+H3_DEV void restore_reduced(const Args& a, uint4 u, int32_t (&q)[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __half22float2(h[j]);
+    q[2 * j] = __float2int_rz(__fmul_rn(f.x, a.up));
+    q[2 * j + 1] = __float2int_rz(__fmul_rn(f.y, a.up));
+  }
 }
 
 // fp16 payloads (scaled-FP16 scheme): rank-order fp32 sum of the W partial chunks, one
@@ -210,7 +254,9 @@ H3_DEV uint4 epilogue_chunk(const Args& a, const int32_t (&q)[8], int64_t r, int
   return x;
 }
 
-template <int W, bool PACKED>
+enum Payload { FP16_P2P = 0, INT8_P2P = 1, FP16_NVLS = 2 };
+
+template <int W, int PAYLOAD>
 __global__ void __launch_bounds__(THREADS) reduce_kernel(const Args a) {
   // Phase 0: this rank's partial is complete (stream order after the row GEMM);
   // announce it to every rank.
@@ -230,7 +276,9 @@ __global__ void __launch_bounds__(THREADS) reduce_kernel(const Args a) {
       const int64_t r = e / chunks;
       const int64_t c0 = (e - r * chunks) << 3;
       int32_t q[8];
-      if (PACKED) {
+      if (PAYLOAD == FP16_NVLS) {
+        restore_reduced(a, load_reduce_nvls(a.mc, a.partial_off + e * 16), q);
+      } else if (PAYLOAD == INT8_P2P) {
         load_restore_int8<W>(a, r, c0, q);
       } else {
         uint4 u[W];
@@ -242,9 +290,13 @@ __global__ void __launch_bounds__(THREADS) reduce_kernel(const Args a) {
       }
       const uint4 y = epilogue_chunk(a, q, r, c0, res[e]);
       res[e] = y;
+      if (PAYLOAD == FP16_NVLS) {
+        store_all_nvls(a.mc, a.final_off + e * 16, y);
+      } else {
 #pragma unroll
-      for (int w = 0; w < W; ++w)
-        if (w != a.rank) reinterpret_cast<uint4*>(a.bases[w] + a.final_off)[e] = y;
+        for (int w = 0; w < W; ++w)
+          if (w != a.rank) reinterpret_cast<uint4*>(a.bases[w] + a.final_off)[e] = y;
+      }
     }
   } else if (threadIdx.x == 0) {
     report_error(a.err, H3_ERR_TIMEOUT);
@@ -290,20 +342,25 @@ __global__ void __launch_bounds__(THREADS) gather_kernel(const Args a) {
 }
 
 template <int W>
-cudaError_t launch(const Args& a, int blocks, bool gather, bool packed, cudaStream_t st) {
+cudaError_t launch(const Args& a, int blocks, bool gather, int payload, cudaStream_t st) {
   if (gather)
     gather_kernel<W><<<blocks, THREADS, 0, st>>>(a);
-  else if (packed)
-    reduce_kernel<W, true><<<blocks, THREADS, 0, st>>>(a);
+  else if (payload == INT8_P2P)
+    reduce_kernel<W, INT8_P2P><<<blocks, THREADS, 0, st>>>(a);
+  else if (payload == FP16_NVLS)
+    reduce_kernel<W, FP16_NVLS><<<blocks, THREADS, 0, st>>>(a);
   else
-    reduce_kernel<W, false><<<blocks, THREADS, 0, st>>>(a);
+    reduce_kernel<W, FP16_P2P><<<blocks, THREADS, 0, st>>>(a);
   return cudaGetLastError();
 }
 
-int run(const void* const* bases, int world, int rank, int64_t flags_off, int64_t partial_off,
-        int64_t final_off, int64_t rows, int64_t width, int shift, const float* row_scale,
-        const float* weight_scale, void* residual_f16, const float* gate, int64_t gate_rows,
-        const int32_t* labels, uint32_t epoch, bool gather, bool packed, void* stream) {
+int run(const void* const* bases, const void* mc, int world, int rank, int64_t flags_off,
+        int64_t partial_off, int64_t final_off, int64_t rows, int64_t width, int shift,
+        const float* row_scale, const float* weight_scale, void* residual_f16, const float* gate,
+        int64_t gate_rows, const int32_t* labels, uint32_t epoch, bool gather, int payload,
+        void* stream) {
+  const bool packed = payload == INT8_P2P;
+  if (payload == FP16_NVLS && (mc == nullptr || !h3host::aligned(mc, 16))) return H3_ERR_INVALID;
   if (bases == nullptr || residual_f16 == nullptr || (world != 2 && world != 4 && world != 8) ||
       rank < 0 || rank >= world || rows < 0 || width <= 0 || width % 8 || epoch == 0 ||
       flags_off < 0 || partial_off < 0 || final_off < 0 || flags_off % 16 ||
@@ -319,6 +376,7 @@ int run(const void* const* bases, int world, int rank, int64_t flags_off, int64_
     if (packed && width % 128 != 0) return H3_ERR_INVALID;
   }
   Args a{};
+  a.mc = reinterpret_cast<uint64_t>(mc);
   for (int w = 0; w < world; ++w) {
     if (bases[w] == nullptr || !h3host::aligned(bases[w], 16)) return H3_ERR_INVALID;
     a.bases[w] = reinterpret_cast<uint64_t>(bases[w]);
@@ -353,9 +411,9 @@ int run(const void* const* bases, int world, int rank, int64_t flags_off, int64_
   const int blocks = (int)std::max<int64_t>(
       1, std::min<int64_t>((items + THREADS - 1) / THREADS, (int64_t)h3host::sm_count(dev) * 8));
   cudaStream_t st = (cudaStream_t)stream;
-  cudaError_t e = world == 2 ? launch<2>(a, blocks, gather, packed, st)
-                  : world == 4 ? launch<4>(a, blocks, gather, packed, st)
-                               : launch<8>(a, blocks, gather, packed, st);
+  cudaError_t e = world == 2 ? launch<2>(a, blocks, gather, payload, st)
+                  : world == 4 ? launch<4>(a, blocks, gather, payload, st)
+                               : launch<8>(a, blocks, gather, payload, st);
   return e == cudaSuccess ? H3_OK : H3_ERR_CUDA;
 }
 
@@ -368,9 +426,20 @@ extern "C" int h3_peer_reduce(const void* const* bases, int world, int rank, int
                               const float* weight_scale, void* residual_f16, const float* gate,
                               int64_t gate_rows, const int32_t* labels, uint32_t epoch,
                               void* stream) {
-  return h3::peer::run(bases, world, rank, flags_off, partial_off, final_off, rows, width, shift,
-                       row_scale, weight_scale, residual_f16, gate, gate_rows, labels, epoch,
-                       false, false, stream);
+  return h3::peer::run(bases, nullptr, world, rank, flags_off, partial_off, final_off, rows,
+                       width, shift, row_scale, weight_scale, residual_f16, gate, gate_rows,
+                       labels, epoch, false, h3::peer::FP16_P2P, stream);
+}
+
+extern "C" int h3_peer_reduce_nvls(const void* const* bases, const void* multicast, int world,
+                                   int rank, int64_t flags_off, int64_t partial_off,
+                                   int64_t final_off, int64_t rows, int64_t width, int shift,
+                                   const float* row_scale, const float* weight_scale,
+                                   void* residual_f16, const float* gate, int64_t gate_rows,
+                                   const int32_t* labels, uint32_t epoch, void* stream) {
+  return h3::peer::run(bases, multicast, world, rank, flags_off, partial_off, final_off, rows,
+                       width, shift, row_scale, weight_scale, residual_f16, gate, gate_rows,
+                       labels, epoch, false, h3::peer::FP16_NVLS, stream);
 }
 
 extern "C" int h3_peer_reduce_int8(const void* const* bases, int world, int rank,
@@ -379,14 +448,15 @@ extern "C" int h3_peer_reduce_int8(const void* const* bases, int world, int rank
                                    const float* weight_scale, void* residual_f16,
                                    const float* gate, int64_t gate_rows, const int32_t* labels,
                                    uint32_t epoch, void* stream) {
-  return h3::peer::run(bases, world, rank, flags_off, partial_off, final_off, rows, width, 0,
-                       row_scale, weight_scale, residual_f16, gate, gate_rows, labels, epoch,
-                       false, true, stream);
+  return h3::peer::run(bases, nullptr, world, rank, flags_off, partial_off, final_off, rows,
+                       width, 0, row_scale, weight_scale, residual_f16, gate, gate_rows, labels,
+                       epoch, false, h3::peer::INT8_P2P, stream);
 }
 
 extern "C" int h3_peer_gather(const void* const* bases, int world, int rank, int64_t flags_off,
                               int64_t final_off, int64_t rows, int64_t width, void* residual_f16,
                               uint32_t epoch, void* stream) {
-  return h3::peer::run(bases, world, rank, flags_off, 0, final_off, rows, width, 0, nullptr,
-                       nullptr, residual_f16, nullptr, 0, nullptr, epoch, true, false, stream);
+  return h3::peer::run(bases, nullptr, world, rank, flags_off, 0, final_off, rows, width, 0,
+                       nullptr, nullptr, residual_f16, nullptr, 0, nullptr, epoch, true,
+                       h3::peer::FP16_P2P, stream);
 }

@@ -66,6 +66,8 @@ SIGNATURES = {
                             _U32, _P],
     "h3_peer_reduce": [_PP, _I, _I, _I64, _I64, _I64, _I64, _I64, _I, _P, _P, _P, _P, _I64, _P,
                        _U32, _P],
+    "h3_peer_reduce_nvls": [_PP, _P, _I, _I, _I64, _I64, _I64, _I64, _I64, _I, _P, _P, _P, _P,
+                            _I64, _P, _U32, _P],
     "h3_peer_gather": [_PP, _I, _I, _I64, _I64, _I64, _I64, _P, _U32, _P],
     "h3_swiglu_rotate_quantize_peer": [_P, _I, _I64, _I64, _PP, _I, _I, _I64, _U32, _I, _P, _P,
                                        _P, _P],

@@ -14,6 +14,11 @@ New B200 fields:
                   or 'allreduce' (NCCL fp16 SUM, the reference's form).  All three give
                   the same bits; 'p2p' needs a torch.distributed NCCL group and the
                   residual form of the row output, and uses 'rowblock' otherwise.
+                  'nvls': 'p2p' with the fp16 partials summed inside the NVSwitch
+                  (multimem.ld_reduce) and the finished rows broadcast through it
+                  (multimem.st) where the group's symmetric memory has a multicast
+                  address (else 'p2p'); the same bits as 'p2p' at TP 2, at TP 4/8 the
+                  switch's summation order (rare last-bit differences of the fp16 sum)
   fc2_max_exchange 'peer' (default: under 'p2p' the FC2 producer exchanges its row
                   maxima over the peer workspace inside the kernel, one pass instead
                   of two and an NCCL MAX) or 'nccl' (the reference's MAX all-reduce
@@ -71,7 +76,7 @@ class H3OperatorPolicy:
             raise ValueError("Unknown FC2 quantizer")
         if self.column_linear_backend not in COLUMN_BACKENDS:
             raise ValueError("Unknown column linear backend")
-        if self.row_transport not in ("p2p", "rowblock", "allreduce"):
+        if self.row_transport not in ("p2p", "nvls", "rowblock", "allreduce"):
             raise ValueError("Unknown row transport")
         if self.row_payload not in ("fp16", "int8_gather"):
             raise ValueError("Unknown row payload")

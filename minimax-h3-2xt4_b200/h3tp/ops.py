@@ -449,15 +449,22 @@ def gated_add(residual, branch, gate=None, labels=None):
 
 def peer_reduce(bases, world: int, rank: int, flags_off: int, partial_off: int, final_off: int,
                 rows: int, width: int, shift: int, row_scale, weight_scale, residual,
-                gate=None, labels=None, epoch: int = 1):
+                gate=None, labels=None, epoch: int = 1, multicast: int = 0):
     """Reduce + fused gated-residual epilogue of this rank's row block from every rank's
-    partial, finished rows stored into the peers' final areas (h3_peer_reduce)."""
+    partial, finished rows stored into the peers' final areas (h3_peer_reduce).  With a
+    non-zero `multicast` address of the same buffers the sum is taken in the NVSwitch
+    and the finished rows are broadcast through it (h3_peer_reduce_nvls)."""
     a = _vec(row_scale, rows, "row_scale")
     ws = _vec(weight_scale, width, "weight_scale")
     if not residual.is_contiguous():
         raise ValueError("residual must be contiguous (updated in place)")
     res, g, grows, lab = _gate_args(residual, gate, labels, rows, width)
     arr = (ctypes.c_void_p * world)(*bases)
+    if multicast:
+        N.call("h3_peer_reduce_nvls", arr, int(multicast), world, rank, flags_off, partial_off,
+               final_off, rows, width, int(shift), a.data_ptr(), ws.data_ptr(), res.data_ptr(),
+               _ptr(g), grows, _ptr(lab), int(epoch), _stream(res))
+        return residual
     N.call("h3_peer_reduce", arr, world, rank, flags_off, partial_off, final_off, rows, width,
            int(shift), a.data_ptr(), ws.data_ptr(), res.data_ptr(), _ptr(g), grows, _ptr(lab),
            int(epoch), _stream(res))

@@ -91,6 +91,12 @@ class PeerWorkspace:
         self.world = int(self.handle.world_size)
         self.rank = int(self.handle.rank)
         self.bases = [int(p) for p in self.handle.buffer_ptrs]
+        # multicast (NVLS) address of the same buffers, 0 where the fabric or the driver
+        # offers none; every rank sees the same answer
+        try:
+            self.multicast = int(self.handle.multicast_ptr) if self.handle.has_multicast_support() else 0
+        except Exception:
+            self.multicast = 0
         self.epoch = 0
         self.max_epoch = 0
         # every rank's flags are zero before any rank signals
@@ -123,9 +129,11 @@ class PeerWorkspace:
         return q, s
 
     def reduce_and_gather(self, rows: int, shift: int, row_scale, weight_scale, residual,
-                          gate=None, labels=None, packed: bool = False):
+                          gate=None, labels=None, packed: bool = False, nvls: bool = False):
         """Sums the partials every rank wrote into partial() (or, packed, partial_u8())
-        into `residual` (fp16 [rows, width], updated in place on every rank)."""
+        into `residual` (fp16 [rows, width], updated in place on every rank).  nvls: the
+        fp16 partials are summed in the NVSwitch and the finished rows broadcast through
+        it, when the buffers have a multicast address (otherwise the p2p kernels run)."""
         self.epoch = next_epoch(self.epoch)
         if packed:
             ops.peer_reduce_int8(self.bases, self.world, self.rank, 0, self.partial_off,
@@ -134,7 +142,8 @@ class PeerWorkspace:
         else:
             ops.peer_reduce(self.bases, self.world, self.rank, 0, self.partial_off,
                             self.final_off, rows, self.width, shift, row_scale, weight_scale,
-                            residual, gate, labels, self.epoch)
+                            residual, gate, labels, self.epoch,
+                            multicast=self.multicast if nvls else 0)
         ops.peer_gather(self.bases, self.world, self.rank, 0, self.final_off, rows, self.width,
                         residual, self.epoch)
         return residual

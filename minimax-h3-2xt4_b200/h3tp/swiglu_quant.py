@@ -132,7 +132,7 @@ def _finish_quantized(q, scale, weight, weight_scale, comm, scaled_transport=Tru
                                    labels=labels)
     if scaled_transport:
         shift = T.shift_for(local_k, world)
-        if (transport == "p2p" and residual is not None and finish_fn is None
+        if (transport in ("p2p", "nvls") and residual is not None and finish_fn is None
                 and residual.is_contiguous() and residual.shape[-1] % 8 == 0 and P.available(comm)):
             # GEMM encode straight into the peer-mapped buffer, then the peer-memory
             # reduce + gated residual + gather (csrc/h3_peer.cu).
@@ -141,7 +141,8 @@ def _finish_quantized(q, scale, weight, weight_scale, comm, scaled_transport=Tru
             with label("int8_gemm_scaled_fp16_encode"):
                 ops.int8_gemm_row_encode(q, weight, shift, out=ws.partial(rows))
             with label("scaled_fp16_peer_reduce_gather"):
-                return ws.reduce_and_gather(rows, shift, scale, weight_scale, residual, gate, labels)
+                return ws.reduce_and_gather(rows, shift, scale, weight_scale, residual, gate, labels,
+                                            nvls=transport == "nvls")
         with label("int8_gemm_scaled_fp16_encode"):
             payload = ops.int8_gemm_row_encode(q, weight, shift)
         if finish_fn is not None:
@@ -183,7 +184,7 @@ def row_linear(x, weight, weight_scale, comm, *, mode="fused_stored", scaled_tra
     shape = x.shape
     ws = None
     _checked_input(x, mode, weight.shape[1])  # before the workspace's collective steps
-    if (peer_max and transport == "p2p" and scaled_transport and finish_fn is None
+    if (peer_max and transport in ("p2p", "nvls") and scaled_transport and finish_fn is None
             and residual is not None and residual.is_contiguous()
             and (payload == "int8_gather" or residual.shape[-1] % 8 == 0)
             and C.world_of(comm) > 1 and weight.shape[1] <= ops.PEER_PRODUCER_MAX_WIDTH

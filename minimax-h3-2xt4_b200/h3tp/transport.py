@@ -121,8 +121,8 @@ def reduce_and_finish(payload: torch.Tensor, comm, shift: int, activation_scale,
         with label("scaled_fp16_fused_epilogue"):
             return ops.row_reduce_finish(payload, shift, activation_scale, weight_scale, out_dtype,
                                          residual=residual, gate=gate, labels=labels)
-    if transport not in ("rowblock", "p2p"):
-        # 'p2p' reaches here only for the forms the peer kernels do not cover (no
+    if transport not in ("rowblock", "p2p", "nvls"):
+        # 'p2p' / 'nvls' reach here only for the forms the peer kernels do not cover (no
         # residual, or a non-NCCL comm); the row-block exchange gives the same bits.
         raise ValueError("Unknown row transport")
     with label("scaled_fp16_exchange"):
@@ -157,7 +157,7 @@ def int8_row_exchange(q, weight, activation_scale, weight_scale, comm, transport
     world = C.world_of(comm)
     rows, width = q.shape[0], weight.shape[0]
     ws = weight_scale.reshape(-1)
-    if (transport == "p2p" and world > 1 and residual is not None and residual.is_contiguous()
+    if (transport in ("p2p", "nvls") and world > 1 and residual is not None and residual.is_contiguous()
             and P.available(comm)):
         wsp = P.workspace(comm, q.device, width, rows)
         with label("int8_gemm_pack_int8"):
@@ -167,7 +167,7 @@ def int8_row_exchange(q, weight, activation_scale, weight_scale, comm, transport
                                          packed=True)
     with label("int8_gemm_pack_int8"):
         payload = ops.int8_gemm_row_pack8(q, weight)
-    if world > 1 and transport in ("rowblock", "p2p"):
+    if world > 1 and transport in ("rowblock", "p2p", "nvls"):
         with label("packed_int8_exchange"):
             parts, a, b = C.exchange_row_blocks(payload, comm)
         A = activation_scale.reshape(-1)[a:b]
@@ -182,7 +182,7 @@ def int8_row_exchange(q, weight, activation_scale, weight_scale, comm, transport
                 full = torch.empty((rows, width), dtype=out_dtype, device=q.device)
         with label("packed_int8_gather"):
             return C.gather_row_blocks(block, full, comm)
-    if transport not in ("rowblock", "p2p", "allreduce"):
+    if transport not in ("rowblock", "p2p", "nvls", "allreduce"):
         raise ValueError("Unknown row transport")
     with label("packed_int8_all_gather"):
         gathered = collect(payload, "int8_gather", comm)

@@ -20,10 +20,11 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 ROOT = Path(__file__).resolve().parents[1]
-M, HIDDEN, FFN = 99, 512, 2048
+SIZES = {"small": (99, 512, 2048), "full_width": (2085, 3072, 8192)}
 
 
-def _weights():
+def _weights(size="small"):
+    M, HIDDEN, FFN = SIZES[size]
     rng = np.random.default_rng(17)
     h = rng.standard_normal((M, HIDDEN)).astype(np.float16)
     X = rng.standard_normal((M, HIDDEN)).astype(np.float16)
@@ -36,7 +37,7 @@ def _weights():
     return h, X, w1, s1, w2, s2, G, segments
 
 
-def _rank(rank, world, port, outdir, transport, payload):
+def _rank(rank, world, port, outdir, transport, payload, size):
     for p in (str(ROOT), str(ROOT / "minimax-h3-2xt4_b200")):
         sys.path.insert(0, p)
     try:
@@ -50,9 +51,12 @@ def _rank(rank, world, port, outdir, transport, payload):
                                 device_id=dev)
         from h3tp.h3_operator_policy import H3OperatorPolicy
         from h3tp.tp_dit import TPDiTMLPINT8
-        h, X, w1, s1, w2, s2, G, segments = _weights()
+        h, X, w1, s1, w2, s2, G, segments = _weights(size)
+        M, HIDDEN, FFN = SIZES[size]
+        # the default TP route: FC1's FP32 SwiGLU epilogue feeding the one-pass producer
         mlp = TPDiTMLPINT8(HIDDEN, FFN, rank, world, device=dev, comm=dist,
-                           policy=H3OperatorPolicy(row_transport=transport, row_payload=payload))
+                           policy=H3OperatorPolicy(row_transport=transport, row_payload=payload,
+                                                   fc1_swiglu_epilogue=payload == "fp16"))
         mlp.fc1.load_shard_from_full(torch.from_numpy(w1), torch.from_numpy(s1))
         mlp.fc2.load_shard_from_full(torch.from_numpy(w2), torch.from_numpy(s2))
         from h3tp import _native, peer
@@ -66,6 +70,8 @@ def _rank(rank, world, port, outdir, transport, payload):
         err = _native.device_error(rank)
         if err:
             raise RuntimeError(f"device error {err}")
+        ws = next(iter(peer._WORKSPACES.values()), None)
+        Path(outdir, f"mc{rank}.txt").write_text(str(int(bool(ws is not None and ws.multicast))))
         peer.release()
         dist.barrier()
         dist.destroy_process_group()
@@ -82,27 +88,41 @@ def _port():
     return p
 
 
-@pytest.mark.parametrize("transport,payload", [("p2p", "fp16"), ("rowblock", "fp16"),
-                                               ("allreduce", "fp16"), ("p2p", "int8_gather"),
-                                               ("allreduce", "int8_gather")])
-def test_mlp_block_over_nccl_matches_oracle(cuda_device, oracle, tmp_path, transport, payload):
+def _check(got, ref, exact, what):
+    if exact:
+        assert np.array_equal(got.view(np.uint16), ref.view(np.uint16)), what
+        return 0
+    # in-switch summation order at TP 4/8: the north-star tolerance, differences counted
+    g, r = got.astype(np.float64), ref.astype(np.float64)
+    rel = np.abs(g - r).max() / max(np.abs(r).max(), 1e-30)
+    cos = float((g * r).sum() / np.sqrt((g * g).sum() * (r * r).sum()))
+    assert rel <= 2e-3 and cos >= 0.9999, (what, rel, cos)
+    return int((got.view(np.uint16) != ref.view(np.uint16)).sum())
+
+
+@pytest.mark.parametrize("transport,payload,size", [
+    ("p2p", "fp16", "small"), ("rowblock", "fp16", "small"), ("allreduce", "fp16", "small"),
+    ("p2p", "int8_gather", "small"), ("allreduce", "int8_gather", "small"),
+    ("nvls", "fp16", "small"), ("p2p", "fp16", "full_width"), ("nvls", "fp16", "full_width")])
+def test_mlp_block_over_nccl_matches_oracle(cuda_device, oracle, tmp_path, transport, payload, size):
     ngpu = torch.cuda.device_count()
     if ngpu < 2:
         pytest.skip("single-GPU box: multi-rank NCCL path not exercised here")
     world = 8 if ngpu >= 8 else (4 if ngpu >= 4 else 2)
     if transport == "allreduce" and payload == "fp16" and world != 2:
         world = 2  # NCCL's fp16 SUM is one RN addition only at two ranks
-    mp.spawn(_rank, args=(world, _port(), str(tmp_path), transport, payload), nprocs=world,
+    mp.spawn(_rank, args=(world, _port(), str(tmp_path), transport, payload, size), nprocs=world,
              join=True)
-    h, X, w1, s1, w2, s2, G, segments = _weights()
+    M, HIDDEN, FFN = SIZES[size]
+    h, X, w1, s1, w2, s2, G, segments = _weights(size)
     labels = np.zeros(M, np.int32)
     for a, b, r in segments:
         labels[a:b] = r
     acts, w2s = [], []
     kl = FFN // world
+    q, a = oracle.column_quantize(h, True)
     for r in range(world):
         w1r, s1r = oracle.packed_rows(w1, s1, r, world, 2)
-        q, a = oracle.column_quantize(h, True)
         acts.append(oracle.swiglu_epilogue(oracle.int8_gemm(q, w1r), a, s1r.ravel()))
         w2s.append(np.ascontiguousarray(w2[:, r * kl:(r + 1) * kl]))
     ref = X.copy()
@@ -117,7 +137,13 @@ def test_mlp_block_over_nccl_matches_oracle(cuda_device, oracle, tmp_path, trans
         restored = oracle.unpack8_restore(packed, HIDDEN)
         oracle.dequantize_i32(restored, qs[0][1], s2.ravel(), out="residual", residual=ref,
                               gate=G, labels=labels)
+    nvls = transport == "nvls" and all((tmp_path / f"mc{r}.txt").read_text() == "1"
+                                       for r in range(world))
+    exact = not (nvls and world > 2)
+    differ = 0
     for r in range(world):
         for call in range(2):
             got = np.load(tmp_path / f"r{r}_{call}.npy")
-            assert np.array_equal(got.view(np.uint16), ref.view(np.uint16)), f"rank {r} of {world}"
+            differ += _check(got, ref, exact, f"rank {r} of {world}, call {call}")
+    print(f"\n[{transport}/{payload}/{size}] world {world}, multicast used: {nvls}, "
+          f"elements differing from the rank-order sum: {differ}")
