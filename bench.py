@@ -72,6 +72,8 @@ def parse():
     ap.add_argument("--transport", choices=["p2p", "nvls", "rowblock", "allreduce"], default="p2p",
                     help="row partial exchange at TP > 1 (peer memory, in-switch NVLS reduction, "
                          "NCCL row blocks or NCCL all-reduce)")
+    ap.add_argument("--chunks", type=int, default=0,
+                    help="TP > 1: row chunks of the pipelined MLP forward (0 = by size, 1 = off)")
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the sampled-row bit-exactness check after the timed region")
     ap.add_argument("--int8-peak", action="store_true",
@@ -438,7 +440,8 @@ def run_ours(args):
                        policy=H3OperatorPolicy(row_payload=args.payload,
                                                row_transport=args.transport,
                                                fc2_max_exchange=args.max_exchange,
-                                               fc1_swiglu_epilogue=args.fc1_epilogue == "swiglu"))
+                                               fc1_swiglu_epilogue=args.fc1_epilogue == "swiglu",
+                                               mlp_pipeline_chunks=args.chunks))
     mlp.fc1.load_shard_from_full(w1, s1)
     mlp.fc2.load_shard_from_full(w2, s2)
     h = h_cpu.to(dev)
@@ -475,7 +478,29 @@ def run_ours(args):
             ev[3].record(stream)
             sub_events.append(ev)
 
+    chunks = mlp.pipeline_chunks(x, h)
+    pipe_events = []  # per step: {name: [(start, end) per chunk]}
+
     def step(xres, record=False):
+        if chunks > 1:
+            # the pipelined TP forward (TPDiTMLPINT8.forward_pipelined) with events
+            # around every launch on the stream it runs on
+            marks = {}
+
+            def timer(name, c, edge):
+                if edge == 0:
+                    e = torch.cuda.Event(enable_timing=True)
+                    e.record()
+                    marks.setdefault(name, []).append([e, None])
+                else:
+                    e = torch.cuda.Event(enable_timing=True)
+                    e.record()
+                    marks[name][-1][1] = e
+
+            mlp.forward_pipelined(xres, h, None, None, chunks, timer if record else None)
+            if record:
+                pipe_events.append(marks)
+            return
         # TPDiTMLPINT8.forward, unrolled so the FC1 GEMM can be bracketed by events.
         codes, row_scale = col._prepare_activation(h, True, 256)
         if record:
@@ -524,8 +549,19 @@ def run_ours(args):
                 dist.barrier()
         launches = ops.launch_count() - calls0
         elapsed_ms = start.elapsed_time(end)
-        fc1_ms = statistics.mean(a.elapsed_time(b) for a, b in fc1_events)
-        fc2_ms = statistics.mean(a.elapsed_time(b) for a, b in fc2_events)
+        if pipe_events:
+            # per step, the summed launch times of each phase (they overlap in time)
+            def phase(name):
+                return statistics.mean(sum(a.elapsed_time(b) for a, b in m[name])
+                                       for m in pipe_events)
+            fc1_ms = phase("fc1_gemm")
+            fc2_ms = phase("peer_producer") + phase("fc2_gemm") + phase("reduce_gather")
+            pipe_phases = {k: phase(k) for k in ("column_quantize", "fc1_gemm", "peer_producer",
+                                                 "fc2_gemm", "reduce_gather")}
+        else:
+            fc1_ms = statistics.mean(a.elapsed_time(b) for a, b in fc1_events)
+            fc2_ms = statistics.mean(a.elapsed_time(b) for a, b in fc2_events)
+            pipe_phases = None
         sub = [0.0] * 4
         if sub_events:
             starts = [b for _, b in fc1_events]
@@ -693,8 +729,13 @@ def run_ours(args):
                                     "(torch._int_mm) and this library's INT32 GEMM, best of 10",
                      "peak_cases": int8},
         "gpu_launches": int(launches),
-        "phases_ms": {"fc1_gemm": round(fc1_ms, 4), "fc2_chain": round(fc2_ms, 4),
-                      "column_quantize_and_rest": round(ms_per_step - fc1_ms - fc2_ms, 4)},
+        "phases_ms": ({"fc1_gemm": round(fc1_ms, 4), "fc2_chain": round(fc2_ms, 4),
+                       "column_quantize_and_rest": round(ms_per_step - fc1_ms - fc2_ms, 4)}
+                      if pipe_phases is None else
+                      {**{k: round(v, 4) for k, v in pipe_phases.items()},
+                       "note": f"pipelined over {chunks} row chunks: summed launch times per "
+                               "step on this rank; they overlap, so they add up to more than "
+                               "the step"}),
         **({"fc2_chain_ms": {k: [round(sub_min[i], 4), round(sub_max[i], 4)] for i, k in
                              enumerate(("peer_producer", "gemm_encode", "reduce_incl_ready_wait",
                                         "gather"))},

@@ -361,7 +361,8 @@ int h3_expf_compare(const float* x, int64_t n, float* ours, float* cuda, void* s
 
 /* Evaluates silu(g) = g / (1 + exp(-g)) three ways: fast[i] as the kernels compute it
  * (h3_expf and a branch-free division of the library's own: reciprocal and
- * Markstein's quotient correction), ieee[i] with h3_expf and the IEEE
+ * Markstein's quotient correction; FLT_MAX where its scalar form and its packed-pair
+ * form, the one the FC1 epilogue runs, disagree), ieee[i] with h3_expf and the IEEE
  * division (the two must agree bit for bit on every fp16 g), and cuda[i] (may be
  * NULL) with CUDA's expf, the reference's form (tilelang_swiglu_quant.py:22-23). */
 int h3_silu_compare(const float* g, int64_t n, float* fast, float* ieee, float* cuda,

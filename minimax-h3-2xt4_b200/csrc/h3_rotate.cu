@@ -544,7 +544,14 @@ __global__ void silu_compare_kernel(const float* __restrict__ g, int64_t n,
                                     float* __restrict__ cuda) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
-    fast[i] = silu_fast(g[i]);
+    // the scalar form, checked against the packed-pair form on both of its lanes
+    const float scalar = silu_fast(g[i]);
+    const int64_t other = (i & 1) ? i - 1 : (i + 1 < n ? i + 1 : i);
+    const f32x2 pair = (i & 1) ? silu_fast2(g[other], g[i]) : silu_fast2(g[i], g[other]);
+    const float packed = (i & 1) ? hi2(pair) : lo2(pair);
+    const bool same = __float_as_uint(packed) == __float_as_uint(scalar) ||
+                      (packed != packed && scalar != scalar);
+    fast[i] = same ? scalar : 3.4028234663852886e38f;  // FLT_MAX: the forms disagree
     ieee[i] = silu_ieee(g[i]);
     if (cuda != nullptr) cuda[i] = __fdiv_rn(g[i], __fadd_rn(1.0f, expf(-g[i])));
   }

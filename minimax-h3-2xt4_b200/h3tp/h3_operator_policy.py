@@ -27,6 +27,9 @@ New B200 fields:
                   reference's packed INT8 group-128 payload,
                   tilelang_transport_tradeoffs.py:40-88), with any row_transport
   quant_division  'rn' (IEEE, bit-exact with the CPU oracle) or 'fast' (__fdividef)
+  mlp_pipeline_chunks  TPDiTMLPINT8 at TP > 1 on the peer transports: row chunks whose
+                  partial-sum exchange overlaps the next chunks' GEMMs (0 = by size:
+                  4 from 16384 rows, 2 from 4096; 1 = off)
   fc1_swiglu_epilogue  off (default): FC1 returns the reference's fp16 [S, 2*ffn/t]
                   [gate|up]; on: FC1 applies the FP32 SwiGLU in its GEMM epilogue and
                   returns fp32 [S, ffn/t] (same bytes, the same FC2 codes).  Turn it on
@@ -63,6 +66,7 @@ class H3OperatorPolicy:
     fc2_max_exchange: str = "peer"
     quant_division: str = "rn"
     fc1_swiglu_epilogue: bool = False
+    mlp_pipeline_chunks: int = 0
 
     def __post_init__(self):
         for name in ("dit_fused_gate", "dit_fused_row_gate", "dit_p0_2_lifetime",
@@ -84,6 +88,8 @@ class H3OperatorPolicy:
             raise ValueError("Unknown FC2 maximum exchange")
         if self.quant_division not in ("rn", "fast"):
             raise ValueError("Unknown quantizer division")
+        if type(self.mlp_pipeline_chunks) is not int or not 0 <= self.mlp_pipeline_chunks <= 64:
+            raise ValueError("mlp_pipeline_chunks must be an int in [0, 64]")
 
     @property
     def scaled_transport(self) -> bool:

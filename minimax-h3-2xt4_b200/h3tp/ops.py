@@ -47,6 +47,17 @@ INPUT_KINDS = {"gateup_f16": N.IN_GATEUP_F16, "act_f32": N.IN_ACT_F32, "act_f16"
 DIVISIONS = {"rn": N.DIV_RN, "fast": N.DIV_FAST}
 
 
+def _out(out, shape, dtype, device, name):
+    """A caller-provided output buffer (contiguous, exact shape / dtype / device), or a
+    fresh one."""
+    if out is None:
+        return torch.empty(shape, dtype=dtype, device=device)
+    if (out.dtype != dtype or tuple(out.shape) != tuple(shape) or not out.is_contiguous()
+            or out.device != device):
+        raise ValueError(f"{name}: contiguous {dtype} {tuple(shape)} buffer on {device} required")
+    return out
+
+
 def _producer_input(x: torch.Tensor, kind: str):
     k = INPUT_KINDS[kind]
     x = _need(x, torch.float32 if k == N.IN_ACT_F32 else torch.float16, "x", 2)
@@ -57,13 +68,13 @@ def _producer_input(x: torch.Tensor, kind: str):
 # ----------------------------------------------------------------------------
 # column path
 # ----------------------------------------------------------------------------
-def column_quantize(x: torch.Tensor, convrot: bool = True):
+def column_quantize(x: torch.Tensor, convrot: bool = True, out_q=None, out_scale=None):
     """Rotation (optional) + per-row INT8 quantisation of the column input.
     Returns (q int8 [M, K], scale fp32 [M, 1])."""
     x = _need(x, torch.float16, "x", 2)
     M, K = x.shape
-    q = torch.empty((M, K), dtype=torch.int8, device=x.device)
-    s = torch.empty((M, 1), dtype=torch.float32, device=x.device)
+    q = _out(out_q, (M, K), torch.int8, x.device, "out_q")
+    s = _out(out_scale, (M, 1), torch.float32, x.device, "out_scale")
     N.call("h3_column_quantize", x.data_ptr(), M, K, int(bool(convrot)), q.data_ptr(),
            s.data_ptr(), _stream(x))
     return q, s
@@ -132,7 +143,7 @@ def int8_gemm_column(q, w, row_scale, weight_scale, bias=None) -> torch.Tensor:
     return out
 
 
-def int8_gemm_swiglu(q, w, row_scale, weight_scale, bias=None, out_dtype=torch.float32):
+def int8_gemm_swiglu(q, w, row_scale, weight_scale, bias=None, out_dtype=torch.float32, out=None):
     """FC1 GEMM with the FP32 SwiGLU epilogue; w is [gate_r | up_r]; output
     [M, w.shape[0] // 2] in out_dtype (fp32 keeps the reference's bits)."""
     q = _need(q, torch.int8, "q", 2)
@@ -145,7 +156,7 @@ def int8_gemm_swiglu(q, w, row_scale, weight_scale, bias=None, out_dtype=torch.f
     ws = _vec(weight_scale, Np, "weight_scale")
     b = None if bias is None else _vec(bias, Np, "bias")
     kind = {torch.float32: N.OUT_F32, torch.float16: N.OUT_F16}[out_dtype]
-    out = torch.empty((M, Np // 2), dtype=out_dtype, device=q.device)
+    out = _out(out, (M, Np // 2), out_dtype, q.device, "out")
     N.call("h3_int8_gemm_swiglu", q.data_ptr(), w.data_ptr(), M, Np, K, a.data_ptr(),
            ws.data_ptr(), _ptr(b), kind, out.data_ptr(), _stream(q))
     return out
@@ -204,13 +215,14 @@ PEER_PRODUCER_MAX_WIDTH = 16384  # H3_PEER_PRODUCER_MAX_WIDTH
 
 
 def swiglu_rotate_quantize_peer(x, bases, world: int, rank: int, slots_off: int, epoch: int,
-                                kind="gateup_f16", division="rn", want_max=False):
+                                kind="gateup_f16", division="rn", want_max=False, out_q=None,
+                                out_scale=None):
     """TP>1 single pass (h3_swiglu_rotate_quantize_peer): the row maxima are exchanged
     with the other ranks over peer memory inside the kernel.  Returns (q, scale [M, 1],
     row_max [M, 1] of the global maxima or None)."""
     x, k, M, W = _producer_input(x, kind)
-    q = torch.empty((M, W), dtype=torch.int8, device=x.device)
-    s = torch.empty((M, 1), dtype=torch.float32, device=x.device)
+    q = _out(out_q, (M, W), torch.int8, x.device, "out_q")
+    s = _out(out_scale, (M, 1), torch.float32, x.device, "out_scale")
     m = torch.empty((M, 1), dtype=torch.float32, device=x.device) if want_max else None
     arr = (ctypes.c_void_p * world)(*bases)
     N.call("h3_swiglu_rotate_quantize_peer", x.data_ptr(), k, M, W, arr, world, rank,

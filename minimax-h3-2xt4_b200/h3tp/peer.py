@@ -128,6 +128,42 @@ class PeerWorkspace:
                                                   division=division)
         return q, s
 
+    # -- row ranges: the pipelined MLP block runs the exchange chunk by chunk ----------
+    def partial_rows(self, row0: int, rows: int) -> torch.Tensor:
+        """Rows [row0, row0 + rows) of this rank's fp16 partial area."""
+        off = self.partial_off + 2 * row0 * self.width
+        return self.buf[off:off + 2 * rows * self.width].view(torch.float16).view(rows, self.width)
+
+    def quantize_rows_at(self, x, row0: int, kind: str = "act_f32", division: str = "rn",
+                         out_q=None, out_scale=None):
+        """quantize_rows for rows [row0, row0 + len(x)) of the block: the row-maximum
+        slots of those rows."""
+        rows = x.shape[0]
+        if row0 < 0 or row0 + rows > self.capacity:
+            raise ValueError("rows outside the workspace")
+        self.max_epoch = next_epoch(self.max_epoch)
+        q, s, _ = ops.swiglu_rotate_quantize_peer(
+            x, self.bases, self.world, self.rank, self.slots_off + 8 * self.world * row0,
+            self.max_epoch, kind=kind, division=division, out_q=out_q, out_scale=out_scale)
+        return q, s
+
+    def reduce_rows(self, row0: int, rows: int, shift: int, row_scale, weight_scale, residual,
+                    gate=None, labels=None, nvls: bool = False):
+        """The reduce + fused gated residual of rows [row0, row0 + rows) (their
+        partials in partial_rows(row0, rows)); `residual`, `row_scale` and `labels` are
+        those rows' own.  Every rank calls it for the same ranges in the same order."""
+        self.epoch = next_epoch(self.epoch)
+        off = 2 * row0 * self.width
+        ops.peer_reduce(self.bases, self.world, self.rank, 0, self.partial_off + off,
+                        self.final_off + off, rows, self.width, shift, row_scale, weight_scale,
+                        residual, gate, labels, self.epoch,
+                        multicast=self.multicast if nvls else 0)
+
+    def gather_rows(self, row0: int, rows: int, residual):
+        """The gather that completes reduce_rows of the same range."""
+        ops.peer_gather(self.bases, self.world, self.rank, 0, self.final_off + 2 * row0 * self.width,
+                        rows, self.width, residual, self.epoch)
+
     def reduce_and_gather(self, rows: int, shift: int, row_scale, weight_scale, residual,
                           gate=None, labels=None, packed: bool = False, nvls: bool = False):
         """Sums the partials every rank wrote into partial() (or, packed, partial_u8())

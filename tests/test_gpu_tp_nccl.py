@@ -37,7 +37,7 @@ def _weights(size="small"):
     return h, X, w1, s1, w2, s2, G, segments
 
 
-def _rank(rank, world, port, outdir, transport, payload, size):
+def _rank(rank, world, port, outdir, transport, payload, size, chunks=1):
     for p in (str(ROOT), str(ROOT / "minimax-h3-2xt4_b200")):
         sys.path.insert(0, p)
     try:
@@ -56,15 +56,18 @@ def _rank(rank, world, port, outdir, transport, payload, size):
         # the default TP route: FC1's FP32 SwiGLU epilogue feeding the one-pass producer
         mlp = TPDiTMLPINT8(HIDDEN, FFN, rank, world, device=dev, comm=dist,
                            policy=H3OperatorPolicy(row_transport=transport, row_payload=payload,
-                                                   fc1_swiglu_epilogue=payload == "fp16"))
+                                                   fc1_swiglu_epilogue=payload == "fp16",
+                                                   mlp_pipeline_chunks=chunks))
         mlp.fc1.load_shard_from_full(torch.from_numpy(w1), torch.from_numpy(s1))
         mlp.fc2.load_shard_from_full(torch.from_numpy(w2), torch.from_numpy(s2))
         from h3tp import _native, peer
         for call in range(2):  # the second call reuses the transport workspace
             x = torch.from_numpy(X.copy()).to(dev)
+            hd = torch.from_numpy(h).to(dev)
             with torch.no_grad():
-                out = mlp(x, torch.from_numpy(h).to(dev), gate=torch.from_numpy(G).to(dev),
-                          segments=segments)
+                if chunks > 1:
+                    assert mlp.pipeline_chunks(x, hd) == chunks
+                out = mlp(x, hd, gate=torch.from_numpy(G).to(dev), segments=segments)
             torch.cuda.synchronize()
             np.save(os.path.join(outdir, f"r{rank}_{call}.npy"), out.cpu().numpy())
         err = _native.device_error(rank)
@@ -100,19 +103,24 @@ def _check(got, ref, exact, what):
     return int((got.view(np.uint16) != ref.view(np.uint16)).sum())
 
 
-@pytest.mark.parametrize("transport,payload,size", [
-    ("p2p", "fp16", "small"), ("rowblock", "fp16", "small"), ("allreduce", "fp16", "small"),
-    ("p2p", "int8_gather", "small"), ("allreduce", "int8_gather", "small"),
-    ("nvls", "fp16", "small"), ("p2p", "fp16", "full_width"), ("nvls", "fp16", "full_width")])
-def test_mlp_block_over_nccl_matches_oracle(cuda_device, oracle, tmp_path, transport, payload, size):
+@pytest.mark.parametrize("transport,payload,size,chunks", [
+    ("p2p", "fp16", "small", 1), ("rowblock", "fp16", "small", 1),
+    ("allreduce", "fp16", "small", 1), ("p2p", "int8_gather", "small", 1),
+    ("allreduce", "int8_gather", "small", 1), ("nvls", "fp16", "small", 1),
+    ("p2p", "fp16", "full_width", 1), ("nvls", "fp16", "full_width", 1),
+    ("p2p", "fp16", "full_width", 3), ("nvls", "fp16", "full_width", 3)])
+def test_mlp_block_over_nccl_matches_oracle(cuda_device, oracle, tmp_path, transport, payload, size,
+                                            chunks):
+    """chunks > 1: the pipelined forward (row chunks, exchange overlapping the GEMMs;
+    M = 2085 in three chunks, the last one ragged)."""
     ngpu = torch.cuda.device_count()
     if ngpu < 2:
         pytest.skip("single-GPU box: multi-rank NCCL path not exercised here")
     world = 8 if ngpu >= 8 else (4 if ngpu >= 4 else 2)
     if transport == "allreduce" and payload == "fp16" and world != 2:
         world = 2  # NCCL's fp16 SUM is one RN addition only at two ranks
-    mp.spawn(_rank, args=(world, _port(), str(tmp_path), transport, payload, size), nprocs=world,
-             join=True)
+    mp.spawn(_rank, args=(world, _port(), str(tmp_path), transport, payload, size, chunks),
+             nprocs=world, join=True)
     M, HIDDEN, FFN = SIZES[size]
     h, X, w1, s1, w2, s2, G, segments = _weights(size)
     labels = np.zeros(M, np.int32)
@@ -145,5 +153,5 @@ def test_mlp_block_over_nccl_matches_oracle(cuda_device, oracle, tmp_path, trans
         for call in range(2):
             got = np.load(tmp_path / f"r{r}_{call}.npy")
             differ += _check(got, ref, exact, f"rank {r} of {world}, call {call}")
-    print(f"\n[{transport}/{payload}/{size}] world {world}, multicast used: {nvls}, "
+    print(f"\n[{transport}/{payload}/{size}/chunks {chunks}] world {world}, multicast used: {nvls}, "
           f"elements differing from the rank-order sum: {differ}")

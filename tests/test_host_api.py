@@ -189,3 +189,24 @@ def test_prepare_rejects_partial_groups_before_the_workspace():
         swiglu_quant.prepare(torch.zeros((4, 2 * 384), dtype=torch.float16), comm,
                              peer_workspace=ws)
     assert ws.seen == [] and comm.calls == []
+
+
+@pytest.mark.parametrize("rows,chunks", [(32768, 4), (2085, 3), (4096, 2), (300, 4), (256, 8),
+                                         (1, 2), (32768 + 77, 4)])
+def test_pipeline_bounds_tile_the_rows(rows, chunks):
+    """The pipelined MLP forward's row chunks cover every row once, start on whole
+    256-row tiles and are never empty."""
+    from h3tp.tp_dit import pipeline_bounds
+    b = pipeline_bounds(rows, chunks)
+    assert b[0][0] == 0 and b[-1][1] == rows
+    assert all(x[1] == y[0] for x, y in zip(b, b[1:]))
+    assert all(a < e for a, e in b) and all(a % 256 == 0 for a, _ in b)
+    assert len(b) <= max(1, chunks)
+
+
+def test_policy_pipeline_chunks_validation():
+    from h3tp.h3_operator_policy import H3OperatorPolicy
+    assert H3OperatorPolicy().mlp_pipeline_chunks == 0
+    for bad in (-1, 65, 2.0, True):
+        with pytest.raises(ValueError):
+            H3OperatorPolicy(mlp_pipeline_chunks=bad)
