@@ -72,6 +72,9 @@ def parse():
     ap.add_argument("--transport", choices=["p2p", "nvls", "rowblock", "allreduce"], default="p2p",
                     help="row partial exchange at TP > 1 (peer memory, in-switch NVLS reduction, "
                          "NCCL row blocks or NCCL all-reduce)")
+    ap.add_argument("--workload", choices=["dit_mlp_block", "dit_linear_block"],
+                    default="dit_mlp_block",
+                    help="dit_linear_block: BASELINE config 4's whole linear set (QKV, O, FC1, FC2)")
     ap.add_argument("--chunks", type=int, default=0,
                     help="TP > 1: row chunks of the pipelined MLP forward (0 = by size, 1 = off)")
     ap.add_argument("--no-parity", action="store_true",
@@ -327,30 +330,11 @@ def oracle_block_rows(rows, h, x, w1, s1, w2, s2, world, payload):
     """The MLP block's residual output for the given rows, computed by the CPU checker
     exactly as `world` ranks shard it (FC1 rows per patches/parallel_int8.packed_rows,
     FC2 contiguous K blocks, rank-order partial reduction)."""
-    import numpy as np
-    from oracle import oracle as O
     import torch
+    from oracle import oracle as O
     idx = torch.from_numpy(rows)
-    hs = h[idx].numpy()
-    ref = x[idx].numpy().copy()
-    w1n, s1n, w2n, s2n = w1.numpy(), s1.numpy(), w2.numpy(), s2.numpy().ravel()
-    q, a = O.column_quantize(hs, True)
-    kl = w2n.shape[1] // world
-    acts, w2s = [], []
-    for r in range(world):
-        w1r, s1r = O.packed_rows(w1n, s1n, r, world, 2)
-        acts.append(O.swiglu_epilogue(O.int8_gemm(q, w1r), a, s1r.ravel()))
-        w2s.append(np.ascontiguousarray(w2n[:, r * kl:(r + 1) * kl]))
-    if payload == "fp16" or world == 1:
-        O.fc2_fused_stored(acts, w2s, s2n, out="residual", residual=ref, kind="act_f32")
-    else:  # packed INT8 group-128 payloads, rank-order reconstruction
-        rots = [O.fc2_rotate(v, "act_f32") for v in acts]
-        gmax = np.max(np.stack([m for _, m in rots]), 0)
-        qs = [O.row_quantize(R, gmax) for R, _ in rots]
-        packed = np.stack([O.pack8(O.int8_gemm(qq, w)) for (qq, _), w in zip(qs, w2s)])
-        restored = O.unpack8_restore(packed, w2n.shape[0])
-        O.dequantize_i32(restored, qs[0][1], s2n, out="residual", residual=ref)
-    return ref
+    return O.mlp_block(x[idx].numpy(), h[idx].numpy(), w1.numpy(), s1.numpy(), w2.numpy(),
+                       s2.numpy(), world, payload=payload)
 
 
 def rows_bit_exact(got, ref):
@@ -763,6 +747,186 @@ def run_ours(args):
     return 0
 
 
+def linear_block_ops(M, hidden, ffn):
+    """QKV [hidden -> 3 hidden] + O [hidden -> hidden] + FC1 [hidden -> 2 ffn] +
+    FC2 [ffn -> hidden], 2 M N K each."""
+    return 2 * M * hidden * (3 * hidden + hidden + 2 * ffn) + 2 * M * ffn * hidden
+
+
+def make_linear_weights(hidden, ffn, seed=2):
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    wqkv = torch.randint(-127, 128, (3 * hidden, hidden), generator=g, dtype=torch.int8)
+    sqkv = (torch.rand((3 * hidden, 1), generator=g) * 9e-3 + 1e-3).float()
+    wo = torch.randint(-127, 128, (hidden, hidden), generator=g, dtype=torch.int8)
+    so = ((torch.rand((hidden, 1), generator=g) * 9e-3 + 1e-3) / 512).float()  # /512 fold
+    return wqkv, sqkv, wo, so
+
+
+def run_linear_block(args):
+    """BASELINE config 4, the whole DiT block linear set at M tokens: QKV (column) ->
+    attention stand-in (the V third) -> O (row, gated residual) -> FC1 (column, SwiGLU)
+    -> FC2 (row, gated residual), through TPDiTLinearBlockINT8.forward; same timing,
+    e2e, parity and clock rules as the MLP block."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    comm = None
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        comm = dist
+    from h3tp import _native, ops
+    from h3tp.h3_operator_policy import H3OperatorPolicy
+    from h3tp.tp_dit import TPDiTLinearBlockINT8
+
+    M, hidden, ffn = args.tokens, args.hidden, args.ffn
+    w1, s1, w2, s2 = make_weights(hidden, ffn)
+    wqkv, sqkv, wo, so = make_linear_weights(hidden, ffn)
+    _, x_cpu = make_inputs(M, hidden)
+    x_cpu = (x_cpu.float() * 4).half()  # the block input and residual, ~N(0, 1)
+    block = TPDiTLinearBlockINT8(hidden, ffn, rank, world, device=dev, comm=comm,
+                                 policy=H3OperatorPolicy(row_transport=args.transport,
+                                                         fc1_swiglu_epilogue=True,
+                                                         mlp_pipeline_chunks=args.chunks))
+    block.qkv_proj.load_shard_from_full(wqkv, sqkv)
+    block.out_proj.load_shard_from_full(wo, so)
+    block.fc1.load_shard_from_full(w1, s1)
+    block.fc2.load_shard_from_full(w2, s2)
+    x = x_cpu.to(dev)
+    stream = torch.cuda.current_stream(dev)
+    with torch.no_grad():
+        for _ in range(max(3, args.warmup)):
+            block(x)
+        torch.cuda.synchronize()
+        if comm:
+            dist.barrier()
+        calls0 = ops.launch_count()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clocks:
+            if comm:
+                dist.barrier()
+            torch.cuda.synchronize()
+            start.record(stream)
+            for _ in range(args.steps):
+                block(x)
+            end.record(stream)
+            torch.cuda.synchronize()
+            if comm:
+                dist.barrier()
+        launches = ops.launch_count() - calls0
+        t = torch.tensor([start.elapsed_time(end)], device=dev, dtype=torch.float64)
+        if comm:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_per_step = float(t[0]) / args.steps
+        x_before = x.clone()
+        x_after = x.clone()
+        block(x_after)
+        torch.cuda.synchronize()
+
+        e2e = None
+        per = M // world if M % world == 0 else M
+        a0, a1 = (rank * per, (rank + 1) * per) if per != M else (0, M)
+        if not args.no_e2e:
+            x_pin = x_cpu.pin_memory()
+            out_pin = torch.empty_like(x_cpu).pin_memory()
+            xd = torch.empty_like(x)
+            n_e2e = max(4, args.steps // 2)
+
+            def run_e2e(n):
+                for _ in range(n):
+                    xd[a0:a1].copy_(x_pin[a0:a1], non_blocking=True)
+                    if per != M:
+                        dist.all_gather_into_tensor(xd, xd[a0:a1])
+                    y = block(xd)
+                    out_pin[a0:a1].copy_(y[a0:a1], non_blocking=True)
+
+            run_e2e(2)
+            torch.cuda.synchronize()
+            if comm:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            run_e2e(n_e2e)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            te = torch.tensor([e0.elapsed_time(e1) / n_e2e], device=dev, dtype=torch.float64)
+            if comm:
+                dist.all_reduce(te, op=dist.ReduceOp.MAX)
+            e2e_ms = float(te[0])
+            e2e = {"value": round(linear_block_ops(M, hidden, ffn) / (e2e_ms * 1e-3) / 1e12, 3),
+                   "unit": "TOPS", "ms_per_step": round(e2e_ms, 4),
+                   "h2d_bytes_per_step": x_cpu.numel() * 2, "d2h_bytes_per_step": x_cpu.numel() * 2,
+                   "api": "TPDiTLinearBlockINT8.forward per step: the residual uploaded from pinned "
+                          "host memory (1/t per rank, all-gathered at t > 1) and each rank's 1/t "
+                          "of the result read back; copies in the stream order of the step"}
+        err = _native.device_error(local)
+        if comm:
+            e = torch.tensor([err], device=dev)
+            dist.all_reduce(e, op=dist.ReduceOp.MAX)
+            err = int(e.item())
+        int8 = measure_int8_peak(dev) if rank == 0 else None
+
+    parity = None
+    if not args.no_parity:
+        from oracle import oracle as O
+        torch.set_num_threads(max(1, (os.cpu_count() or 1) // world))
+        rows = sample_rows(0, M, rank)
+        idx = torch.from_numpy(rows)
+        ref = O.linear_block(x_before.cpu()[idx].numpy(), wqkv.numpy(), sqkv.numpy(), wo.numpy(),
+                             so.numpy(), w1.numpy(), s1.numpy(), w2.numpy(), s2.numpy(), world)
+        n_rows, n_bad = rows_bit_exact(x_after[idx.to(dev)].cpu().numpy(), ref)
+        c = torch.tensor([n_rows, n_bad], device=dev, dtype=torch.int64)
+        if comm:
+            dist.all_reduce(c, op=dist.ReduceOp.SUM)
+        n_rows, n_bad = (int(v) for v in c.tolist())
+        parity = {"rows": n_rows, "mismatched_rows": n_bad, "bit_exact": n_bad == 0, "tp": world,
+                  "checker": "CPU oracle composition (oracle.linear_block)"}
+    if comm:
+        dist.barrier()
+    ops_step = linear_block_ops(M, hidden, ffn)
+    value = ops_step / (ms_per_step * 1e-3) / 1e12
+    peak = int8["peak"] if int8 else None
+    cfg = workload_config(args, world)
+    cfg["workload"] = "dit_linear_block"
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "TOPS", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "us_per_block": round(ms_per_step * 1e3, 1), "tops_per_gpu": round(value / world, 3),
+        "frac_of_int8_peak_per_gpu": round(value / world / peak, 4) if peak else None,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded N(0,1) residual, random int8 weights)", "config": cfg,
+        "roofline": {"kernel": "the whole block (four tcgen05 GEMMs with their producers and "
+                               "transports)", "bound": "tensor",
+                     "achieved": round(value / world, 2), "peak": peak, "unit": "TOPS",
+                     "frac": round(value / world / peak, 4) if peak else None, "traffic": None,
+                     "peak_source": "measured in this run (see the MLP block line)"},
+        "gpu_launches": int(launches), "device_error": err,
+    }
+    if parity is not None:
+        line["parity"] = parity
+    clk = clocks.summary()
+    line["clocks"] = {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
+                      "reasons": clk["reasons"], "samples": clk["samples"]}
+    if e2e is not None:
+        line["e2e"] = e2e
+    if comm:
+        from h3tp import peer
+        peer.release()
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_sweep(args):
     """M x (K, N) through the column linear (rotation + row quant +
     GEMM + ordered fp16 epilogue) and the TP1 row linear (post-SwiGLU fp16 input:
@@ -871,6 +1035,8 @@ def main():
         return run_reference(args)
     if args.int8_peak:
         return run_int8_peak(args)
+    if args.workload == "dit_linear_block":
+        return run_linear_block(args)
     if args.sweep or args.sweep_producers:
         return run_sweep(args)
     return run_ours(args)

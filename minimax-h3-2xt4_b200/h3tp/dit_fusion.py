@@ -168,7 +168,8 @@ def row_gated(module, value, residual, gate, segments, comm, input_act=None):
     if (input_act not in (None, "swiglu") or module.weight.dtype != torch.int8
             or module.weight.shape[0] != residual.shape[1]
             or module.weight_scale.numel() != residual.shape[1]
-            or module.weight_scale.dtype != torch.float32 or kl % 256):
+            or module.weight_scale.dtype != torch.float32
+            or (kl % 256 if input_act == "swiglu" else (kl * world) % 256)):
         return None
     labels = None
     if gate is not None:

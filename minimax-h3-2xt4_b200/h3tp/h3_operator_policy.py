@@ -141,8 +141,10 @@ def row_linear(module, x, fallback, comm, input_act=None):
                                     payload=policy.row_payload,
                                     peer_max=policy.fc2_max_exchange == "peer")
         _fallback("FC2 fused quantizer", str(x.device), None)
-    if input_act is None and x.shape[-1] % 256 == 0 and module.convrot_groupsize == 256:
-        # O projection: local ConvRot of owned groups, global row max, quantise.
+    if (input_act is None and (x.shape[-1] * module.world_size) % 256 == 0
+            and module.convrot_groupsize == 256):
+        # O projection: local ConvRot of owned groups (or, for slices that split a group,
+        # of the gathered rows), global row max, quantise.
         from .row_quant import global_row_quantize
         q, scale = global_row_quantize(x, comm, module.world_size, 256, None, division=division)
         out = quant._finish_quantized(q, scale, module.weight, module.weight_scale.reshape(-1),

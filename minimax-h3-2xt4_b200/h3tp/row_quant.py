@@ -10,7 +10,12 @@ reference's production __fdividef).
 global_row_quantize(): the O-projection's local ConvRot of whole owned 256-groups,
 MAX all-reduce of the row maxima, then quantisation (tilelang_row_quant.py:89-146,
 the P0-C local-rotation variant, which is the only form that needs no padded
-full-width GEMM once the rotation is a butterfly rather than a GEMM).
+full-width GEMM once the rotation is a butterfly rather than a GEMM).  When a rank's
+slice does not hold whole groups (the O projection at TP 8: 3072 / 8 = 384 columns),
+the rows are gathered first, as the reference's exact full-gather route does
+(parallel_int8.py:72-94): every rank rotates and quantises the complete row (one global
+row maximum, no exchange of maxima) and keeps its own columns' codes - the same codes
+the local route gives wherever both apply.
 """
 from __future__ import annotations
 
@@ -50,11 +55,13 @@ def global_row_quantize(x: torch.Tensor, comm, world_size: int | None = None, gr
     if groupsize != 256:
         raise ValueError("Whole regular ConvRot256 groups required")
     flat = x.reshape(-1, x.shape[-1])
-    if flat.shape[-1] % groupsize:
-        raise ValueError("ConvRot groups must remain wholly owned by a rank")
     kind = "act_f32" if flat.dtype == torch.float32 else "act_f16"
     flat = flat.contiguous()
     world = C.world_of(comm) if world_size is None else world_size
+    if flat.shape[-1] % groupsize:
+        if world == 1 or (flat.shape[-1] * world) % groupsize:
+            raise ValueError("ConvRot groups must remain wholly owned by a rank")
+        return _gathered_row_quantize(flat, comm, world, kind, division)
     if world == 1:
         q, s, _ = ops.swiglu_rotate_quantize_local(flat, kind, division)
         if consume_input:
@@ -68,3 +75,19 @@ def global_row_quantize(x: torch.Tensor, comm, world_size: int | None = None, gr
     if consume_input:
         x.set_()
     return q, s
+
+
+def _gathered_row_quantize(flat: torch.Tensor, comm, world: int, kind: str, division: str):
+    """Rows gathered over the group (rank order along the features), rotated and
+    quantised whole on every rank; returns this rank's columns of the codes and the
+    row scales."""
+    width = flat.shape[-1]
+    with label("gather_rows"):
+        parts = [torch.empty_like(flat) for _ in range(world)]
+        comm.all_gather(parts, flat)
+        full = torch.cat(parts, dim=-1)
+        del parts
+    with label("full_row_quantization"):
+        q, s, _ = ops.swiglu_rotate_quantize_local(full, kind, division)
+    r = C.rank_of(comm)
+    return q[:, r * width:(r + 1) * width].contiguous(), s

@@ -198,142 +198,157 @@ class TPDiTMLPINT8(nn.Module):
 
     def forward(self, x: torch.Tensor, h: torch.Tensor, gate=None, segments=None) -> torch.Tensor:
         """x: fp16 residual [S, hidden] (updated in place); h: fp16 normed input."""
-        chunks = self.pipeline_chunks(x, h, gate)
-        if chunks > 1:
-            return self.forward_pipelined(x, h, gate, segments, chunks)
-        fc1_out = self.fc1(h)
-        return self.fc2(fc1_out, input_act="swiglu", residual=x, gate=gate, segments=segments)
+        return mlp_forward(self.fc1, self.fc2, x, h, gate, segments)
 
     def pipeline_chunks(self, x, h, gate=None) -> int:
-        """Row chunks of the pipelined TP > 1 forward (1: the plain module chain).
-
-        The pipelined form needs the peer-memory row transport (p2p or nvls) with the
-        scaled-fp16 payload, the in-kernel maximum exchange, FC1's SwiGLU epilogue, no
-        LoRA, an NCCL group, and fp16 contiguous [S, hidden] residual and input."""
-        from . import ops, peer as P
-        pol = getattr(self.fc2, "operator_policy", None)
-        world = self.fc2.world_size
-        if (pol is None or world == 1 or pol.mlp_pipeline_chunks == 1
-                or pol.row_transport not in ("p2p", "nvls") or pol.row_payload != "fp16"
-                or pol.fc2_max_exchange != "peer" or not pol.scaled_transport
-                or pol.fc2_quantizer not in ("fused_stored", "fused_recompute")
-                or not getattr(self.fc1, "_swiglu_epilogue", False)
-                or getattr(self.fc1, "lora_adapter", None) is not None
-                or getattr(self.fc2, "lora_adapter", None) is not None
-                or torch.is_grad_enabled()):
-            return 1
-        hidden, kl = self.fc2.out_features, self.fc2.in_features_per_rank
-        if (x.dtype != torch.float16 or h.dtype != torch.float16 or x.ndim != 2 or h.ndim != 2
-                or x.shape != h.shape or x.shape[1] != hidden or not x.is_contiguous()
-                or not h.is_contiguous() or not x.is_cuda or hidden % 8 or kl % 256
-                or kl > ops.PEER_PRODUCER_MAX_WIDTH or (gate is not None and gate.ndim != 2)):
-            return 1
-        if not P.available(self.fc2._comm()):
-            return 1
-        rows = x.shape[0]
-        chunks = pol.mlp_pipeline_chunks or (4 if rows >= 4 * 4096 else 2 if rows >= 2 * 2048 else 1)
-        return max(1, min(chunks, rows // 256))
+        return mlp_pipeline_chunks(self.fc1, self.fc2, x, h, gate)
 
     def forward_pipelined(self, x, h, gate=None, segments=None, chunks: int = 4, timer=None):
-        """The TP > 1 forward over row chunks, with the partial-sum exchange of one chunk
-        overlapping the GEMMs of the next.
+        return mlp_forward_pipelined(self.fc1, self.fc2, x, h, gate, segments, chunks, timer)
 
-        Per chunk c: column quantise + FC1 GEMM with the SwiGLU epilogue (F_c), the FC2
-        producer with the row maxima exchanged in the kernel (P_c), the FC2 GEMM writing
-        its scaled-fp16 partial into the peer workspace (G_c), the reduce + gated
-        residual of the rank's rows (R_c) and the gather of the other ranks' rows.  F and G
-        run on the caller's stream; P and R, the only kernels that wait for other ranks,
-        run on one exchange stream in the same order on every rank (P0, P1, R0, P2, R1,
-        ..., R_{n-1}), so no two kernels that wait on other GPUs are ever in flight
-        together on a GPU.  Issue order on the caller's stream is F0, F1, G0, F2, G1, ...:
-        R_c, which is bound by NVLink and holds few SM resources, runs while the tensor
-        cores work on F_{c+2} and G_{c+1}.  The bits are those of forward(): the same
-        kernels on the same rows, the rows of a chunk reduced in rank order.
-        `timer(name, chunk, start_or_end)` (optional) is called around each launch to
-        record events on the stream it runs on."""
-        from . import ops, peer as P, transport as T
-        from .dit_fusion import labels_for
-        dev = x.device
-        rows, hidden = x.shape
-        world = self.fc2.world_size
-        kl = self.fc2.in_features_per_rank
-        pol = self.fc2.operator_policy
-        comm = self.fc2._comm()
-        labels = None
-        if gate is not None:
-            labels = labels_for(x, segments, gate.shape[0])
-            if labels is None:
-                raise ValueError("gate given without a valid segment layout")
-            gate = gate.contiguous()
-        ws = P.workspace(comm, dev, hidden, rows)
-        comp = torch.cuda.current_stream(dev)
-        xs = _exchange_stream(dev)
-        q1 = torch.empty((rows, hidden), dtype=torch.int8, device=dev)
-        s1 = torch.empty((rows, 1), dtype=torch.float32, device=dev)
-        act = torch.empty((rows, kl), dtype=torch.float32, device=dev)
-        q2 = torch.empty((rows, kl), dtype=torch.int8, device=dev)
-        s2 = torch.empty((rows, 1), dtype=torch.float32, device=dev)
-        for t in (act, q2, s2, x) + tuple(v for v in (gate, labels) if v is not None):
-            t.record_stream(xs)
-        xs.wait_stream(comp)
-        shift = T.shift_for(kl, world)
-        w1s = self.fc1.weight_scale.reshape(-1)
-        w2s = self.fc2.weight_scale.reshape(-1)
-        nvls = pol.row_transport == "nvls"
-        bounds = pipeline_bounds(rows, chunks)
-        ev = {k: [torch.cuda.Event() for _ in bounds] for k in ("fc1", "prod", "fc2")}
-        mark = timer or (lambda *a: None)
 
-        def front(c):
-            a, b = bounds[c]
-            mark("column_quantize", c, 0)
-            ops.column_quantize(h[a:b], True, out_q=q1[a:b], out_scale=s1[a:b])
-            mark("column_quantize", c, 1)
-            mark("fc1_gemm", c, 0)
-            ops.int8_gemm_swiglu(q1[a:b], self.fc1.weight, s1[a:b], w1s, None, torch.float32,
-                                 out=act[a:b])
-            mark("fc1_gemm", c, 1)
-            ev["fc1"][c].record(comp)
+def mlp_forward(fc1, fc2, x, h, gate=None, segments=None):
+    """FC1 -> FC2 with the gated residual: pipelined over row chunks where
+    mlp_pipeline_chunks allows it, else the plain module chain."""
+    chunks = mlp_pipeline_chunks(fc1, fc2, x, h, gate)
+    if chunks > 1:
+        return mlp_forward_pipelined(fc1, fc2, x, h, gate, segments, chunks)
+    fc1_out = fc1(h)
+    return fc2(fc1_out, input_act="swiglu", residual=x, gate=gate, segments=segments)
 
-        def producer(c):
-            a, b = bounds[c]
-            xs.wait_event(ev["fc1"][c])
-            with torch.cuda.stream(xs):
-                mark("peer_producer", c, 0)
-                ws.quantize_rows_at(act[a:b], a, "act_f32", pol.quant_division, out_q=q2[a:b],
-                                    out_scale=s2[a:b])
-                mark("peer_producer", c, 1)
-            ev["prod"][c].record(xs)
 
-        def back(c):
-            a, b = bounds[c]
-            comp.wait_event(ev["prod"][c])
-            mark("fc2_gemm", c, 0)
-            ops.int8_gemm_row_encode(q2[a:b], self.fc2.weight, shift, out=ws.partial_rows(a, b - a))
-            mark("fc2_gemm", c, 1)
-            ev["fc2"][c].record(comp)
+def mlp_pipeline_chunks(fc1, fc2, x, h, gate=None) -> int:
+    """Row chunks of the pipelined TP > 1 forward (1: the plain module chain).
 
-        def exchange(c):
-            a, b = bounds[c]
-            xs.wait_event(ev["fc2"][c])
-            with torch.cuda.stream(xs):
-                mark("reduce_gather", c, 0)
-                ws.reduce_rows(a, b - a, shift, s2[a:b], w2s, x[a:b], gate,
-                               None if labels is None else labels[a:b], nvls=nvls)
-                ws.gather_rows(a, b - a, x[a:b])
-                mark("reduce_gather", c, 1)
+    The pipelined form needs the peer-memory row transport (p2p or nvls) with the
+    scaled-fp16 payload, the in-kernel maximum exchange, FC1's SwiGLU epilogue, no
+    LoRA, an NCCL group, and fp16 contiguous [S, hidden] residual and input."""
+    from . import ops, peer as P
+    pol = getattr(fc2, "operator_policy", None)
+    world = fc2.world_size
+    if (pol is None or world == 1 or pol.mlp_pipeline_chunks == 1
+            or pol.row_transport not in ("p2p", "nvls") or pol.row_payload != "fp16"
+            or pol.fc2_max_exchange != "peer" or not pol.scaled_transport
+            or pol.fc2_quantizer not in ("fused_stored", "fused_recompute")
+            or not getattr(fc1, "_swiglu_epilogue", False)
+            or getattr(fc1, "lora_adapter", None) is not None
+            or getattr(fc2, "lora_adapter", None) is not None
+            or torch.is_grad_enabled()):
+        return 1
+    hidden, kl = fc2.out_features, fc2.in_features_per_rank
+    if (x.dtype != torch.float16 or h.dtype != torch.float16 or x.ndim != 2 or h.ndim != 2
+            or x.shape != h.shape or x.shape[1] != hidden or not x.is_contiguous()
+            or not h.is_contiguous() or not x.is_cuda or hidden % 8 or kl % 256
+            or kl > ops.PEER_PRODUCER_MAX_WIDTH or (gate is not None and gate.ndim != 2)):
+        return 1
+    if not P.available(fc2._comm()):
+        return 1
+    rows = x.shape[0]
+    chunks = pol.mlp_pipeline_chunks or (4 if rows >= 4 * 4096 else 2 if rows >= 2 * 2048 else 1)
+    return max(1, min(chunks, rows // 256))
 
-        n = len(bounds)
-        front(0)
-        producer(0)
-        for c in range(n):
-            if c + 1 < n:
-                front(c + 1)
-                producer(c + 1)
-            back(c)
-            exchange(c)
-        comp.wait_stream(xs)
-        return x
+
+def mlp_forward_pipelined(fc1, fc2, x, h, gate=None, segments=None, chunks: int = 4,
+                          timer=None):
+    """The TP > 1 forward over row chunks, with the partial-sum exchange of one chunk
+    overlapping the GEMMs of the next.
+
+    Per chunk c: column quantise + FC1 GEMM with the SwiGLU epilogue (F_c), the FC2
+    producer with the row maxima exchanged in the kernel (P_c), the FC2 GEMM writing
+    its scaled-fp16 partial into the peer workspace (G_c), the reduce + gated
+    residual of the rank's rows (R_c) and the gather of the other ranks' rows.  F and G
+    run on the caller's stream; P and R, the only kernels that wait for other ranks,
+    run on one exchange stream in the same order on every rank (P0, P1, R0, P2, R1,
+    ..., R_{n-1}), so no two kernels that wait on other GPUs are ever in flight
+    together on a GPU.  Issue order on the caller's stream is F0, F1, G0, F2, G1, ...:
+    R_c, which is bound by NVLink and holds few SM resources, runs while the tensor
+    cores work on F_{c+2} and G_{c+1}.  The bits are those of forward(): the same
+    kernels on the same rows, the rows of a chunk reduced in rank order.
+    `timer(name, chunk, start_or_end)` (optional) is called around each launch to
+    record events on the stream it runs on."""
+    from . import ops, peer as P, transport as T
+    from .dit_fusion import labels_for
+    dev = x.device
+    rows, hidden = x.shape
+    world = fc2.world_size
+    kl = fc2.in_features_per_rank
+    pol = fc2.operator_policy
+    comm = fc2._comm()
+    labels = None
+    if gate is not None:
+        labels = labels_for(x, segments, gate.shape[0])
+        if labels is None:
+            raise ValueError("gate given without a valid segment layout")
+        gate = gate.contiguous()
+    ws = P.workspace(comm, dev, hidden, rows)
+    comp = torch.cuda.current_stream(dev)
+    xs = _exchange_stream(dev)
+    q1 = torch.empty((rows, hidden), dtype=torch.int8, device=dev)
+    s1 = torch.empty((rows, 1), dtype=torch.float32, device=dev)
+    act = torch.empty((rows, kl), dtype=torch.float32, device=dev)
+    q2 = torch.empty((rows, kl), dtype=torch.int8, device=dev)
+    s2 = torch.empty((rows, 1), dtype=torch.float32, device=dev)
+    for t in (act, q2, s2, x) + tuple(v for v in (gate, labels) if v is not None):
+        t.record_stream(xs)
+    xs.wait_stream(comp)
+    shift = T.shift_for(kl, world)
+    w1s = fc1.weight_scale.reshape(-1)
+    w2s = fc2.weight_scale.reshape(-1)
+    nvls = pol.row_transport == "nvls"
+    bounds = pipeline_bounds(rows, chunks)
+    ev = {k: [torch.cuda.Event() for _ in bounds] for k in ("fc1", "prod", "fc2")}
+    mark = timer or (lambda *a: None)
+
+    def front(c):
+        a, b = bounds[c]
+        mark("column_quantize", c, 0)
+        ops.column_quantize(h[a:b], True, out_q=q1[a:b], out_scale=s1[a:b])
+        mark("column_quantize", c, 1)
+        mark("fc1_gemm", c, 0)
+        ops.int8_gemm_swiglu(q1[a:b], fc1.weight, s1[a:b], w1s, None, torch.float32,
+                             out=act[a:b])
+        mark("fc1_gemm", c, 1)
+        ev["fc1"][c].record(comp)
+
+    def producer(c):
+        a, b = bounds[c]
+        xs.wait_event(ev["fc1"][c])
+        with torch.cuda.stream(xs):
+            mark("peer_producer", c, 0)
+            ws.quantize_rows_at(act[a:b], a, "act_f32", pol.quant_division, out_q=q2[a:b],
+                                out_scale=s2[a:b])
+            mark("peer_producer", c, 1)
+        ev["prod"][c].record(xs)
+
+    def back(c):
+        a, b = bounds[c]
+        comp.wait_event(ev["prod"][c])
+        mark("fc2_gemm", c, 0)
+        ops.int8_gemm_row_encode(q2[a:b], fc2.weight, shift, out=ws.partial_rows(a, b - a))
+        mark("fc2_gemm", c, 1)
+        ev["fc2"][c].record(comp)
+
+    def exchange(c):
+        a, b = bounds[c]
+        xs.wait_event(ev["fc2"][c])
+        with torch.cuda.stream(xs):
+            mark("reduce_gather", c, 0)
+            ws.reduce_rows(a, b - a, shift, s2[a:b], w2s, x[a:b], gate,
+                           None if labels is None else labels[a:b], nvls=nvls)
+            ws.gather_rows(a, b - a, x[a:b])
+            mark("reduce_gather", c, 1)
+
+    n = len(bounds)
+    front(0)
+    producer(0)
+    for c in range(n):
+        if c + 1 < n:
+            front(c + 1)
+            producer(c + 1)
+        back(c)
+        exchange(c)
+    comp.wait_stream(xs)
+    return x
 
 
 def pipeline_bounds(rows: int, chunks: int) -> list[tuple[int, int]]:
@@ -384,6 +399,8 @@ class TPDiTLinearBlockINT8(nn.Module):
         inner = self.hidden // self.world_size
         qkv = self.qkv_proj(x)
         attn_out = qkv[:, 2 * inner:3 * inner].contiguous()
+        del qkv
         x = self.out_proj(attn_out, residual=x, gate=gate_msa, segments=segments)
-        fc1_out = self.fc1(x)
-        return self.fc2(fc1_out, input_act="swiglu", residual=x, gate=gate_mlp, segments=segments)
+        # FC1 reads the updated residual (the norm is the identity here): a copy, since
+        # the MLP updates x in place
+        return mlp_forward(self.fc1, self.fc2, x, x.clone(), gate_mlp, segments)

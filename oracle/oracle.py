@@ -342,3 +342,78 @@ def fc2_fused_stored(xs, weights, weight_scale, out="f32", residual=None, gate=N
     y = row_reduce_finish(enc, shift, scale, weight_scale, out=out, residual=residual,
                           gate=gate, labels=labels)
     return y, qs, partials
+
+
+# ----------------------------------------------------------------------------
+# compositions of whole blocks at TP = world (the arithmetic of every rank, combined
+# the way the collectives combine it); inputs and outputs are numpy arrays
+# ----------------------------------------------------------------------------
+def mlp_block(x, h, w1, s1, w2, s2, world, gate=None, labels=None, payload="fp16"):
+    """TPDiTMLPINT8.forward at TP = world (tp_dit.py:347-366): FC1 on rank shards
+    (packed_rows, components [gate | up]) with the FP32 SwiGLU, FC2 over contiguous K
+    blocks with the global row maximum, scaled-fp16 partials summed in rank order (or,
+    payload 'int8_gather', the packed INT8 group-128 payloads), gated residual.
+    Returns the updated residual (x is not modified)."""
+    ref = np.array(x, dtype=np.float16, copy=True)
+    s2 = np.asarray(s2, np.float32).ravel()
+    q, a = column_quantize(h, True)
+    kl = w2.shape[1] // world
+    acts, w2s = [], []
+    for r in range(world):
+        w1r, s1r = packed_rows(w1, s1, r, world, 2)
+        acts.append(swiglu_epilogue(int8_gemm(q, w1r), a, np.asarray(s1r).ravel()))
+        w2s.append(np.ascontiguousarray(w2[:, r * kl:(r + 1) * kl]))
+    if payload == "fp16" or world == 1:
+        fc2_fused_stored(acts, w2s, s2, out="residual", residual=ref, gate=gate, labels=labels,
+                         kind="act_f32")
+        return ref
+    rots = [fc2_rotate(v, "act_f32") for v in acts]
+    gmax = np.max(np.stack([m for _, m in rots]), 0)
+    qs = [row_quantize(R, gmax) for R, _ in rots]
+    packed = np.stack([pack8(int8_gemm(qq, w)) for (qq, _), w in zip(qs, w2s)])
+    restored = unpack8_restore(packed, w2.shape[0])
+    dequantize_i32(restored, qs[0][1], s2, out="residual", residual=ref, gate=gate, labels=labels)
+    return ref
+
+
+def o_projection(x, attn, wo, so, world, gate=None, labels=None):
+    """RowParallel O projection with the gated residual at TP = world: attn [M, K] is the
+    full attention output (rank r holds columns [r K/t, (r+1) K/t)).  The rows are
+    rotated per 256-group and quantised with one global row maximum (whether each rank
+    rotates its own whole groups or, when its slice splits a group, the gathered rows,
+    the codes are the same); each rank multiplies its columns' codes; TP 1 dequantises
+    the exact INT32 sum, TP > 1 sums the scaled-fp16 partials in rank order.  Returns
+    the updated residual."""
+    ref = np.array(x, dtype=np.float16, copy=True)
+    so = np.asarray(so, np.float32).ravel()
+    R, m = fc2_rotate(np.ascontiguousarray(attn, np.float16), "act_f16")
+    q, a = row_quantize(R, m)
+    K = attn.shape[1]
+    kl = K // world
+    parts = [int8_gemm(np.ascontiguousarray(q[:, r * kl:(r + 1) * kl]),
+                       np.ascontiguousarray(wo[:, r * kl:(r + 1) * kl])) for r in range(world)]
+    if world == 1:
+        dequantize_i32(parts[0], a, so, out="residual", residual=ref, gate=gate, labels=labels)
+        return ref
+    shift = transport_shift(K)
+    enc = np.stack([fp16_encode(p, shift) for p in parts])
+    row_reduce_finish(enc, shift, a, so, out="residual", residual=ref, gate=gate, labels=labels)
+    return ref
+
+
+def linear_block(x, wqkv, sqkv, wo, so, w1, s1, w2, s2, world, gate_msa=None, gate_mlp=None,
+                 labels=None):
+    """TPDiTLinearBlockINT8.forward at TP = world: QKV column projection (components
+    q | k | v), the V third as the attention output, O projection + gated residual,
+    then the MLP block on the updated residual (its own input, the norm being the
+    identity).  Returns the final residual."""
+    hidden = x.shape[1]
+    inner = hidden // world
+    q, a = column_quantize(x, True)
+    attn = []
+    for r in range(world):
+        wr, sr = packed_rows(wqkv, sqkv, r, world, 3)
+        qkv = column_epilogue(int8_gemm(q, wr), a, np.asarray(sr).ravel())
+        attn.append(qkv[:, 2 * inner:3 * inner])
+    x1 = o_projection(x, np.concatenate(attn, 1), wo, so, world, gate_msa, labels)
+    return mlp_block(x1, x1, w1, s1, w2, s2, world, gate_mlp, labels)

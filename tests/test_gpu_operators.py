@@ -321,3 +321,34 @@ def test_unsupported_geometry_raises_before_launch(cuda_device):
         ops.int8_gemm_i32(q, w)                  # K not a multiple of 16
     with pytest.raises(ValueError):
         ops.int8_gemm_i32(q.cpu(), w.cpu())      # no CPU fallback
+
+
+def _linear_block_weights(rng, hidden, ffn):
+    wqkv, sqkv = _weights(rng, 3 * hidden, hidden)
+    wo, so = _weights(rng, hidden, hidden, fold=512)
+    w1, s1 = _weights(rng, 2 * ffn, hidden)
+    w2, s2 = _weights(rng, hidden, ffn, fold=512)
+    return wqkv, sqkv, wo, so, w1, s1, w2, s2
+
+
+def test_linear_block_tp1_matches_oracle(cuda_device, oracle):
+    """TPDiTLinearBlockINT8 (QKV -> O + gated residual -> FC1 -> FC2 + gated residual,
+    BASELINE config 4's linear set) at TP 1, bit-exact against oracle.linear_block."""
+    from h3tp.tp_dit import TPDiTLinearBlockINT8
+    rng = np.random.default_rng(31)
+    M, hidden, ffn = 300, 512, 1024
+    W = _linear_block_weights(rng, hidden, ffn)
+    X = rng.standard_normal((M, hidden)).astype(np.float16)
+    G1 = rng.standard_normal((3, hidden)).astype(np.float32)
+    G2 = rng.standard_normal((3, hidden)).astype(np.float32)
+    segments = [(0, 100, 2), (100, 300, 0)]
+    labels = np.array([2] * 100 + [0] * 200, np.int32)
+    blk = TPDiTLinearBlockINT8(hidden, ffn, 0, 1, device=cuda_device)
+    for mod, (w, sc) in zip((blk.qkv_proj, blk.out_proj, blk.fc1, blk.fc2),
+                            zip(W[0::2], W[1::2])):
+        mod.load_shard_from_full(torch.from_numpy(w), torch.from_numpy(sc))
+    x = _t(X, cuda_device)
+    with torch.no_grad():
+        y = blk(x, gate_msa=_t(G1, cuda_device), gate_mlp=_t(G2, cuda_device), segments=segments)
+    ref = oracle.linear_block(X, *W, 1, G1, G2, labels)
+    _eq(_np(y), ref)

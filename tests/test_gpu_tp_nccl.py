@@ -155,3 +155,92 @@ def test_mlp_block_over_nccl_matches_oracle(cuda_device, oracle, tmp_path, trans
             differ += _check(got, ref, exact, f"rank {r} of {world}, call {call}")
     print(f"\n[{transport}/{payload}/{size}/chunks {chunks}] world {world}, multicast used: {nvls}, "
           f"elements differing from the rank-order sum: {differ}")
+
+
+LB = (515, 3072, 8192)  # rows, hidden, ffn: at TP 8 the O projection's 384 columns split groups
+
+
+def _lb_weights():
+    rng = np.random.default_rng(23)
+    M, H, F = LB
+    mk = lambda n, k, fold=1.0: (rng.integers(-127, 128, size=(n, k), dtype=np.int8),  # noqa: E731
+                                 (rng.uniform(1e-3, 1e-2, size=(n, 1)) / fold).astype(np.float32))
+    wqkv, sqkv = mk(3 * H, H)
+    wo, so = mk(H, H, 512)
+    w1, s1 = mk(2 * F, H)
+    w2, s2 = mk(H, F, 512)
+    X = rng.standard_normal((M, H)).astype(np.float16)
+    G1 = rng.standard_normal((3, H)).astype(np.float32)
+    G2 = rng.standard_normal((3, H)).astype(np.float32)
+    segments = [(0, 200, 1), (200, M, 2)]
+    return X, (wqkv, sqkv, wo, so, w1, s1, w2, s2), G1, G2, segments
+
+
+def _lb_rank(rank, world, port, outdir, transport):
+    for p in (str(ROOT), str(ROOT / "minimax-h3-2xt4_b200")):
+        sys.path.insert(0, p)
+    try:
+        import torch.distributed as dist
+        from datetime import timedelta
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                                device_id=dev)
+        from h3tp.h3_operator_policy import H3OperatorPolicy
+        from h3tp.tp_dit import TPDiTLinearBlockINT8
+        from h3tp import _native, peer
+        M, H, F = LB
+        X, W, G1, G2, segments = _lb_weights()
+        blk = TPDiTLinearBlockINT8(H, F, rank, world, device=dev, comm=dist,
+                                   policy=H3OperatorPolicy(row_transport=transport,
+                                                           fc1_swiglu_epilogue=True,
+                                                           mlp_pipeline_chunks=2))
+        for mod, w, sc in zip((blk.qkv_proj, blk.out_proj, blk.fc1, blk.fc2), W[0::2], W[1::2]):
+            mod.load_shard_from_full(torch.from_numpy(w), torch.from_numpy(sc))
+        for call in range(2):
+            x = torch.from_numpy(X.copy()).to(dev)
+            with torch.no_grad():
+                out = blk(x, gate_msa=torch.from_numpy(G1).to(dev),
+                          gate_mlp=torch.from_numpy(G2).to(dev), segments=segments)
+            torch.cuda.synchronize()
+            np.save(os.path.join(outdir, f"r{rank}_{call}.npy"), out.cpu().numpy())
+        if _native.device_error(rank):
+            raise RuntimeError("device error")
+        ws = next(iter(peer._WORKSPACES.values()), None)
+        Path(outdir, f"mc{rank}.txt").write_text(str(int(bool(ws is not None and ws.multicast))))
+        peer.release()
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        Path(outdir, f"err{rank}.txt").write_text(traceback.format_exc())
+        raise
+
+
+@pytest.mark.parametrize("transport", ["p2p", "nvls"])
+def test_linear_block_over_nccl_matches_oracle(cuda_device, oracle, tmp_path, transport):
+    """QKV -> O (+ gated residual) -> pipelined FC1/FC2 (+ gated residual) on every GPU
+    of the box (hidden 3072: at 8 ranks each O-projection slice is 384 columns, so the
+    rows are gathered and rotated whole)."""
+    ngpu = torch.cuda.device_count()
+    if ngpu < 2:
+        pytest.skip("single-GPU box: multi-rank NCCL path not exercised here")
+    world = 8 if ngpu >= 8 else (4 if ngpu >= 4 else 2)
+    mp.spawn(_lb_rank, args=(world, _port(), str(tmp_path), transport), nprocs=world, join=True)
+    M, H, F = LB
+    X, W, G1, G2, segments = _lb_weights()
+    labels = np.zeros(M, np.int32)
+    for a, b, r in segments:
+        labels[a:b] = r
+    ref = oracle.linear_block(X, *W, world, G1, G2, labels)
+    nvls = transport == "nvls" and all((tmp_path / f"mc{r}.txt").read_text() == "1"
+                                       for r in range(world))
+    exact = not (nvls and world > 2)
+    differ = 0
+    for r in range(world):
+        for call in range(2):
+            differ += _check(np.load(tmp_path / f"r{r}_{call}.npy"), ref, exact,
+                             f"rank {r} of {world}, call {call}")
+    print(f"\n[linear block {transport}] world {world}, multicast used: {nvls}, "
+          f"elements differing from the rank-order sum: {differ}")

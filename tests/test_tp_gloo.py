@@ -98,6 +98,29 @@ def test_o_projection_module_tp2(oracle, tmp_path):
         assert np.array_equal(np.load(tmp_path / f"r{r}.npy").view(np.uint16), ref.view(np.uint16))
 
 
+def test_o_projection_module_partial_groups_tp4(oracle, tmp_path):
+    """K = 768 over 4 ranks: 192 columns each, so every rank's slice splits a ConvRot
+    group (the O projection at TP 8 in miniature).  The rows are gathered, rotated and
+    quantised whole; each rank multiplies its own columns' codes."""
+    world, K = 4, 768
+    _run(tp_worker.oproj_case, world, tmp_path, K)
+    rng = np.random.default_rng(9)
+    M, N = 29, 64
+    x = rng.standard_normal((M, K)).astype(np.float16)
+    w = rng.integers(-127, 128, size=(N, K), dtype=np.int8)
+    s = (rng.uniform(1e-3, 1e-2, (N, 1)) / 512).astype(np.float32)
+    R, m = oracle.fc2_rotate(x, "act_f16")
+    q, a = oracle.row_quantize(R, m)
+    kl = K // world
+    shift = oracle.transport_shift(K)
+    enc = np.stack([oracle.fp16_encode(oracle.int8_gemm(np.ascontiguousarray(q[:, r * kl:(r + 1) * kl]),
+                                                        np.ascontiguousarray(w[:, r * kl:(r + 1) * kl])),
+                                       shift) for r in range(world)])
+    ref = oracle.row_reduce_finish(enc, shift, a, s.ravel(), out="f32").astype(np.float16)
+    for r in range(world):
+        assert np.array_equal(np.load(tmp_path / f"r{r}.npy").view(np.uint16), ref.view(np.uint16))
+
+
 def test_unsupported_geometry_raises_before_any_collective(tmp_path):
     _run(tp_worker.guard_case, 2, tmp_path)
     for r in range(2):

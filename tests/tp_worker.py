@@ -63,14 +63,14 @@ def fc2_case(rank, world, port, outdir, mode, transport, scaled, payload="fp16")
         raise
 
 
-def oproj_case(rank, world, port, outdir):
+def oproj_case(rank, world, port, outdir, K=None):
     import torch
     try:
         dist = _init(rank, world, port)
         from h3tp.tp_dit import RowParallelLinearINT8
         from h3tp.h3_operator_policy import H3OperatorPolicy
         rng = np.random.default_rng(9)
-        M, K, N = 29, 256 * world, 64
+        M, K, N = 29, K or 256 * world, 64
         x = rng.standard_normal((M, K)).astype(np.float16)
         w = rng.integers(-127, 128, size=(N, K), dtype=np.int8)
         s = (rng.uniform(1e-3, 1e-2, (N, 1)) / 512).astype(np.float32)
