@@ -970,11 +970,33 @@ def run_sweep(args):
                                       "ms": round(ms, 4), "tops": round(tops, 2),
                                       "frac_of_int8_estimate": round(tops / peak, 4)}), flush=True)
                 del x
-        # row 2 of the scope table: the column input producer, fused modulated RMSNorm ->
-        # ConvRot -> quant, against the unfused route (norm -> fp16 h -> quantiser)
+        # the activation producers of the MLP block at M = 32768 (HBM-bound): the column
+        # quantiser of FC1's input and the TP1 FC2 producer (SwiGLU output -> ConvRot ->
+        # row maximum -> codes in one pass)
         from h3tp import ops
         M = 32768
         hbm = peaks()["hbm_gbs"]
+        staging = os.environ.get("H3_ROW_STAGING", "1") != "0"
+        for K in (3072, 5120):
+            hq = torch.randn((M, K), generator=g, device=dev).half()
+            ms = timed(lambda: ops.column_quantize(hq, True))
+            nbytes = M * K * 2 + M * K + 4 * M
+            print(json.dumps({"sweep": "column_quantize", "M": M, "K": K, "ms": round(ms, 4),
+                              "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                              "frac_of_hbm": round(nbytes / (ms * 1e-3) / 1e9 / hbm, 4),
+                              "row_staging": staging}), flush=True)
+            del hq
+        for kl in (8192, 4096):
+            act = torch.randn((M, kl), generator=g, device=dev) * 0.7
+            ms = timed(lambda: ops.swiglu_rotate_quantize_local(act, "act_f32"))
+            nbytes = M * kl * 4 + M * kl + 8 * M
+            print(json.dumps({"sweep": "fc2_producer_tp1", "M": M, "Kl": kl, "ms": round(ms, 4),
+                              "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                              "frac_of_hbm": round(nbytes / (ms * 1e-3) / 1e9 / hbm, 4),
+                              "row_staging": staging}), flush=True)
+            del act
+        # row 2 of the scope table: the column input producer, fused modulated RMSNorm ->
+        # ConvRot -> quant, against the unfused route (norm -> fp16 h -> quantiser)
         for K in (3072, 5120, 5376):
             x = torch.randn((M, K), generator=g, device=dev).half()
             w = torch.rand((K,), generator=g, device=dev) + 0.5

@@ -6,6 +6,7 @@
 // contract nor reorder it.  The library is also built with --fmad=false.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -498,6 +499,11 @@ int sm_count(int device);
 int* error_word(int device);       // device view of the lazily created mapped error word
 int* error_word_host(int device);  // host view of it (nullptr before its first use)
 int check_launch();                                  // maps cudaGetLastError to a status
+// Tensor map of `rows` rows of `row_bytes` bytes each (row pitch = row_bytes) viewed as
+// uint8 [rows][row_bytes / 128][128], copied in boxes of box_lines 128-byte lines of
+// one row with the 128-byte swizzle (row staging of the activation producers).
+bool encode_row_map(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes,
+                    int box_lines);
 
 inline bool aligned(const void* p, unsigned a) { return ((uintptr_t)p % a) == 0; }
 

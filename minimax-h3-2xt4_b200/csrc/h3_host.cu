@@ -1,5 +1,7 @@
 // Host-side plumbing of the C ABI: device binding, SM counts, the device-side error
 // word that bounded waits set, and status strings.
+#include <cudaTypedefs.h>
+
 #include <mutex>
 
 #include "h3_common.cuh"
@@ -86,6 +88,37 @@ int* error_word_host(int device) {
   if (device < 0 || device >= kMaxDevices) return nullptr;
   std::lock_guard<std::mutex> lock(g_mutex);
   return g_error_host[device];
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 tiled_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+bool encode_row_map(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes,
+                    int box_lines) {
+  auto fn = tiled_encoder();
+  if (fn == nullptr || rows <= 0 || row_bytes <= 0 || row_bytes % 128 != 0 || box_lines < 1 ||
+      box_lines > 256 || (row_bytes / 128) % box_lines != 0 || !aligned(base, 16))
+    return false;
+  cuuint64_t dims[3] = {128, (cuuint64_t)(row_bytes / 128), (cuuint64_t)rows};
+  cuuint64_t strides[2] = {128, (cuuint64_t)row_bytes};
+  cuuint32_t box[3] = {128, (cuuint32_t)box_lines, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 int check_launch() {

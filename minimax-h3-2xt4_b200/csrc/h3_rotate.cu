@@ -102,7 +102,7 @@ static RowTeam row_team(int64_t width) {
 
 // Dynamic shared memory of a producer CTA: one 16 x 17 tile of pairs per half warp and
 // the 32-float reduction buffer.
-static size_t producer_smem(int threads) {
+__host__ __device__ inline size_t producer_smem(int threads) {
   return (size_t)(threads / 16) * 16 * 17 * sizeof(unsigned long long) + 32 * sizeof(float);
 }
 
@@ -140,6 +140,183 @@ H3_DEV void load_activation2(const void* x, int64_t row, int64_t width, int64_t 
   }
 #pragma unroll
   for (int j = 0; j < 16; ++j) p[j] = pk2(a[j], b[j]);
+}
+
+// ---------------------------------------------------------------------------
+// Row staging (the persistent producers).  A CTA keeps ROW_STAGES rows of its input in
+// flight: each row is copied global -> shared memory by TMA (cp.async.bulk.tensor,
+// boxes of 128-byte lines with the 128-byte swizzle, completing on the stage's
+// mbarrier) while the CTA rotates and quantises an earlier row.  With the swizzle,
+// 16-byte chunk c of line l sits at chunk position c ^ (l & 7) of the line, so the
+// 16-byte reads of the lanes' 32- or 64-byte blocks fall on eight different bank
+// groups in every quarter warp.  The copies read this GPU's own memory (no multicast).
+// ---------------------------------------------------------------------------
+constexpr int ROW_STAGES = 2;
+constexpr unsigned long long STAGE_TIMEOUT_NS = 2000000000ull;
+
+struct RowStage {
+  int row_bytes;    // bytes of one input row (a multiple of 128)
+  int stage_bytes;  // row_bytes rounded up to 1024
+  int box_lines;    // 128-byte lines per TMA box (<= 256, divides row_bytes / 128)
+  int boxes;        // boxes per row
+  int* err;
+};
+
+H3_DEV uint32_t stage_su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// Thread 0: the copy of `row` into one stage, completing on its barrier.
+H3_DEV void stage_issue(const CUtensorMap* map, const RowStage& st, uint8_t* buf, uint64_t* bar,
+                        int64_t row) {
+  const uint32_t b = stage_su32(bar);
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(b),
+               "r"((uint32_t)st.row_bytes)
+               : "memory");
+  for (int k = 0; k < st.boxes; ++k)
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(stage_su32(buf + k * st.box_lines * 128)),
+        "l"(map), "r"(0), "r"(k * st.box_lines), "r"((int)row), "r"(b)
+        : "memory");
+}
+
+// Bounded wait for a stage's copy (2 s of %globaltimer).
+H3_DEV bool stage_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t b = stage_su32(bar);
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(b), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    uint64_t now;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+    if (it == 0)
+      t0 = now;
+    else if (now - t0 > STAGE_TIMEOUT_NS)
+      return false;
+  }
+}
+
+// The 16-byte chunk at byte `off` of a staged (swizzled) row.
+H3_DEV uint4 stage_chunk(const uint8_t* stage, int64_t off) {
+  const int64_t line = off >> 7;
+  const int c = (int)((off >> 4) & 7) ^ (int)(line & 7);
+  return *reinterpret_cast<const uint4*>(stage + (line << 7) + (c << 4));
+}
+
+H3_DEV void stage_half16(const uint8_t* stage, int64_t off, float (&v)[16]) {
+  const uint4 u[2] = {stage_chunk(stage, off), stage_chunk(stage, off + 16)};
+  const __half2* h = reinterpret_cast<const __half2*>(u);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float2 f = __half22float2(h[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+}
+
+H3_DEV void stage_float16(const uint8_t* stage, int64_t off, float (&v)[16]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint4 u = stage_chunk(stage, off + 16 * j);
+    v[4 * j] = __uint_as_float(u.x);
+    v[4 * j + 1] = __uint_as_float(u.y);
+    v[4 * j + 2] = __uint_as_float(u.z);
+    v[4 * j + 3] = __uint_as_float(u.w);
+  }
+}
+
+// load_activation2 from a staged row (byte offsets of the row as laid out in HBM).
+template <int KIND>
+H3_DEV void stage_activation2(const uint8_t* stage, int64_t width, int64_t blk0, int64_t blk1,
+                              bool ok0, bool ok1, f32x2 (&p)[16]) {
+  float a[16], b[16];
+  if (KIND == H3_IN_GATEUP_F16) {
+    float g0[16], g1[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) g0[j] = g1[j] = a[j] = b[j] = 0.0f;
+    if (ok0) {
+      stage_half16(stage, blk0 * 32, g0);
+      stage_half16(stage, 2 * width + blk0 * 32, a);
+    }
+    if (ok1) {
+      stage_half16(stage, blk1 * 32, g1);
+      stage_half16(stage, 2 * width + blk1 * 32, b);
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) p[j] = pk2(swiglu_f32(g0[j], a[j]), swiglu_f32(g1[j], b[j]));
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) a[j] = b[j] = 0.0f;
+  if (KIND == H3_IN_ACT_F32) {
+    if (ok0) stage_float16(stage, blk0 * 64, a);
+    if (ok1) stage_float16(stage, blk1 * 64, b);
+  } else {
+    if (ok0) stage_half16(stage, blk0 * 32, a);
+    if (ok1) stage_half16(stage, blk1 * 32, b);
+  }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) p[j] = pk2(a[j], b[j]);
+}
+
+// Shared memory of a staged producer CTA: the 1024-aligned stages, then the rotation
+// tiles and reduction buffer of producer_smem, then the stage barriers.
+static size_t staged_smem(int threads, const RowStage& st) {
+  return 1024 + (size_t)ROW_STAGES * st.stage_bytes + producer_smem(threads) + ROW_STAGES * 8;
+}
+
+
+// The staged prologue: barriers initialised and the CTA's first ROW_STAGES rows in
+// flight.  Returns the stage area; *bars_out receives the barriers.
+H3_DEV uint8_t* stage_begin(uint8_t* smem_raw, const CUtensorMap* map, const RowStage& st,
+                            int64_t rows, uint8_t*& rest, uint64_t*& bars) {
+  uint8_t* stages = smem_raw + ((1024u - (stage_su32(smem_raw) & 1023u)) & 1023u);
+  rest = stages + ROW_STAGES * st.stage_bytes;
+  bars = reinterpret_cast<uint64_t*>(rest + producer_smem(blockDim.x));
+  if (threadIdx.x == 0) {
+    for (int k = 0; k < ROW_STAGES; ++k)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(stage_su32(bars + k)) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int k = 0; k < ROW_STAGES; ++k) {
+      const int64_t r = blockIdx.x + (int64_t)k * gridDim.x;
+      if (r < rows) stage_issue(map, st, stages + k * st.stage_bytes, bars + k, r);
+    }
+  }
+  __syncthreads();
+  return stages;
+}
+
+// Waits for the stage of loop iteration `it` (row `row`).  On a timeout (which would
+// mean the copy engine failed) every thread learns it together; thread 0 records
+// H3_ERR_TIMEOUT and waits, bounded, for the copies still in flight, and the caller
+// returns.
+H3_DEV bool stage_ready(const RowStage& st, uint64_t* bars, int it, int64_t row, int64_t rows) {
+  const bool ok = stage_wait(bars + it % ROW_STAGES, (uint32_t)(it / ROW_STAGES) & 1u);
+  if (!__syncthreads_or(!ok)) return true;
+  if (threadIdx.x == 0) {
+    report_error(st.err, H3_ERR_TIMEOUT);
+    for (int k = 0; k < ROW_STAGES; ++k) {
+      const int j = it + k;
+      if (row + (int64_t)k * gridDim.x < rows)
+        stage_wait(bars + j % ROW_STAGES, (uint32_t)(j / ROW_STAGES) & 1u);
+    }
+  }
+  return false;
+}
+
+// After every lane has read the stage of iteration `it`: refill it with the row
+// ROW_STAGES iterations ahead.
+H3_DEV void stage_next(const CUtensorMap* map, const RowStage& st, uint8_t* stages,
+                       uint64_t* bars, int it, int64_t row, int64_t rows) {
+  __syncthreads();
+  const int64_t next = row + (int64_t)ROW_STAGES * gridDim.x;
+  if (threadIdx.x == 0 && next < rows)
+    stage_issue(map, st, stages + (it % ROW_STAGES) * st.stage_bytes, bars + it % ROW_STAGES, next);
 }
 
 H3_DEV float block_reduce_max(float v, float* red) {
@@ -216,12 +393,18 @@ H3_DEV void quantize_store(const f32x2 (&v)[NP][16], const bool (&ok)[NP][2],
 // FC2 producer.  One CTA per row (grid-stride over rows); each thread owns NB = 2 * NP
 // 16-value blocks, processed as NP packed pairs of blocks that lie in different
 // ConvRot groups (blocks tid + (2p) * T and tid + (2p + 1) * T for T threads).
-template <int KIND, int MODE, int NP>
+template <int KIND, int MODE, int NP, bool STAGED>
 __global__ void __launch_bounds__(512) swiglu_rotate_kernel(
     const void* __restrict__ x, int64_t rows, int64_t width, float* __restrict__ rotated,
     float* __restrict__ row_max, const float* __restrict__ row_max_in, int division,
-    int8_t* __restrict__ q, float* __restrict__ scale_out) {
-  extern __shared__ f32x2 smem2[];
+    int8_t* __restrict__ q, float* __restrict__ scale_out, const __grid_constant__ CUtensorMap map,
+    const RowStage st) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* rest = smem_raw;
+  uint8_t* stages = nullptr;
+  uint64_t* bars = nullptr;
+  if (STAGED) stages = stage_begin(smem_raw, &map, st, rows, rest, bars);
+  f32x2* smem2 = reinterpret_cast<f32x2*>(rest);
   const int tid = threadIdx.x;
   const int half = tid >> 4, b = tid & 15;
   f32x2* tile = smem2 + half * (16 * 17);
@@ -237,12 +420,22 @@ __global__ void __launch_bounds__(512) swiglu_rotate_kernel(
       ok[p][e] = blk[p][e] < blocks;  // uniform across each half warp
     }
 
-  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+  int it = 0;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x, ++it) {
     f32x2 v[NP][16];
+    if (STAGED) {
+      if (!stage_ready(st, bars, it, row, rows)) return;
+      const uint8_t* stg = stages + (it % ROW_STAGES) * st.stage_bytes;
+#pragma unroll
+      for (int p = 0; p < NP; ++p)
+        stage_activation2<KIND>(stg, width, blk[p][0], blk[p][1], ok[p][0], ok[p][1], v[p]);
+      stage_next(&map, st, stages, bars, it, row, rows);
+    }
     float m_nan = 0.0f;
 #pragma unroll
     for (int p = 0; p < NP; ++p) {
-      load_activation2<KIND>(x, row, width, blk[p][0], blk[p][1], ok[p][0], ok[p][1], v[p]);
+      if (!STAGED)
+        load_activation2<KIND>(x, row, width, blk[p][0], blk[p][1], ok[p][0], ok[p][1], v[p]);
       convrot256_halfwarp2(v[p], tile, b);
       // invalid blocks rotate zeros, which leave the maximum unchanged
 #pragma unroll
@@ -464,11 +657,17 @@ H3_DEV void modulated_norm_pairs(f32x2 (&v)[NP][16], const int64_t (&blk)[NP][2]
 // (NORM), optional ConvRot256 with an fp16 rounding of the rotated value, then the row
 // quantiser.  One CTA per row, packed pairs of blocks as in swiglu_rotate_kernel.
 // QUANT = false stops after the norm (its fp16 output only).
-template <int NP, bool ROTATE, bool NORM, bool QUANT>
+template <int NP, bool ROTATE, bool NORM, bool QUANT, bool STAGED>
 __global__ void __launch_bounds__(512) column_quantize_kernel(
     const __half* __restrict__ x, int64_t rows, int64_t k, int8_t* __restrict__ q,
-    float* __restrict__ scale_out, const NormArgs na) {
-  extern __shared__ f32x2 smem2[];
+    float* __restrict__ scale_out, const NormArgs na, const __grid_constant__ CUtensorMap map,
+    const RowStage st) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* rest = smem_raw;
+  uint8_t* stages = nullptr;
+  uint64_t* bars = nullptr;
+  if (STAGED) stages = stage_begin(smem_raw, &map, st, rows, rest, bars);
+  f32x2* smem2 = reinterpret_cast<f32x2*>(rest);
   const int tid = threadIdx.x;
   const int half = tid >> 4, b = tid & 15;
   f32x2* tile = smem2 + half * (16 * 17);
@@ -483,11 +682,21 @@ __global__ void __launch_bounds__(512) column_quantize_kernel(
       blk[p][e] = tid + (int64_t)(2 * p + e) * blockDim.x;
       ok[p][e] = blk[p][e] < blocks;
     }
-  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+  int it = 0;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x, ++it) {
     f32x2 v[NP][16];
+    if (STAGED) {
+      if (!stage_ready(st, bars, it, row, rows)) return;
+      const uint8_t* stg = stages + (it % ROW_STAGES) * st.stage_bytes;
 #pragma unroll
-    for (int p = 0; p < NP; ++p)
-      load_activation2<H3_IN_ACT_F16>(x, row, k, blk[p][0], blk[p][1], ok[p][0], ok[p][1], v[p]);
+      for (int p = 0; p < NP; ++p)
+        stage_activation2<H3_IN_ACT_F16>(stg, k, blk[p][0], blk[p][1], ok[p][0], ok[p][1], v[p]);
+      stage_next(&map, st, stages, bars, it, row, rows);
+    } else {
+#pragma unroll
+      for (int p = 0; p < NP; ++p)
+        load_activation2<H3_IN_ACT_F16>(x, row, k, blk[p][0], blk[p][1], ok[p][0], ok[p][1], v[p]);
+    }
     if (NORM) modulated_norm_pairs<NP>(v, blk, ok, row, k, na, red);
     if (!QUANT) continue;
     float m_nan = 0.0f;
@@ -581,16 +790,79 @@ static bool allow_smem(K kernel, size_t smem, bool& done) {
   return true;
 }
 
+// Whether the producers stage their rows through TMA (default) or load them straight
+// into registers: H3_ROW_STAGING=0 in the environment selects the latter, for
+// comparisons; both give the same bits.
+static bool row_staging_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("H3_ROW_STAGING");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return on;
+}
+
+// Row staging geometry and tensor map for `rows` rows of `row_bytes` bytes at x; false
+// when the rows cannot be staged (then the kernels load straight from HBM).
+static bool plan_row_stage(const void* x, int64_t rows, int64_t row_bytes, int threads,
+                           CUtensorMap* map, RowStage* st) {
+  if (!row_staging_enabled() || rows <= 0 || rows >= ((int64_t)1 << 31) || row_bytes % 128)
+    return false;
+  const int64_t lines = row_bytes / 128;
+  const int box = lines <= 256 ? (int)lines : 256;
+  if (lines % box) return false;
+  st->row_bytes = (int)row_bytes;
+  st->stage_bytes = (int)((row_bytes + 1023) / 1024 * 1024);
+  st->box_lines = box;
+  st->boxes = (int)(lines / box);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  st->err = h3host::error_word(dev);
+  if (st->err == nullptr || staged_smem(threads, *st) > 227 * 1024) return false;
+  return h3host::encode_row_map(map, x, rows, row_bytes, box);
+}
+
+// A persistent grid for a staged kernel: resident CTAs per SM times the SMs, at most one
+// CTA per row.
+template <typename K>
+static int staged_grid(K kernel, int threads, size_t smem, int64_t rows) {
+  int per_sm = 0, dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) !=
+          cudaSuccess ||
+      per_sm < 1)
+    return 0;
+  return (int)std::min<int64_t>(rows, (int64_t)per_sm * h3host::sm_count(dev));
+}
+
+// Bytes of one producer input row as it lies in HBM.
+static int64_t producer_row_bytes(int kind, int64_t width) {
+  return kind == H3_IN_GATEUP_F16 ? 4 * width : kind == H3_IN_ACT_F32 ? 4 * width : 2 * width;
+}
+
 template <int KIND, int MODE, int NP>
 static int launch_producer_np(const void* x, int64_t rows, int64_t width, float* rotated,
                               float* row_max, const float* row_max_in, int division, int8_t* q,
                               float* scale, int threads, cudaStream_t stream) {
+  CUtensorMap map;
+  RowStage st{};
+  if (plan_row_stage(x, rows, producer_row_bytes(KIND, width), threads, &map, &st)) {
+    static bool smem_set = false;
+    const size_t smem = staged_smem(threads, st);
+    if (!allow_smem(swiglu_rotate_kernel<KIND, MODE, NP, true>, smem, smem_set)) return H3_ERR_CUDA;
+    const int grid = staged_grid(swiglu_rotate_kernel<KIND, MODE, NP, true>, threads, smem, rows);
+    if (grid > 0) {
+      swiglu_rotate_kernel<KIND, MODE, NP, true><<<grid, threads, smem, stream>>>(
+          x, rows, width, rotated, row_max, row_max_in, division, q, scale, map, st);
+      return h3host::check_launch();
+    }
+  }
   static bool smem_set = false;
   const size_t smem = producer_smem(threads);
-  if (!allow_smem(swiglu_rotate_kernel<KIND, MODE, NP>, smem, smem_set)) return H3_ERR_CUDA;
+  if (!allow_smem(swiglu_rotate_kernel<KIND, MODE, NP, false>, smem, smem_set)) return H3_ERR_CUDA;
   const int grid = (int)std::min<int64_t>(rows, 1 << 20);
-  swiglu_rotate_kernel<KIND, MODE, NP><<<grid, threads, smem, stream>>>(
-      x, rows, width, rotated, row_max, row_max_in, division, q, scale);
+  memset(&map, 0, sizeof(map));
+  swiglu_rotate_kernel<KIND, MODE, NP, false><<<grid, threads, smem, stream>>>(
+      x, rows, width, rotated, row_max, row_max_in, division, q, scale, map, RowStage{});
   return h3host::check_launch();
 }
 
@@ -769,14 +1041,29 @@ extern "C" int h3_column_quantize(const void* x_f16, int64_t rows, int64_t k, in
   const int grid = (int)std::min<int64_t>(rows, 1 << 20);
   cudaStream_t st = (cudaStream_t)stream;
   const __half* xh = reinterpret_cast<const __half*>(x_f16);
-  static bool smem_set[2][2] = {{false, false}, {false, false}};
+  static bool smem_set[2][2][2] = {};
+  CUtensorMap map;
+  RowStage rs{};
+  const bool staged = plan_row_stage(x_f16, rows, 2 * k, t.threads, &map, &rs);
+  if (!staged) memset(&map, 0, sizeof(map));
 #define H3_COLQ(NPV, ROT)                                                                  \
   do {                                                                                     \
-    if (!allow_smem(column_quantize_kernel<NPV, ROT, false, true>, smem,                   \
-                    smem_set[NPV - 1][ROT]))                                               \
+    if (staged) {                                                                          \
+      auto kern = column_quantize_kernel<NPV, ROT, false, true, true>;                     \
+      const size_t ssm = staged_smem(t.threads, rs);                                       \
+      if (!allow_smem(kern, ssm, smem_set[NPV - 1][ROT][1])) return H3_ERR_CUDA;           \
+      const int g = staged_grid(kern, t.threads, ssm, rows);                               \
+      if (g > 0) {                                                                         \
+        kern<<<g, t.threads, ssm, st>>>(xh, rows, k, q, scale, NormArgs{}, map, rs);       \
+        break;                                                                             \
+      }                                                                                    \
+      memset(&map, 0, sizeof(map));                                                        \
+    }                                                                                      \
+    if (!allow_smem(column_quantize_kernel<NPV, ROT, false, true, false>, smem,            \
+                    smem_set[NPV - 1][ROT][0]))                                            \
       return H3_ERR_CUDA;                                                                  \
-    column_quantize_kernel<NPV, ROT, false, true>                                          \
-        <<<grid, t.threads, smem, st>>>(xh, rows, k, q, scale, NormArgs{});                \
+    column_quantize_kernel<NPV, ROT, false, true, false>                                   \
+        <<<grid, t.threads, smem, st>>>(xh, rows, k, q, scale, NormArgs{}, map, RowStage{}); \
   } while (0)
   if (t.nb == 1) {
     if (convrot) H3_COLQ(1, true); else H3_COLQ(1, false);
@@ -873,14 +1160,29 @@ extern "C" int h3_modulated_norm_quantize(const void* x_f16, int64_t rows, int64
   const int grid = (int)std::min<int64_t>(rows, 1 << 20);
   cudaStream_t st = (cudaStream_t)stream;
   const __half* xh = reinterpret_cast<const __half*>(x_f16);
-  static bool smem_set[2][3] = {{false, false, false}, {false, false, false}};
+  static bool smem_set[2][3][2] = {};
+  CUtensorMap map;
+  RowStage rs{};
+  const bool staged = plan_row_stage(x_f16, rows, 2 * width, t.threads, &map, &rs);
+  if (!staged) memset(&map, 0, sizeof(map));
 #define H3_NORMQ(NPV, ROT, QU, SLOT)                                                       \
   do {                                                                                     \
-    if (!allow_smem(column_quantize_kernel<NPV, ROT, true, QU>, smem,                      \
-                    smem_set[NPV - 1][SLOT]))                                              \
+    if (staged) {                                                                          \
+      auto kern = column_quantize_kernel<NPV, ROT, true, QU, true>;                        \
+      const size_t ssm = staged_smem(t.threads, rs);                                       \
+      if (!allow_smem(kern, ssm, smem_set[NPV - 1][SLOT][1])) return H3_ERR_CUDA;          \
+      const int g = staged_grid(kern, t.threads, ssm, rows);                               \
+      if (g > 0) {                                                                         \
+        kern<<<g, t.threads, ssm, st>>>(xh, rows, width, q, row_scale, na, map, rs);       \
+        break;                                                                             \
+      }                                                                                    \
+      memset(&map, 0, sizeof(map));                                                        \
+    }                                                                                      \
+    if (!allow_smem(column_quantize_kernel<NPV, ROT, true, QU, false>, smem,               \
+                    smem_set[NPV - 1][SLOT][0]))                                           \
       return H3_ERR_CUDA;                                                                  \
-    column_quantize_kernel<NPV, ROT, true, QU>                                             \
-        <<<grid, t.threads, smem, st>>>(xh, rows, width, q, row_scale, na);                \
+    column_quantize_kernel<NPV, ROT, true, QU, false>                                      \
+        <<<grid, t.threads, smem, st>>>(xh, rows, width, q, row_scale, na, map, RowStage{}); \
   } while (0)
   if (t.nb == 1) {
     if (!quant) H3_NORMQ(1, false, false, 0);
