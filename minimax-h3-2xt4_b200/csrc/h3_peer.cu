@@ -55,7 +55,10 @@ namespace peer {
 constexpr int MAX_WORLD = 8;
 constexpr int64_t READY = 0, DONE = 256, COUNTER = 512;
 constexpr unsigned long long TIMEOUT_NS = 2000000000ull;
-constexpr int THREADS = 256;
+// 128 threads a CTA: with up to 64 registers a thread, one CTA fits on an SM beside a
+// GEMM CTA (576 threads, <= 96 registers), so a reduce issued on another stream runs
+// while the tensor cores work (the pipelined TP forward relies on it).
+constexpr int THREADS = 128;
 
 struct Args {
   uint64_t bases[MAX_WORLD];
@@ -409,7 +412,7 @@ int run(const void* const* bases, const void* mc, int world, int rank, int64_t f
   const int64_t items = (gather ? rows - (a.row_end - a.row_begin) : a.row_end - a.row_begin) *
                         (width / 8);
   const int blocks = (int)std::max<int64_t>(
-      1, std::min<int64_t>((items + THREADS - 1) / THREADS, (int64_t)h3host::sm_count(dev) * 8));
+      1, std::min<int64_t>((items + THREADS - 1) / THREADS, (int64_t)h3host::sm_count(dev) * 16));
   cudaStream_t st = (cudaStream_t)stream;
   cudaError_t e = world == 2 ? launch<2>(a, blocks, gather, payload, st)
                   : world == 4 ? launch<4>(a, blocks, gather, payload, st)
