@@ -976,7 +976,7 @@ def run_sweep(args):
         from h3tp import ops
         M = 32768
         hbm = peaks()["hbm_gbs"]
-        staging = os.environ.get("H3_ROW_STAGING", "1") != "0"
+        staging = os.environ.get("H3_ROW_STAGING", "0") == "1"
         for K in (3072, 5120):
             hq = torch.randn((M, K), generator=g, device=dev).half()
             ms = timed(lambda: ops.column_quantize(hq, True))
