@@ -152,6 +152,44 @@ def test_peer_wait_gives_up_with_timeout_status(cuda_device):
     assert _native.device_error(dev.index or 0) == 0  # reading clears it
 
 
+def test_recorded_failure_reaches_the_next_forward_without_a_sync(cuda_device):
+    """A bounded wait that gives up (rank 1 never signals) records H3_ERR_TIMEOUT in
+    the host-mapped error word: h3_device_error_peek sees it without synchronising or
+    clearing, the next module forward on that GPU raises H3Error, and once
+    h3_device_error has read and cleared the word the forward runs again."""
+    import time
+    from h3tp import _native, ops
+    from h3tp.tp_dit import ColumnParallelLinearINT8
+    dev = cuda_device
+    idx = dev.index or 0
+    rows, width = 16, 256
+    bufs, roff, foff = _buffers(dev, 2, rows, width)
+    bases = [b.data_ptr() for b in bufs]
+    res = torch.zeros((rows, width), dtype=torch.float16, device=dev)
+    A = torch.ones(rows, dtype=torch.float32, device=dev)
+    S = torch.ones(width, dtype=torch.float32, device=dev)
+    assert _native.device_error(idx) == 0
+    assert _native.device_error_peek(idx) == 0
+    ops.peer_reduce(bases, 2, 0, 0, roff, foff, rows, width, 0, A, S, res, None, None, 1)
+    deadline = time.time() + 30
+    while _native.device_error_peek(idx) == 0 and time.time() < deadline:
+        time.sleep(0.05)  # the word is read from host memory while the kernel waits
+    assert _native.device_error_peek(idx) == _native.H3_ERR_TIMEOUT
+    mod = ColumnParallelLinearINT8(256, 256, 0, 1, device=dev)
+    mod.weight.data.fill_(1)
+    mod.weight_scale.data.fill_(1e-3)
+    x = torch.ones((4, 256), dtype=torch.float16, device=dev)
+    with pytest.raises(_native.H3Error):
+        with torch.no_grad():
+            mod(x)
+    assert _native.device_error(idx) == _native.H3_ERR_TIMEOUT  # synchronises, clears
+    assert _native.device_error_peek(idx) == 0
+    with torch.no_grad():
+        y = mod(x)
+    torch.cuda.synchronize()
+    assert torch.isfinite(y.float()).all()
+
+
 def test_peer_rejects_bad_geometry(cuda_device):
     from h3tp import ops
     dev = cuda_device
