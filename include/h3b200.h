@@ -315,7 +315,7 @@ int h3_peer_gather(const void* const* bases, int world, int rank, int64_t flags_
  * states for concurrent communicators.  Waits are bounded (2 s per CTA in total); a
  * wait that gives up uses the local maximum and leaves H3_ERR_TIMEOUT in
  * h3_device_error.  row_max (optional) receives the global maxima.  width up to
- * H3_PEER_PRODUCER_MAX_WIDTH (two rows of one CTA are staged in shared memory). */
+ * H3_PEER_PRODUCER_MAX_WIDTH (a row of each CTA is staged in shared memory). */
 #define H3_PEER_PRODUCER_MAX_WIDTH 16384
 int h3_swiglu_rotate_quantize_peer(const void* x, int input_kind, int64_t rows,
                                    int64_t width, const void* const* bases, int world,

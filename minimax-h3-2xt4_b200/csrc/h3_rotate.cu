@@ -473,11 +473,12 @@ __global__ void __launch_bounds__(512) swiglu_rotate_kernel(
 }
 
 // FC2 producer at TP>1 in one pass.  The row loop is pipelined by one row: a CTA
-// rotates row i, publishes its local maximum to every rank, stashes the rotated values
-// in shared memory, and only then waits for the global maximum of its previous row and
-// quantises that row from the stash, so the NVLink round trip of a maximum overlaps
-// the next row's loads and rotation.  Each thread reads back only what it stashed, so
-// the stash needs no barrier; two stash buffers alternate between rows.  Launched as a
+// rotates row i into registers and publishes its local maximum to every rank, then
+// waits for the global maximum of its previous row, quantises that row from the shared-
+// memory stash, and only then moves row i from its registers into the stash, so the
+// NVLink round trip of a maximum overlaps the next row's loads and rotation.  Each
+// thread reads back only what it stashed, and reads row i-1 before it overwrites it
+// with row i, so one stash buffer suffices and needs no barrier.  Launched as a
 // persistent grid (every CTA resident), so a CTA waiting for a peer's row never waits
 // for a CTA that cannot run.
 template <int KIND, int NP>
@@ -490,7 +491,7 @@ __global__ void __launch_bounds__(512) swiglu_rotate_peer_kernel(
   const int half = tid >> 4, b = tid & 15;
   f32x2* tile = smem2 + half * (16 * 17);
   float* red = reinterpret_cast<float*>(smem2 + (T / 16) * (16 * 17));
-  f32x2* stash = reinterpret_cast<f32x2*>(red + 32);  // [2][NP * 16][T]
+  f32x2* stash = reinterpret_cast<f32x2*>(red + 32);  // [NP * 16][T]
   const int64_t blocks = width / 16;
   int64_t blk[NP][2];
   bool ok[NP][2];
@@ -505,14 +506,13 @@ __global__ void __launch_bounds__(512) swiglu_rotate_peer_kernel(
   int64_t prev = -1;
   bool prev_finite = false;
   float prev_local = 0.0f;
-  int buf = 0;
 
   for (int64_t row = blockIdx.x;; row += gridDim.x) {
     const bool have = row < rows;
     bool finite = false;
     float m = 0.0f;
+    f32x2 v[NP][16];
     if (have) {
-      f32x2 v[NP][16];
       float m_nan = 0.0f;
 #pragma unroll
       for (int p = 0; p < NP; ++p) {
@@ -525,11 +525,6 @@ __global__ void __launch_bounds__(512) swiglu_rotate_peer_kernel(
       finite = m < __uint_as_float(0x7f800000u);  // false for +inf and NaN
       if (!finite) m = block_reduce_max(local_max_ignoring_nan<NP>(v, ok), red);
       peer_publish(pm, row, m);
-      f32x2* st = stash + (size_t)buf * NP * 16 * T;
-#pragma unroll
-      for (int p = 0; p < NP; ++p)
-#pragma unroll
-        for (int i = 0; i < 16; ++i) st[(p * 16 + i) * T + tid] = v[p][i];
     }
     if (prev >= 0) {
       const float g = peer_wait(pm, prev, prev_local, red, deadline);
@@ -538,12 +533,11 @@ __global__ void __launch_bounds__(512) swiglu_rotate_peer_kernel(
       const bool fin = prev_finite && g < __uint_as_float(0x7f800000u);
       const float scale = row_scale_from_max(g);
       const float inv = __fdiv_rn(1.0f, scale);
-      const f32x2* st = stash + (size_t)(buf ^ 1) * NP * 16 * T;
       f32x2 w[NP][16];
 #pragma unroll
       for (int p = 0; p < NP; ++p)
 #pragma unroll
-        for (int i = 0; i < 16; ++i) w[p][i] = st[(p * 16 + i) * T + tid];
+        for (int i = 0; i < 16; ++i) w[p][i] = stash[(p * 16 + i) * T + tid];
       quantize_store<NP>(w, ok, blk, fin, scale, inv, division, q + prev * width);
       if (tid == 0) {
         scale_out[prev] = scale;
@@ -551,10 +545,14 @@ __global__ void __launch_bounds__(512) swiglu_rotate_peer_kernel(
       }
     }
     if (!have) break;
+    // row i-1 is read (above, by this same thread): row i takes its place
+#pragma unroll
+    for (int p = 0; p < NP; ++p)
+#pragma unroll
+      for (int i = 0; i < 16; ++i) stash[(p * 16 + i) * T + tid] = v[p][i];
     prev = row;
     prev_finite = finite;
     prev_local = m;
-    buf ^= 1;
   }
 }
 
@@ -902,9 +900,9 @@ static int dispatch_kind(int kind, const void* x, int64_t rows, int64_t width, f
   }
 }
 
-// The peer producer's shared memory: the producer's plus two stashes of one row.
+// The peer producer's shared memory: the producer's plus the stash of one row.
 static size_t peer_producer_smem(int threads, int np) {
-  return producer_smem(threads) + 2 * (size_t)np * 16 * threads * sizeof(unsigned long long);
+  return producer_smem(threads) + (size_t)np * 16 * threads * sizeof(unsigned long long);
 }
 
 template <int KIND, int NP>
