@@ -62,6 +62,10 @@ def parse():
                     help="BASELINE config 5 shape sweep on one GPU: one JSON line per point")
     ap.add_argument("--sweep-producers", action="store_true",
                     help="only the activation-producer lines of the sweep")
+    ap.add_argument("--sweep-only", default="",
+                    help="comma-separated producer lines to run (column_quantize, "
+                         "fc2_producer_tp1, fc2_producer_tp1_gateup, norm_producer, "
+                         "fc2_producer_tp); all when empty")
     ap.add_argument("--fc1-epilogue", choices=["swiglu", "fp16"], default="swiglu",
                     help="FC1 writes the FP32 SwiGLU activation, or fp16 [gate|up] with the "
                          "SwiGLU applied in the FC2 producer (the reference's form)")
@@ -974,10 +978,15 @@ def run_sweep(args):
         # quantiser of FC1's input and the TP1 FC2 producer (SwiGLU output -> ConvRot ->
         # row maximum -> codes in one pass)
         from h3tp import ops
-        M = 32768
+        M = args.tokens
         hbm = peaks()["hbm_gbs"]
         staging = os.environ.get("H3_ROW_STAGING", "0") == "1"
-        for K in (3072, 5120):
+        only = set(filter(None, args.sweep_only.split(",")))
+
+        def sizes(line, values):
+            return values if not only or line in only else ()
+
+        for K in sizes("column_quantize", (3072, 5120)):
             hq = torch.randn((M, K), generator=g, device=dev).half()
             ms = timed(lambda: ops.column_quantize(hq, True))
             nbytes = M * K * 2 + M * K + 4 * M
@@ -986,7 +995,7 @@ def run_sweep(args):
                               "frac_of_hbm": round(nbytes / (ms * 1e-3) / 1e9 / hbm, 4),
                               "row_staging": staging}), flush=True)
             del hq
-        for kl in (8192, 4096):
+        for kl in sizes("fc2_producer_tp1", (8192, 4096)):
             act = torch.randn((M, kl), generator=g, device=dev) * 0.7
             ms = timed(lambda: ops.swiglu_rotate_quantize_local(act, "act_f32"))
             nbytes = M * kl * 4 + M * kl + 8 * M
@@ -995,9 +1004,21 @@ def run_sweep(args):
                               "frac_of_hbm": round(nbytes / (ms * 1e-3) / 1e9 / hbm, 4),
                               "row_staging": staging}), flush=True)
             del act
+        # the same with the reference's default FC1 output: fp16 [gate | up], the FP32
+        # SwiGLU computed in the producer
+        for kl in sizes("fc2_producer_tp1_gateup", (8192, 4096)):
+            gu = torch.randn((M, 2 * kl), generator=g, device=dev).half()
+            ms = timed(lambda: ops.swiglu_rotate_quantize_local(gu, "gateup_f16"))
+            nbytes = M * 2 * kl * 2 + M * kl + 8 * M
+            print(json.dumps({"sweep": "fc2_producer_tp1_gateup", "M": M, "Kl": kl,
+                              "ms": round(ms, 4),
+                              "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                              "frac_of_hbm": round(nbytes / (ms * 1e-3) / 1e9 / hbm, 4),
+                              "row_staging": staging}), flush=True)
+            del gu
         # row 2 of the scope table: the column input producer, fused modulated RMSNorm ->
         # ConvRot -> quant, against the unfused route (norm -> fp16 h -> quantiser)
-        for K in (3072, 5120, 5376):
+        for K in sizes("norm_producer", (3072, 5120, 5376)):
             x = torch.randn((M, K), generator=g, device=dev).half()
             w = torch.rand((K,), generator=g, device=dev) + 0.5
             sh = torch.randn((3, K), generator=g, device=dev) * 0.1
@@ -1021,7 +1042,7 @@ def run_sweep(args):
         # in-kernel row-maximum exchange against the two passes of the NCCL route (the
         # MAX all-reduce between them not included) and the TP1 single pass, one GPU
         # emulating `world` ranks whose slots are all published before the launch.
-        for world in (2, 4, 8):
+        for world in sizes("fc2_producer_tp", (2, 4, 8)):
             kl = 8192 // world
             act = torch.randn((M, kl), generator=g, device=dev) * 0.7
             _, mx = ops.swiglu_rotate_max(act, "act_f32", store=False)

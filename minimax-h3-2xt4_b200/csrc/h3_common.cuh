@@ -250,9 +250,12 @@ H3_DEV f32x2 silu_fast2(float g0, float g1) {
   return pk2(silu_fix(g0, lo2(den), lo2(q0), lo2(q)), silu_fix(g1, hi2(den), hi2(q0), hi2(q)));
 }
 
-// swiglu_f32 of two (gate, up) pairs
+// swiglu_f32 of two (gate, up) pairs.  The final products are the scalar __fmul_rn,
+// which is never contracted: a caller may add the result (the ConvRot butterfly does),
+// and a mul.rn.f32x2 feeding an add.rn.f32x2 can become a fused multiply-add.
 H3_DEV f32x2 swiglu_f32x2(float g0, float g1, float u0, float u1) {
-  return mul2(silu_fast2(g0, g1), pk2(u0, u1));
+  const f32x2 s = silu_fast2(g0, g1);
+  return pk2(__fmul_rn(lo2(s), u0), __fmul_rn(hi2(s), u1));
 }
 
 // Row scale of the production row quantizer (tilelang_row_quant.py:37-38):

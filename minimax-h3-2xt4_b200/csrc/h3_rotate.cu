@@ -125,8 +125,9 @@ H3_DEV void load_activation2(const void* x, int64_t row, int64_t width, int64_t 
       load_half16_as_float(xr + blk1 * 16, g1);
       load_half16_as_float(xr + width + blk1 * 16, b);
     }
+    // two (gate, up) pairs on packed lanes: the same bits as swiglu_f32 of each
 #pragma unroll
-    for (int j = 0; j < 16; ++j) p[j] = pk2(swiglu_f32(g0[j], a[j]), swiglu_f32(g1[j], b[j]));
+    for (int j = 0; j < 16; ++j) p[j] = swiglu_f32x2(g0[j], g1[j], a[j], b[j]);
     return;
   }
 #pragma unroll
