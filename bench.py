@@ -466,7 +466,11 @@ def run_ours(args):
             ev[3].record(stream)
             sub_events.append(ev)
 
-    chunks = mlp.pipeline_chunks(x, h)
+    with torch.no_grad():  # the forward's own choice under inference
+        chunks = mlp.pipeline_chunks(x, h)
+    nvls_active = False
+    if peer_route and args.transport == "nvls":
+        nvls_active = P.workspace(comm, dev, hidden, M).multicast != 0
     pipe_events = []  # per step: {name: [(start, end) per chunk]}
 
     def step(xres, record=False):
@@ -706,7 +710,8 @@ def run_ours(args):
         "frac_of_int8_peak_per_gpu": round(value / world / peak, 4) if peak else None,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic (seeded N(0,1) input with 1% x20 outlier columns, random int8 weights)",
-        "config": workload_config(args, world),
+        "config": {**workload_config(args, world), "pipeline_chunks": chunks,
+                   **({"nvls_multicast": nvls_active} if args.transport == "nvls" else {})},
         "roofline": {"kernel": ("gemm_i8_pair_kernel<EPI_SWIGLU> (FC1)" if args.fc1_epilogue == "swiglu"
                                else "gemm_i8_pair_kernel<EPI_COLUMN> (FC1)"), "bound": "tensor",
                      "achieved": round(achieved, 2), "peak": peak, "unit": "TOPS",
