@@ -79,8 +79,9 @@ def parse():
     ap.add_argument("--workload", choices=["dit_mlp_block", "dit_linear_block"],
                     default="dit_mlp_block",
                     help="dit_linear_block: BASELINE config 4's whole linear set (QKV, O, FC1, FC2)")
-    ap.add_argument("--chunks", type=int, default=0,
-                    help="TP > 1: row chunks of the pipelined MLP forward (0 = by size, 1 = off)")
+    ap.add_argument("--chunks", type=int, default=1,
+                    help="TP > 1: row chunks of the pipelined MLP forward (1 = off, the policy "
+                         "default; 0 = by size)")
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the sampled-row bit-exactness check after the timed region")
     ap.add_argument("--int8-peak", action="store_true",

@@ -272,33 +272,58 @@ __global__ void __launch_bounds__(THREADS) reduce_kernel(const Args a) {
     const int64_t chunks = a.width >> 3;
     const int64_t total = (a.row_end - a.row_begin) * chunks;
     const int64_t first = a.row_begin * chunks;  // uint4 index of the block's first chunk
+    const int64_t stride = (int64_t)gridDim.x * THREADS;
     uint4* res = reinterpret_cast<uint4*>(a.residual);
-    for (int64_t i = blockIdx.x * (int64_t)THREADS + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * THREADS) {
-      const int64_t e = first + i;  // uint4 index of the chunk in [rows][width]
-      const int64_t r = e / chunks;
-      const int64_t c0 = (e - r * chunks) << 3;
-      int32_t q[8];
-      if (PAYLOAD == FP16_NVLS) {
-        restore_reduced(a, load_reduce_nvls(a.mc, a.partial_off + e * 16), q);
-      } else if (PAYLOAD == INT8_P2P) {
-        load_restore_int8<W>(a, r, c0, q);
-      } else {
-        uint4 u[W];
+    // U chunks per thread and iteration, all their loads issued before any is used: the
+    // NVLink (or switch) round trip is paid once per U chunks.  U keeps the loaded
+    // words within the register budget that lets a CTA sit beside a GEMM CTA.
+    constexpr int U = PAYLOAD == FP16_NVLS ? 4 : (PAYLOAD == FP16_P2P && W == 2) ? 2 : 1;
+    constexpr int L = PAYLOAD == FP16_P2P ? W : 1;  // words loaded per chunk
+    for (int64_t i0 = blockIdx.x * (int64_t)THREADS + threadIdx.x; i0 < total; i0 += stride * U) {
+      uint4 u[U][L], x[U];
 #pragma unroll
-        for (int w = 0; w < W; ++w)
-          u[w] = w == a.rank ? load_received(a.bases[w], a.partial_off + e * 16)
-                             : load_peer(a.bases[w], a.partial_off + e * 16);
-        restore_fp16<W>(a, u, q);
+      for (int k = 0; k < U; ++k) {
+        const int64_t i = i0 + k * stride;
+        if (i >= total || PAYLOAD == INT8_P2P) continue;
+        const int64_t e = first + i;  // uint4 index of the chunk in [rows][width]
+        if (PAYLOAD == FP16_NVLS) {
+          u[k][0] = load_reduce_nvls(a.mc, a.partial_off + e * 16);
+        } else {
+#pragma unroll
+          for (int w = 0; w < L; ++w)
+            u[k][w] = w == a.rank ? load_received(a.bases[w], a.partial_off + e * 16)
+                                  : load_peer(a.bases[w], a.partial_off + e * 16);
+        }
+        x[k] = res[e];
       }
-      const uint4 y = epilogue_chunk(a, q, r, c0, res[e]);
-      res[e] = y;
-      if (PAYLOAD == FP16_NVLS) {
-        store_all_nvls(a.mc, a.final_off + e * 16, y);
-      } else {
 #pragma unroll
-        for (int w = 0; w < W; ++w)
-          if (w != a.rank) reinterpret_cast<uint4*>(a.bases[w] + a.final_off)[e] = y;
+      for (int k = 0; k < U; ++k) {
+        const int64_t i = i0 + k * stride;
+        if (i >= total) break;
+        const int64_t e = first + i;
+        const int64_t r = e / chunks;
+        const int64_t c0 = (e - r * chunks) << 3;
+        int32_t q[8];
+        if (PAYLOAD == FP16_NVLS) {
+          restore_reduced(a, u[k][0], q);
+        } else if (PAYLOAD == INT8_P2P) {
+          load_restore_int8<W>(a, r, c0, q);
+          x[k] = res[e];
+        } else {
+          uint4 uw[W];
+#pragma unroll
+          for (int w = 0; w < W; ++w) uw[w] = u[k][w < L ? w : 0];
+          restore_fp16<W>(a, uw, q);
+        }
+        const uint4 y = epilogue_chunk(a, q, r, c0, x[k]);
+        res[e] = y;
+        if (PAYLOAD == FP16_NVLS) {
+          store_all_nvls(a.mc, a.final_off + e * 16, y);
+        } else {
+#pragma unroll
+          for (int w = 0; w < W; ++w)
+            if (w != a.rank) reinterpret_cast<uint4*>(a.bases[w] + a.final_off)[e] = y;
+        }
       }
     }
   } else if (threadIdx.x == 0) {

@@ -28,8 +28,11 @@ New B200 fields:
                   tilelang_transport_tradeoffs.py:40-88), with any row_transport
   quant_division  'rn' (IEEE, bit-exact with the CPU oracle) or 'fast' (__fdividef)
   mlp_pipeline_chunks  TPDiTMLPINT8 at TP > 1 on the peer transports: row chunks whose
-                  partial-sum exchange overlaps the next chunks' GEMMs (0 = by size:
-                  4 from 16384 rows, 2 from 4096; 1 = off)
+                  partial-sum exchange overlaps the next chunks' GEMMs (1 = off, the
+                  default; 0 = by size: 4 from 16384 rows, 2 from 4096).  Off by
+                  default because it measured slower on B200: the persistent GEMM and
+                  producer grids contend for the SMs (TP2, M = 32768: 1.63 ms a block
+                  unpipelined, 1.77 ms at 2 chunks, 2.05 ms at 4)
   fc1_swiglu_epilogue  off (default): FC1 returns the reference's fp16 [S, 2*ffn/t]
                   [gate|up]; on: FC1 applies the FP32 SwiGLU in its GEMM epilogue and
                   returns fp32 [S, ffn/t] (same bytes, the same FC2 codes).  Turn it on
@@ -66,7 +69,7 @@ class H3OperatorPolicy:
     fc2_max_exchange: str = "peer"
     quant_division: str = "rn"
     fc1_swiglu_epilogue: bool = False
-    mlp_pipeline_chunks: int = 0
+    mlp_pipeline_chunks: int = 1
 
     def __post_init__(self):
         for name in ("dit_fused_gate", "dit_fused_row_gate", "dit_p0_2_lifetime",

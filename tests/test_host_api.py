@@ -206,7 +206,7 @@ def test_pipeline_bounds_tile_the_rows(rows, chunks):
 
 def test_policy_pipeline_chunks_validation():
     from h3tp.h3_operator_policy import H3OperatorPolicy
-    assert H3OperatorPolicy().mlp_pipeline_chunks == 0
+    assert H3OperatorPolicy().mlp_pipeline_chunks == 1
     for bad in (-1, 65, 2.0, True):
         with pytest.raises(ValueError):
             H3OperatorPolicy(mlp_pipeline_chunks=bad)
