@@ -384,6 +384,38 @@ def measure_int8_peak(dev):
     return out
 
 
+def kernel_clock_mhz(dev, fn, probe_ns=8_000_000):
+    """SM clock (MHz) while fn() runs back to back: the library's clock probe (one
+    sleeping 32-thread CTA, which fits beside a GEMM CTA) runs on a second stream from
+    the end of the second launch for probe_ns, and reports SM cycles / elapsed ns.  The
+    nvidia-smi samples of `clocks` are taken every 200 ms, mostly between kernels; this
+    is the clock inside the kernels."""
+    import math
+    import torch
+    from h3tp import ops
+    main = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(device=dev)
+    out = torch.zeros(2, dtype=torch.int64, device=dev)
+    for _ in range(3):
+        fn()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(main)
+    fn()
+    e1.record(main)
+    torch.cuda.synchronize(dev)
+    n = 4 + math.ceil(2.0 * probe_ns * 1e-6 / max(e0.elapsed_time(e1), 1e-3))
+    ev = torch.cuda.Event()
+    for i in range(n):
+        fn()
+        if i == 1:
+            ev.record(main)
+            side.wait_event(ev)
+            ops.sm_clock_probe(out, probe_ns, side)
+    torch.cuda.synchronize(dev)
+    ns, cycles = out.tolist()
+    return round(cycles / ns * 1e3, 1) if ns else None
+
+
 def run_int8_peak(args):
     import torch
     dev = torch.device("cuda", 0)
@@ -664,6 +696,22 @@ def run_ours(args):
 
         # INT8 tensor peak, measured on this GPU now (rank 0; the others wait)
         int8 = measure_int8_peak(dev) if rank == 0 else None
+        # the SM clock inside FC1 and inside cuBLAS's INT8 GEMM at the FC1 shape (rank 0)
+        sm_clock = None
+        if rank == 0:
+            codes1, rs1 = col._prepare_activation(h, True, 256)
+            act1 = torch.empty((M, ffn // world), dtype=torch.float32, device=dev)
+            w1s = mlp.fc1.weight_scale.reshape(-1)
+            sm_clock = {"fc1_gemm_mhz": kernel_clock_mhz(dev, lambda: ops.int8_gemm_swiglu(
+                codes1, mlp.fc1.weight, rs1, w1s, None, torch.float32, out=act1))}
+            del act1
+            qa = torch.randint(-128, 128, (8192, 3072), device=dev, dtype=torch.int8)
+            qb = torch.randint(-127, 128, (16384, 3072), device=dev, dtype=torch.int8)
+            sm_clock["cublas_int8_8192x16384x3072_mhz"] = kernel_clock_mhz(
+                dev, lambda: torch._int_mm(qa, qb.t()))
+            del qa, qb
+            sm_clock["method"] = ("h3_sm_clock_probe beside back-to-back launches: SM cycles / "
+                                  "globaltimer ns over 8 ms")
 
     # Sampled-row bit-exactness of the device step and of the e2e output, checked on
     # every rank by the CPU checker (outside every timed region).
@@ -737,6 +785,7 @@ def run_ours(args):
                               "the wait for the slowest rank's ready flag"}
            if sub_events else {}),
         "device_error": err,
+        **({"sm_clock_in_kernel": sm_clock} if sm_clock else {}),
     }
     if parity is not None:
         line["parity"] = parity

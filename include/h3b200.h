@@ -70,6 +70,11 @@ int h3_device_error(int device, int* code);
  * host can poll it once per operator call at no device cost.  *code = 0 when nothing
  * has failed (or nothing has run yet on that device). */
 int h3_device_error_peek(int device, int* code);
+/* Measurement aid (no reference counterpart): one 32-thread CTA that sleeps for `ns`
+ * nanoseconds (<= 10 s) and writes out[0] = elapsed ns of %globaltimer, out[1] = SM
+ * cycles of %clock64 over the same interval (out: 2 x u64 in device memory).  Launched
+ * on a second stream beside other kernels, out[1] / out[0] is the SM clock they ran at. */
+int h3_sm_clock_probe(unsigned long long ns, unsigned long long* out, void* stream);
 
 /* ----------------------------------------------------------------------------
  * Column path (QKV / FC1): ColumnParallelLinearINT8.forward, tp_dit.py:69-96

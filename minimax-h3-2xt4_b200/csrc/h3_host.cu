@@ -160,3 +160,36 @@ extern "C" int h3_device_error_peek(int device, int* code) {
   *code = w == nullptr ? 0 : *w;
   return H3_OK;
 }
+
+// ---------------------------------------------------------------------------
+// SM clock probe.  One thread that reads %clock64 and %globaltimer, sleeps in 1 us steps
+// until `ns` nanoseconds have passed and reads both again: cycles / time is the SM clock
+// over that interval.  Launched beside other kernels (one 32-thread CTA, no shared
+// memory, so it fits on an SM next to a GEMM CTA) it gives the clock those kernels ran
+// at, which sampled nvidia-smi readings taken between kernels miss.  Bounded by design.
+// ---------------------------------------------------------------------------
+namespace h3host {
+__global__ void clock_probe_kernel(unsigned long long ns, unsigned long long* out) {
+  if (threadIdx.x != 0) return;
+  unsigned long long g0, g;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g0));
+  const long long c0 = clock64();
+  g = g0;
+  while (g - g0 < ns) {
+    __nanosleep(1000);
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g));
+  }
+  const long long c1 = clock64();
+  out[0] = g - g0;
+  out[1] = (unsigned long long)(c1 - c0);
+}
+}  // namespace h3host
+
+extern "C" int h3_sm_clock_probe(unsigned long long ns, unsigned long long* out, void* stream) {
+  if (out == nullptr || ns == 0 || ns > 10000000000ull) return H3_ERR_INVALID;
+  int dev;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(out, &dev)) return s;
+  h3host::clock_probe_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(ns, out);
+  return h3host::check_launch();
+}

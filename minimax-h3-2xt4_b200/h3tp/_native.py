@@ -40,6 +40,7 @@ SIGNATURES = {
     "h3_status_string": [_I],
     "h3_device_error": [_I, _P],
     "h3_device_error_peek": [_I, _P],
+    "h3_sm_clock_probe": [ctypes.c_uint64, _P, _P],
     "h3_column_quantize": [_P, _I64, _I64, _I, _P, _P, _P],
     "h3_int8_gemm_i32": [_P, _P, _I64, _I64, _I64, _P, _P],
     "h3_int8_gemm_column": [_P, _P, _I64, _I64, _I64, _P, _P, _I64, _P, _P, _P],
@@ -120,7 +121,7 @@ def check(status: int, name: str) -> None:
 # Entry points that enqueue exactly one kernel per successful call.
 _LAUNCHING = {n for n in SIGNATURES if n not in (
     "h3_abi_version", "h3_status_string", "h3_device_error", "h3_device_error_peek",
-    "h3_transport_shift", "h3_column_linear_noalloc_error")}
+    "h3_transport_shift", "h3_column_linear_noalloc_error", "h3_sm_clock_probe")}
 _launches = 0
 
 

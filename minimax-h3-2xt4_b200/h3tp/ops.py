@@ -18,6 +18,16 @@ def launch_count() -> int:
     return N.launch_count()
 
 
+def sm_clock_probe(out: torch.Tensor, ns: int, stream: torch.cuda.Stream) -> None:
+    """Enqueues the SM clock probe on `stream`: a 32-thread kernel that sleeps `ns`
+    nanoseconds and writes [elapsed ns, SM cycles] into `out` (int64 [2], on the GPU),
+    so that cycles / ns is the SM clock while other kernels ran beside it."""
+    out = _need(out, torch.int64, "out", 1)
+    if out.numel() != 2:
+        raise ValueError("out must hold 2 int64 values")
+    N.call("h3_sm_clock_probe", int(ns), out.data_ptr(), stream.cuda_stream)
+
+
 def _ptr(t: torch.Tensor | None):
     return None if t is None else t.data_ptr()
 
