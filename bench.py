@@ -485,13 +485,17 @@ def run_ours(args):
         if record:
             ev[0].record(stream)
         shift = T.shift_for(ffn // world, world)
-        ops.int8_gemm_row_encode(q, mlp.fc2.weight, shift, out=ws.partial(M))
+        push = args.transport == "p2p" and not P.PULL  # the route row_linear takes
+        if push:
+            ws.encode_push(q, mlp.fc2.weight, shift)
+        else:
+            ops.int8_gemm_row_encode(q, mlp.fc2.weight, shift, out=ws.partial(M))
         if record:
             ev[1].record(stream)
         ws.epoch = P.next_epoch(ws.epoch)
         ops.peer_reduce(ws.bases, ws.world, ws.rank, 0, ws.partial_off, ws.final_off, M, hidden,
                         shift, scale, mlp.fc2.weight_scale.reshape(-1), xres, None, None, ws.epoch,
-                        multicast=ws.multicast if args.transport == "nvls" else 0)
+                        multicast=ws.multicast if args.transport == "nvls" else 0, pushed=push)
         if record:
             ev[2].record(stream)
         ops.peer_gather(ws.bases, ws.world, ws.rank, 0, ws.final_off, M, hidden, xres, ws.epoch)
@@ -782,7 +786,12 @@ def run_ours(args):
                              enumerate(("peer_producer", "gemm_encode", "reduce_incl_ready_wait",
                                         "gather"))},
             "fc2_chain_note": "[min, max] over ranks of the mean per step; the reduce includes "
-                              "the wait for the slowest rank's ready flag"}
+                              "the wait for the slowest rank's ready flag",
+            "fc2_exchange": ("push: the row GEMM stores each partial row into its owner's "
+                             "buffer over NVLink, the owner reduces from local memory"
+                             if args.transport == "p2p" and not P.PULL else
+                             "pull: the row GEMM writes locally, each owner loads its rows "
+                             "from every peer")}
            if sub_events else {}),
         "device_error": err,
         **({"sm_clock_in_kernel": sm_clock} if sm_clock else {}),

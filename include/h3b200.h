@@ -291,6 +291,24 @@ int h3_peer_reduce(const void* const* bases, int world, int rank, int64_t flags_
  * h3_peer_gather are those of h3_peer_reduce.  Bit-identical to h3_peer_reduce at
  * world 2; at world 4 and 8 the switch's summation order is its own (rare last-bit
  * differences of the fp16 sum where the fp32 partial sums are inexact). */
+/* The reduce-scatter fused into the row GEMM: h3_int8_gemm_row_encode whose output row
+ * r (owner o = r / per) is stored straight into rank o's buffer (NVLink stores from the
+ * GEMM epilogue, overlapping its tensor work) at partial_off, slot row rank * per +
+ * (r - o * per), so that each owner's partial area holds [world][per][n]: every rank's
+ * rows of its block.  The area must hold world * per rows.  bases / world / rank as for
+ * h3_peer_reduce; n % 8 == 0. */
+int h3_int8_gemm_row_encode_push(const int8_t* q, const int8_t* w, int64_t m, int64_t n,
+                                 int64_t k, int shift, const void* const* bases, int world,
+                                 int rank, int64_t partial_off, void* stream);
+/* h3_peer_reduce after h3_int8_gemm_row_encode_push: the owned rows' partials are
+ * already in this rank's buffer (slot w = rank w), so the reduce reads local memory
+ * only; the same rank-order sum, epilogue, final-row stores into every peer, flags and
+ * h3_peer_gather.  Same bits as h3_peer_reduce. */
+int h3_peer_reduce_pushed(const void* const* bases, int world, int rank, int64_t flags_off,
+                          int64_t partial_off, int64_t final_off, int64_t rows, int64_t width,
+                          int shift, const float* row_scale, const float* weight_scale,
+                          void* residual_f16, const float* gate, int64_t gate_rows,
+                          const int32_t* labels, uint32_t epoch, void* stream);
 int h3_peer_reduce_nvls(const void* const* bases, const void* multicast, int world, int rank,
                         int64_t flags_off, int64_t partial_off, int64_t final_off, int64_t rows,
                         int64_t width, int shift, const float* row_scale,

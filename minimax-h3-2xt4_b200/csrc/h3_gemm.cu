@@ -72,6 +72,17 @@ enum Epi {
   EPI_ROW_PACK8 = 5
 };
 
+// Owner-routed encode output (EPI_ROW_ENCODE with world > 0): row r of this rank's
+// partial belongs to rank o = r / per, and is stored into o's peer-mapped workspace at
+// bases[o] + partial_off, slot row rank * per + (r - o * per) - the reduce-scatter of
+// the partials fused into the GEMM's epilogue.
+struct PushOut {
+  uint64_t bases[8];
+  int64_t partial_off;
+  int64_t per;
+  int world, rank;
+};
+
 struct Args {
   int64_t M;          // rows of A / output rows
   int64_t N;          // output columns (SWIGLU: gate rows = n_packed / 2)
@@ -90,6 +101,7 @@ struct Args {
   int scale_vec;  // weight scales / bias may use 128-bit loads
   int out_wide;   // output rows may use 256-bit stores (32-byte base, N % 16 == 0)
   int res_wide;   // residual rows may use 256-bit loads and stores (same conditions)
+  PushOut push;   // EPI_ROW_ENCODE: owner-routed output when push.world > 0
   int* err;
 };
 
@@ -680,8 +692,21 @@ H3_DEV void epilogue_tile(const Args& args, uint32_t tbase, int64_t row, bool ro
         float y[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) y[j] = __fmul_rn(__int2float_rn((int32_t)r[j]), args.enc_factor);
-        store_f16_chunk<16>(reinterpret_cast<__half*>(args.out) + row * N + n0, n0, N, y,
-                            (N & 7) == 0, args.out_wide != 0);
+        __half* dst;
+        if (args.push.world > 0) {
+          // the owner's slot row for this rank, selected without indexing the
+          // parameter array by a register
+          const int64_t owner = row / args.push.per;
+          uint64_t base = args.push.bases[0];
+#pragma unroll
+          for (int o = 1; o < 8; ++o)
+            if (owner == o) base = args.push.bases[o];
+          const int64_t slot = (int64_t)args.push.rank * args.push.per + (row - owner * args.push.per);
+          dst = reinterpret_cast<__half*>(base + args.push.partial_off) + slot * N + n0;
+        } else {
+          dst = reinterpret_cast<__half*>(args.out) + row * N + n0;
+        }
+        store_f16_chunk<16>(dst, n0, N, y, (N & 7) == 0, args.out_wide != 0);
       } else {  // EPI_ROW_DEQUANT
         float y[16];
 #pragma unroll
@@ -851,6 +876,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    // owner-routed rows went to other GPUs: performed before the kernel completes
+    if (EPI == EPI_ROW_ENCODE && args.push.world > 0) __threadfence_system();
   }
 
   tc_fence_before();
@@ -1036,6 +1063,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    if (EPI == EPI_ROW_ENCODE && args.push.world > 0) __threadfence_system();
   }
 
   tc_fence_before();
@@ -1152,7 +1180,13 @@ static int launch(const int8_t* q, const int8_t* w, int64_t M, int64_t N, int64_
   set_raster(args, (pair ? BM2 : BM) * K, (EPI == EPI_SWIGLU ? 2 * tile_n : tile_n) * K);
   {
     const void* o = EPI == EPI_ROW_DEQUANT ? args.row.out : args.out;
-    args.out_wide = o != nullptr && h3host::aligned(o, 32) && N % 16 == 0;
+    bool wide = o != nullptr && h3host::aligned(o, 32);
+    if (args.push.world > 0) {
+      wide = args.push.partial_off % 32 == 0;
+      for (int w = 0; w < args.push.world; ++w)
+        wide = wide && args.push.bases[w] % 32 == 0;
+    }
+    args.out_wide = wide && N % 16 == 0;
     args.res_wide = EPI == EPI_ROW_DEQUANT && args.row.residual != nullptr &&
                     h3host::aligned(args.row.residual, 32) && N % 16 == 0 &&
                     (args.row.gate == nullptr || h3host::aligned(args.row.gate, 16));
@@ -1248,6 +1282,27 @@ extern "C" int h3_int8_gemm_row_encode(const int8_t* q, const int8_t* w, int64_t
     return H3_ERR_INVALID;
   Args a = blank_args();
   a.out = out_f16;
+  a.enc_factor = ldexpf(1.0f, -shift);
+  return launch<EPI_ROW_ENCODE>(q, w, m, n, k, a, (cudaStream_t)stream);
+}
+
+extern "C" int h3_int8_gemm_row_encode_push(const int8_t* q, const int8_t* w, int64_t m,
+                                            int64_t n, int64_t k, int shift,
+                                            const void* const* bases, int world, int rank,
+                                            int64_t partial_off, void* stream) {
+  if (shift < 0 || shift > 60 || bases == nullptr || (world != 2 && world != 4 && world != 8) ||
+      rank < 0 || rank >= world || partial_off < 0 || partial_off % 16 != 0 || n % 8 != 0)
+    return H3_ERR_INVALID;
+  Args a = blank_args();
+  for (int r = 0; r < world; ++r) {
+    if (bases[r] == nullptr || !h3host::aligned(bases[r], 16)) return H3_ERR_INVALID;
+    a.push.bases[r] = reinterpret_cast<uint64_t>(bases[r]);
+  }
+  a.push.world = world;
+  a.push.rank = rank;
+  a.push.partial_off = partial_off;
+  a.push.per = m > 0 ? (m + world - 1) / world : 1;
+  a.out = const_cast<void*>(bases[rank]);
   a.enc_factor = ldexpf(1.0f, -shift);
   return launch<EPI_ROW_ENCODE>(q, w, m, n, k, a, (cudaStream_t)stream);
 }

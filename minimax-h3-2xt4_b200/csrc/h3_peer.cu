@@ -257,7 +257,10 @@ H3_DEV uint4 epilogue_chunk(const Args& a, const int32_t (&q)[8], int64_t r, int
   return x;
 }
 
-enum Payload { FP16_P2P = 0, INT8_P2P = 1, FP16_NVLS = 2 };
+// FP16_PUSHED: the row GEMM already stored every rank's partial of this rank's block
+// into this rank's buffer (slot w = rank w's rows, h3_int8_gemm_row_encode_push), so
+// the reduce reads only local memory.
+enum Payload { FP16_P2P = 0, INT8_P2P = 1, FP16_NVLS = 2, FP16_PUSHED = 3 };
 
 template <int W, int PAYLOAD>
 __global__ void __launch_bounds__(THREADS) reduce_kernel(const Args a) {
@@ -274,11 +277,16 @@ __global__ void __launch_bounds__(THREADS) reduce_kernel(const Args a) {
     const int64_t first = a.row_begin * chunks;  // uint4 index of the block's first chunk
     const int64_t stride = (int64_t)gridDim.x * THREADS;
     uint4* res = reinterpret_cast<uint4*>(a.residual);
+    uint64_t own = a.bases[0];  // this rank's buffer, without indexing by a register
+#pragma unroll
+    for (int w = 1; w < W; ++w)
+      if (w == a.rank) own = a.bases[w];
     // U chunks per thread and iteration, all their loads issued before any is used: the
     // NVLink (or switch) round trip is paid once per U chunks.  U keeps the loaded
     // words within the register budget that lets a CTA sit beside a GEMM CTA.
-    constexpr int U = PAYLOAD == FP16_NVLS ? 4 : (PAYLOAD == FP16_P2P && W == 2) ? 2 : 1;
-    constexpr int L = PAYLOAD == FP16_P2P ? W : 1;  // words loaded per chunk
+    constexpr int U = PAYLOAD == FP16_NVLS ? 4
+                      : ((PAYLOAD == FP16_P2P || PAYLOAD == FP16_PUSHED) && W == 2) ? 2 : 1;
+    constexpr int L = (PAYLOAD == FP16_P2P || PAYLOAD == FP16_PUSHED) ? W : 1;  // words a chunk
     for (int64_t i0 = blockIdx.x * (int64_t)THREADS + threadIdx.x; i0 < total; i0 += stride * U) {
       uint4 u[U][L], x[U];
 #pragma unroll
@@ -288,6 +296,11 @@ __global__ void __launch_bounds__(THREADS) reduce_kernel(const Args a) {
         const int64_t e = first + i;  // uint4 index of the chunk in [rows][width]
         if (PAYLOAD == FP16_NVLS) {
           u[k][0] = load_reduce_nvls(a.mc, a.partial_off + e * 16);
+        } else if (PAYLOAD == FP16_PUSHED) {
+          // chunk i of slot w (rank w's rows of this block) in this rank's own buffer
+#pragma unroll
+          for (int w = 0; w < L; ++w)
+            u[k][w] = load_received(own, a.partial_off + (w * a.per * chunks + i) * 16);
         } else {
 #pragma unroll
           for (int w = 0; w < L; ++w)
@@ -377,6 +390,8 @@ cudaError_t launch(const Args& a, int blocks, bool gather, int payload, cudaStre
     reduce_kernel<W, INT8_P2P><<<blocks, THREADS, 0, st>>>(a);
   else if (payload == FP16_NVLS)
     reduce_kernel<W, FP16_NVLS><<<blocks, THREADS, 0, st>>>(a);
+  else if (payload == FP16_PUSHED)
+    reduce_kernel<W, FP16_PUSHED><<<blocks, THREADS, 0, st>>>(a);
   else
     reduce_kernel<W, FP16_P2P><<<blocks, THREADS, 0, st>>>(a);
   return cudaGetLastError();
@@ -457,6 +472,17 @@ extern "C" int h3_peer_reduce(const void* const* bases, int world, int rank, int
   return h3::peer::run(bases, nullptr, world, rank, flags_off, partial_off, final_off, rows,
                        width, shift, row_scale, weight_scale, residual_f16, gate, gate_rows,
                        labels, epoch, false, h3::peer::FP16_P2P, stream);
+}
+
+extern "C" int h3_peer_reduce_pushed(const void* const* bases, int world, int rank,
+                                     int64_t flags_off, int64_t partial_off, int64_t final_off,
+                                     int64_t rows, int64_t width, int shift,
+                                     const float* row_scale, const float* weight_scale,
+                                     void* residual_f16, const float* gate, int64_t gate_rows,
+                                     const int32_t* labels, uint32_t epoch, void* stream) {
+  return h3::peer::run(bases, nullptr, world, rank, flags_off, partial_off, final_off, rows,
+                       width, shift, row_scale, weight_scale, residual_f16, gate, gate_rows,
+                       labels, epoch, false, h3::peer::FP16_PUSHED, stream);
 }
 
 extern "C" int h3_peer_reduce_nvls(const void* const* bases, const void* multicast, int world,

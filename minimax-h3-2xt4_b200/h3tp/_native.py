@@ -67,6 +67,9 @@ SIGNATURES = {
                             _U32, _P],
     "h3_peer_reduce": [_PP, _I, _I, _I64, _I64, _I64, _I64, _I64, _I, _P, _P, _P, _P, _I64, _P,
                        _U32, _P],
+    "h3_peer_reduce_pushed": [_PP, _I, _I, _I64, _I64, _I64, _I64, _I64, _I, _P, _P, _P, _P, _I64, _P,
+                       _U32, _P],
+    "h3_int8_gemm_row_encode_push": [_P, _P, _I64, _I64, _I64, _I, _PP, _I, _I, _I64, _P],
     "h3_peer_reduce_nvls": [_PP, _P, _I, _I, _I64, _I64, _I64, _I64, _I64, _I, _P, _P, _P, _P,
                             _I64, _P, _U32, _P],
     "h3_peer_gather": [_PP, _I, _I, _I64, _I64, _I64, _I64, _P, _U32, _P],

@@ -279,6 +279,21 @@ def int8_gemm_row_encode(q, w, shift: int, out: torch.Tensor | None = None) -> t
     return out
 
 
+def int8_gemm_row_encode_push(q, w, shift: int, bases, world: int, rank: int,
+                              partial_off: int) -> None:
+    """INT8 GEMM + scaled-FP16 encode with every output row stored into the peer-mapped
+    buffer of the rank that owns it (h3_int8_gemm_row_encode_push): the reduce-scatter
+    of the partials fused into the GEMM epilogue."""
+    q = _need(q, torch.int8, "q", 2)
+    w = _need(w, torch.int8, "weight", 2)
+    M, K = q.shape
+    if w.shape[1] != K:
+        raise ValueError("Input and weight inner dimensions must match")
+    arr = (ctypes.c_void_p * world)(*bases)
+    N.call("h3_int8_gemm_row_encode_push", q.data_ptr(), w.data_ptr(), M, w.shape[0], K,
+           int(shift), arr, world, rank, int(partial_off), _stream(q))
+
+
 def _gate_args(residual, gate, labels, M, Nn):
     if residual is None:
         return None, None, 0, None
@@ -471,11 +486,12 @@ def gated_add(residual, branch, gate=None, labels=None):
 
 def peer_reduce(bases, world: int, rank: int, flags_off: int, partial_off: int, final_off: int,
                 rows: int, width: int, shift: int, row_scale, weight_scale, residual,
-                gate=None, labels=None, epoch: int = 1, multicast: int = 0):
+                gate=None, labels=None, epoch: int = 1, multicast: int = 0, pushed: bool = False):
     """Reduce + fused gated-residual epilogue of this rank's row block from every rank's
     partial, finished rows stored into the peers' final areas (h3_peer_reduce).  With a
     non-zero `multicast` address of the same buffers the sum is taken in the NVSwitch
-    and the finished rows are broadcast through it (h3_peer_reduce_nvls)."""
+    and the finished rows are broadcast through it (h3_peer_reduce_nvls).  pushed: the
+    partials were owner-routed by int8_gemm_row_encode_push (h3_peer_reduce_pushed)."""
     a = _vec(row_scale, rows, "row_scale")
     ws = _vec(weight_scale, width, "weight_scale")
     if not residual.is_contiguous():
@@ -487,9 +503,9 @@ def peer_reduce(bases, world: int, rank: int, flags_off: int, partial_off: int, 
                final_off, rows, width, int(shift), a.data_ptr(), ws.data_ptr(), res.data_ptr(),
                _ptr(g), grows, _ptr(lab), int(epoch), _stream(res))
         return residual
-    N.call("h3_peer_reduce", arr, world, rank, flags_off, partial_off, final_off, rows, width,
-           int(shift), a.data_ptr(), ws.data_ptr(), res.data_ptr(), _ptr(g), grows, _ptr(lab),
-           int(epoch), _stream(res))
+    N.call("h3_peer_reduce_pushed" if pushed else "h3_peer_reduce", arr, world, rank, flags_off,
+           partial_off, final_off, rows, width, int(shift), a.data_ptr(), ws.data_ptr(),
+           res.data_ptr(), _ptr(g), grows, _ptr(lab), int(epoch), _stream(res))
     return residual
 
 

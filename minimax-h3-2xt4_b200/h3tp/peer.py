@@ -6,18 +6,23 @@ tilelang_dit_fusion.py:146-151).  Over NVSwitch every GPU can load from and stor
 into every peer's HBM directly, so here the exchange is two kernels of our own
 (csrc/h3_peer.cu):
 
-  1. the row GEMM's encode epilogue writes the partial straight into this rank's
-     peer-mapped buffer (no staging copy);
-  2. h3_peer_reduce: each rank loads its rows of every rank's partial (NVLink loads),
-     sums in rank order, decodes, dequantises and updates its rows of the gated
-     residual (the same bits as h3_row_reduce_finish), and stores the finished rows
-     into every peer (NVLink stores, the other direction of the links);
+  1. the row GEMM's encode epilogue stores every partial row straight into the
+     peer-mapped buffer of the rank that owns that row (h3_int8_gemm_row_encode_push:
+     the reduce-scatter rides on the GEMM, NVLink stores overlapping its tensor work);
+  2. h3_peer_reduce_pushed: each rank sums the slots of its rows from local memory in
+     rank order, decodes, dequantises and updates its rows of the gated residual (the
+     same bits as h3_row_reduce_finish), and stores the finished rows into every peer
+     (NVLink stores);
   3. h3_peer_gather: each rank copies the peers' finished rows into its residual.
+(With nvls, or H3_P2P_PULL=1, step 1 writes the partial locally and step 2 loads the
+owned rows from every peer instead: h3_peer_reduce / h3_peer_reduce_nvls.)
 
 The buffers are torch symmetric memory (one allocation per rank, mapped into every
 rank); synchronisation is by epoch flags in the same buffers, with bounded waits.
 """
 from __future__ import annotations
+
+import os
 
 import torch
 import torch.distributed as dist
@@ -26,6 +31,10 @@ from . import ops
 
 FLAGS_BYTES = 1024
 _ALIGN = 256
+# The p2p route pushes the partial rows to their owners from the row GEMM's epilogue;
+# H3_P2P_PULL=1 selects the form in which each owner loads them from the peers instead
+# (the same bits; kept for comparison).
+PULL = os.environ.get("H3_P2P_PULL", "0") == "1"
 
 
 def _group_name(group) -> str:
@@ -59,7 +68,9 @@ def layout(width: int, rows: int) -> dict:
     columns: flags | partial (fp16 [rows][width], or the packed INT8 rows, which are
     smaller) | final rows (fp16 [rows][width]) | row-maximum slots (u64 [rows][8]).
     Every area starts on a 256-byte boundary."""
-    region = -(-rows * width * 2 // _ALIGN) * _ALIGN
+    # world * ceil(rows / world) <= rows + 7 rows: the owner-routed partials
+    # (encode_push) of up to 8 ranks fit the partial area
+    region = -(-(rows + 8) * width * 2 // _ALIGN) * _ALIGN
     slots = -(-rows * 8 * 8 // _ALIGN) * _ALIGN
     return {"partial_off": FLAGS_BYTES, "final_off": FLAGS_BYTES + region,
             "slots_off": FLAGS_BYTES + 2 * region, "nbytes": FLAGS_BYTES + 2 * region + slots}
@@ -164,14 +175,30 @@ class PeerWorkspace:
         ops.peer_gather(self.bases, self.world, self.rank, 0, self.final_off + 2 * row0 * self.width,
                         rows, self.width, residual, self.epoch)
 
+    def encode_push(self, q, weight, shift: int):
+        """The row GEMM with its scaled-fp16 partial rows stored straight into their
+        owners' buffers (ops.int8_gemm_row_encode_push): the reduce-scatter of the
+        partials rides on the GEMM's epilogue.  Follow with reduce_and_gather(pushed=True)."""
+        rows = q.shape[0]
+        if rows > self.capacity:
+            raise ValueError(f"{rows} rows exceed the workspace capacity {self.capacity}")
+        ops.int8_gemm_row_encode_push(q, weight, shift, self.bases, self.world, self.rank,
+                                      self.partial_off)
+
     def reduce_and_gather(self, rows: int, shift: int, row_scale, weight_scale, residual,
-                          gate=None, labels=None, packed: bool = False, nvls: bool = False):
-        """Sums the partials every rank wrote into partial() (or, packed, partial_u8())
-        into `residual` (fp16 [rows, width], updated in place on every rank).  nvls: the
-        fp16 partials are summed in the NVSwitch and the finished rows broadcast through
-        it, when the buffers have a multicast address (otherwise the p2p kernels run)."""
+                          gate=None, labels=None, packed: bool = False, nvls: bool = False,
+                          pushed: bool = False):
+        """Sums the partials every rank wrote into partial() (or, packed, partial_u8();
+        pushed: the owner-routed partials of encode_push) into `residual` (fp16 [rows,
+        width], updated in place on every rank).  nvls: the fp16 partials are summed in
+        the NVSwitch and the finished rows broadcast through it, when the buffers have a
+        multicast address (otherwise the p2p kernels run)."""
         self.epoch = next_epoch(self.epoch)
-        if packed:
+        if pushed:
+            ops.peer_reduce(self.bases, self.world, self.rank, 0, self.partial_off,
+                            self.final_off, rows, self.width, shift, row_scale, weight_scale,
+                            residual, gate, labels, self.epoch, pushed=True)
+        elif packed:
             ops.peer_reduce_int8(self.bases, self.world, self.rank, 0, self.partial_off,
                                  self.final_off, rows, self.width, row_scale, weight_scale,
                                  residual, gate, labels, self.epoch)

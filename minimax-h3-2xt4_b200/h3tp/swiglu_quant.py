@@ -134,15 +134,22 @@ def _finish_quantized(q, scale, weight, weight_scale, comm, scaled_transport=Tru
         shift = T.shift_for(local_k, world)
         if (transport in ("p2p", "nvls") and residual is not None and finish_fn is None
                 and residual.is_contiguous() and residual.shape[-1] % 8 == 0 and P.available(comm)):
-            # GEMM encode straight into the peer-mapped buffer, then the peer-memory
-            # reduce + gated residual + gather (csrc/h3_peer.cu).
+            # p2p: the GEMM's encode epilogue stores each partial row into its owner's
+            # peer-mapped buffer (the reduce-scatter rides on the GEMM), then the owner's
+            # local reduce + gated residual, the finished rows stored into every peer,
+            # and the gather (csrc/h3_gemm.cu, csrc/h3_peer.cu).  nvls (or P.PULL): the
+            # GEMM writes locally and the reduce reads the peers.
             rows = q.shape[0]
             ws = P.workspace(comm, q.device, weight.shape[0], rows)
+            push = transport == "p2p" and not P.PULL
             with label("int8_gemm_scaled_fp16_encode"):
-                ops.int8_gemm_row_encode(q, weight, shift, out=ws.partial(rows))
+                if push:
+                    ws.encode_push(q, weight, shift)
+                else:
+                    ops.int8_gemm_row_encode(q, weight, shift, out=ws.partial(rows))
             with label("scaled_fp16_peer_reduce_gather"):
                 return ws.reduce_and_gather(rows, shift, scale, weight_scale, residual, gate, labels,
-                                            nvls=transport == "nvls")
+                                            nvls=transport == "nvls", pushed=push)
         with label("int8_gemm_scaled_fp16_encode"):
             payload = ops.int8_gemm_row_encode(q, weight, shift)
         if finish_fn is not None:

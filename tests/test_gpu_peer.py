@@ -86,6 +86,62 @@ def test_peer_transport_bit_exact(cuda_device, oracle, world, rows, width, k):
     assert _native.device_error(dev.index or 0) == 0
 
 
+@pytest.mark.parametrize("world,rows,width,k", [(2, 130, 512, 512), (4, 77, 264, 256),
+                                                (8, 99, 1024, 256), (2, 1030, 3072, 1024)])
+def test_peer_transport_pushed_bit_exact(cuda_device, oracle, world, rows, width, k):
+    """The fused reduce-scatter: each emulated rank's row GEMM stores every partial row
+    into the buffer of the rank that owns it (h3_int8_gemm_row_encode_push, slot row
+    rank * per + local row), the owner sums its slots from local memory
+    (h3_peer_reduce_pushed); slots and residuals against the oracle, bit for bit."""
+    from h3tp import _native, ops, transport
+    rng = np.random.default_rng(world + 40)
+    shift = transport.shift_for(k, world)
+    qs = [rng.integers(-128, 128, size=(rows, k), dtype=np.int8) for _ in range(world)]
+    ws = [rng.integers(-127, 128, size=(width, k), dtype=np.int8) for _ in range(world)]
+    enc = np.stack([oracle.fp16_encode(oracle.int8_gemm(q, w), shift) for q, w in zip(qs, ws)])
+    a = rng.uniform(1e-4, 1e-2, size=rows).astype(np.float32)
+    s = rng.uniform(1e-5, 1e-4, size=width).astype(np.float32)
+    X = rng.standard_normal((rows, width)).astype(np.float16)
+    G = rng.standard_normal((3, width)).astype(np.float32)
+    labels = rng.integers(0, 3, size=rows).astype(np.int32)
+    ref = X.copy()
+    oracle.row_reduce_finish(enc, shift, a, s, out="residual", residual=ref, gate=G, labels=labels)
+
+    dev = cuda_device
+    per = -(-rows // world)
+    bufs, roff, foff = _buffers(dev, world, world * per, width)
+    bases = [b.data_ptr() for b in bufs]
+    A, S = torch.from_numpy(a).to(dev), torch.from_numpy(s).to(dev)
+    Gd, L = torch.from_numpy(G).to(dev), torch.from_numpy(labels).to(dev)
+    qd = [torch.from_numpy(q).to(dev) for q in qs]
+    wd = [torch.from_numpy(w).to(dev) for w in ws]
+    res = [torch.from_numpy(X.copy()).to(dev) for _ in range(world)]
+    for epoch in (1, 2):
+        for r in range(world):
+            res[r].copy_(torch.from_numpy(X))
+            ops.int8_gemm_row_encode_push(qd[r], wd[r], shift, bases, world, r, roff)
+        torch.cuda.synchronize()
+        for o in range(world):
+            slots = bufs[o][roff:roff + world * per * width * 2].view(torch.float16)
+            slots = slots.view(world, per, width).cpu().numpy()
+            lo, hi = o * per, min(rows, (o + 1) * per)
+            for r in range(world):
+                got = slots[r, :hi - lo].view(np.uint16)
+                assert np.array_equal(got, enc[r][lo:hi].view(np.uint16)), (o, r)
+        for b in bufs:
+            _set(b, READY, range(world), epoch)
+        for r in range(world):
+            ops.peer_reduce(bases, world, r, 0, roff, foff, rows, width, shift, A, S, res[r], Gd, L,
+                            epoch, pushed=True)
+        for r in range(world):
+            ops.peer_gather(bases, world, r, 0, foff, rows, width, res[r], epoch)
+        torch.cuda.synchronize()
+        for r in range(world):
+            got = res[r].cpu().numpy()
+            assert np.array_equal(got.view(np.uint16), ref.view(np.uint16)), f"rank {r} epoch {epoch}"
+    assert _native.device_error(dev.index or 0) == 0
+
+
 @pytest.mark.parametrize("world,rows,width,k", [(2, 130, 512, 512), (8, 99, 1024, 256)])
 def test_peer_transport_packed_int8_bit_exact(cuda_device, oracle, world, rows, width, k):
     """The same exchange with the packed INT8 payload ('int8_gather'): the row GEMM packs
