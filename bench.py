@@ -485,7 +485,7 @@ def run_ours(args):
         if record:
             ev[0].record(stream)
         shift = T.shift_for(ffn // world, world)
-        push = args.transport == "p2p" and not P.PULL  # the route row_linear takes
+        push = args.transport == "p2p" and P.pushes(world)  # the route row_linear takes
         if push:
             ws.encode_push(q, mlp.fc2.weight, shift)
         else:
@@ -789,7 +789,7 @@ def run_ours(args):
                               "the wait for the slowest rank's ready flag",
             "fc2_exchange": ("push: the row GEMM stores each partial row into its owner's "
                              "buffer over NVLink, the owner reduces from local memory"
-                             if args.transport == "p2p" and not P.PULL else
+                             if args.transport == "p2p" and P.pushes(world) else
                              "pull: the row GEMM writes locally, each owner loads its rows "
                              "from every peer")}
            if sub_events else {}),

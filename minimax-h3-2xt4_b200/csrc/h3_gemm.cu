@@ -102,6 +102,7 @@ struct Args {
   int out_wide;   // output rows may use 256-bit stores (32-byte base, N % 16 == 0)
   int res_wide;   // residual rows may use 256-bit loads and stores (same conditions)
   PushOut push;   // EPI_ROW_ENCODE: owner-routed output when push.world > 0
+  int m_rotate;   // M-blocks the tile order is rotated by (owner-routed output)
   int* err;
 };
 
@@ -306,6 +307,11 @@ H3_DEV void tmem_wait_ld(uint32_t (&a)[8], uint32_t (&b)[8]) {
 // L2) sweep all M-blocks, N fastest, so A is read from HBM once per group; otherwise
 // groups of group_m M-blocks (16 when unset) sweep all N-blocks, M fastest, so B is
 // read once per group.  The host picks the form with less HBM traffic.
+H3_DEV void rotate_m(const Args& a, int& mb) {
+  mb += a.m_rotate;
+  if (mb >= a.tiles_m) mb -= a.tiles_m;
+}
+
 H3_DEV void tile_coords(int tile, const Args& a, int& mb, int& nb) {
   if (a.group_n > 0) {
     const int group = a.group_n * a.tiles_m;
@@ -315,6 +321,7 @@ H3_DEV void tile_coords(int tile, const Args& a, int& mb, int& nb) {
     const int local = tile - g * group;
     nb = first_n + local % gn;
     mb = local / gn;
+    rotate_m(a, mb);
     return;
   }
   const int G = a.group_m > 0 ? a.group_m : 16;
@@ -325,6 +332,7 @@ H3_DEV void tile_coords(int tile, const Args& a, int& mb, int& nb) {
   const int local = tile - g * group;
   mb = first_m + local % gm;
   nb = local / gm;
+  rotate_m(a, mb);
 }
 
 // ---------------------------------------------------------------------------
@@ -1187,6 +1195,14 @@ static int launch(const int8_t* q, const int8_t* w, int64_t M, int64_t N, int64_
         wide = wide && args.push.bases[w] % 32 == 0;
     }
     args.out_wide = wide && N % 16 == 0;
+    // Owner-routed rows: every rank starts on its own row block and walks the blocks
+    // from there, so that at any time the ranks store into different owners instead of
+    // all into the owner of the same rows (an incast on one GPU's links).
+    args.m_rotate = 0;
+    if (args.push.world > 0) {
+      const int64_t tm = (M + (pair ? BM2 : BM) - 1) / (pair ? BM2 : BM);
+      args.m_rotate = (int)(((int64_t)args.push.rank * args.push.per / (pair ? BM2 : BM)) % tm);
+    }
     args.res_wide = EPI == EPI_ROW_DEQUANT && args.row.residual != nullptr &&
                     h3host::aligned(args.row.residual, 32) && N % 16 == 0 &&
                     (args.row.gate == nullptr || h3host::aligned(args.row.gate, 16));

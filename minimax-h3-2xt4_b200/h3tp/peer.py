@@ -14,8 +14,9 @@ into every peer's HBM directly, so here the exchange is two kernels of our own
      same bits as h3_row_reduce_finish), and stores the finished rows into every peer
      (NVLink stores);
   3. h3_peer_gather: each rank copies the peers' finished rows into its residual.
-(With nvls, or H3_P2P_PULL=1, step 1 writes the partial locally and step 2 loads the
-owned rows from every peer instead: h3_peer_reduce / h3_peer_reduce_nvls.)
+That is the push form (`pushes(world)`); in the pull form, and with nvls, step 1 writes
+the partial locally and step 2 loads the owned rows from every peer instead
+(h3_peer_reduce / h3_peer_reduce_nvls).
 
 The buffers are torch symmetric memory (one allocation per rank, mapped into every
 rank); synchronisation is by epoch flags in the same buffers, with bounded waits.
@@ -31,10 +32,18 @@ from . import ops
 
 FLAGS_BYTES = 1024
 _ALIGN = 256
-# The p2p route pushes the partial rows to their owners from the row GEMM's epilogue;
-# H3_P2P_PULL=1 selects the form in which each owner loads them from the peers instead
-# (the same bits; kept for comparison).
-PULL = os.environ.get("H3_P2P_PULL", "0") == "1"
+# Two forms of the p2p exchange, the same bits: 'pull' (each owner loads its rows of
+# every rank's partial after the GEMM) and 'push' (the GEMM epilogue stores every
+# partial row into its owner's buffer).  H3_P2P_EXCHANGE=push|pull overrides the
+# default, which is the form measured faster at that world size.
+_EXCHANGE = os.environ.get("H3_P2P_EXCHANGE", "")
+
+
+def pushes(world: int) -> bool:
+    """Whether the p2p route at `world` ranks takes the push form."""
+    if _EXCHANGE in ("push", "pull"):
+        return _EXCHANGE == "push"
+    return False
 
 
 def _group_name(group) -> str:

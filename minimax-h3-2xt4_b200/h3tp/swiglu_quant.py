@@ -134,14 +134,14 @@ def _finish_quantized(q, scale, weight, weight_scale, comm, scaled_transport=Tru
         shift = T.shift_for(local_k, world)
         if (transport in ("p2p", "nvls") and residual is not None and finish_fn is None
                 and residual.is_contiguous() and residual.shape[-1] % 8 == 0 and P.available(comm)):
-            # p2p: the GEMM's encode epilogue stores each partial row into its owner's
-            # peer-mapped buffer (the reduce-scatter rides on the GEMM), then the owner's
-            # local reduce + gated residual, the finished rows stored into every peer,
-            # and the gather (csrc/h3_gemm.cu, csrc/h3_peer.cu).  nvls (or P.PULL): the
-            # GEMM writes locally and the reduce reads the peers.
+            # p2p, push form: the GEMM's encode epilogue stores each partial row into its
+            # owner's peer-mapped buffer (the reduce-scatter rides on the GEMM), then the
+            # owner's local reduce + gated residual, the finished rows stored into every
+            # peer, and the gather (csrc/h3_gemm.cu, csrc/h3_peer.cu).  Pull form (and
+            # nvls): the GEMM writes locally and the reduce reads the peers.
             rows = q.shape[0]
             ws = P.workspace(comm, q.device, weight.shape[0], rows)
-            push = transport == "p2p" and not P.PULL
+            push = transport == "p2p" and P.pushes(world)
             with label("int8_gemm_scaled_fp16_encode"):
                 if push:
                     ws.encode_push(q, weight, shift)
