@@ -210,3 +210,17 @@ def test_policy_pipeline_chunks_validation():
     for bad in (-1, 65, 2.0, True):
         with pytest.raises(ValueError):
             H3OperatorPolicy(mlp_pipeline_chunks=bad)
+
+
+def test_p2p_exchange_form_override(monkeypatch):
+    """The p2p exchange form: the measured default per TP size, overridden by
+    H3_P2P_EXCHANGE (read at import); either form gives the same bits."""
+    import importlib
+    from h3tp import peer
+    for env, want in (("push", True), ("pull", False)):
+        monkeypatch.setenv("H3_P2P_EXCHANGE", env)
+        importlib.reload(peer)
+        assert all(peer.pushes(w) is want for w in (2, 4, 8))
+    monkeypatch.delenv("H3_P2P_EXCHANGE", raising=False)
+    importlib.reload(peer)
+    assert all(isinstance(peer.pushes(w), bool) for w in (2, 4, 8))
