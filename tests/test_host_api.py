@@ -224,3 +224,29 @@ def test_p2p_exchange_form_override(monkeypatch):
     monkeypatch.delenv("H3_P2P_EXCHANGE", raising=False)
     importlib.reload(peer)
     assert all(isinstance(peer.pushes(w), bool) for w in (2, 4, 8))
+
+
+def test_bench_reference_arm_json_contract():
+    """bench.py --impl reference on a tiny block: one JSON line with the contract's keys,
+    the e2e object of a host-only run and the CPU baseline it describes."""
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    r = subprocess.run([sys.executable, str(root / "bench.py"), "--impl", "reference",
+                        "--tokens", "512", "--hidden", "256", "--ffn", "512", "--steps", "2",
+                        "--warmup", "1", "--ref-rows", "64"],
+                       capture_output=True, text=True, timeout=300, cwd=str(root))
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config",
+                "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["impl"] == "reference" and d["steps"] == 2 and d["value"] > 0
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+    assert d["cpu_baseline"]["kind"] in ("port", "reference") and d["cpu_baseline"]["cores"] >= 1
+    assert d["config"]["workload"] == "dit_mlp_block" and d["config"]["M"] == 512
