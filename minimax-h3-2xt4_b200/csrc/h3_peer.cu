@@ -362,6 +362,153 @@ __global__ void __launch_bounds__(THREADS) reduce_kernel(const Args a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Pull reduce with bulk copies (the default p2p form).  The owned rows of every rank's
+// partial reach shared memory through cp.async.bulk - the SM's bulk-copy unit, one
+// 2-8 KB request per rank and tile, completing on the stage's mbarrier - instead of one
+// 16-byte load per lane: NVLink then carries a few large reads instead of many small
+// ones, and no thread holds a register while they are in flight.  The copies read the
+// peers' memory directly and carry no multicast.  BULK_STAGES tiles of BULK_STAGE bytes
+// (the W ranks' slices of BULK_STAGE / 16 / W chunks) are in flight per CTA; the sum,
+// decode, epilogue and final-row stores are those of reduce_kernel.  Every wait is
+// bounded; a CTA that gives up records H3_ERR_TIMEOUT, waits (bounded again) for the
+// copies it issued to land before it leaves, and publishes no done flag.
+// ---------------------------------------------------------------------------
+constexpr int BULK_THREADS = 128;
+constexpr int BULK_STAGES = 4;
+constexpr int BULK_STAGE = 16384;
+
+H3_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+H3_DEV bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait for a stage barrier; `deadline` is set at the first wait that has to
+// spin and bounds all later ones of the same caller.
+H3_DEV bool bulk_wait(uint32_t bar, uint32_t parity, uint64_t& deadline) {
+  while (!mbar_try(bar, parity)) {
+    const uint64_t now = globaltimer();
+    if (deadline == 0) deadline = now + TIMEOUT_NS;
+    if (now > deadline) return false;
+  }
+  return true;
+}
+
+// Thread 0: tile t of the owned block (chunks [t * TC, ...)) from every rank into stage s.
+template <int W>
+H3_DEV void bulk_issue(const Args& a, uint8_t* stages, uint64_t* bars, int64_t t, int s,
+                       int64_t total, uint64_t block_off) {
+  constexpr int TC = BULK_STAGE / 16 / W;
+  const int64_t c0 = t * TC;
+  const uint32_t bytes = (uint32_t)(min((int64_t)TC, total - c0) * 16);
+  const uint32_t bar = smem_u32(bars + s);
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+               "r"(bytes * W)
+               : "memory");
+#pragma unroll
+  for (int w = 0; w < W; ++w) {
+    const uint32_t dst = smem_u32(stages + ((int64_t)s * W + w) * TC * 16);
+    const uint64_t src = a.bases[w] + block_off + (uint64_t)c0 * 16;
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+  }
+}
+
+template <int W>
+__global__ void __launch_bounds__(BULK_THREADS) reduce_bulk_kernel(const Args a) {
+  extern __shared__ __align__(128) uint8_t stages[];
+  __shared__ __align__(8) uint64_t bars[BULK_STAGES];
+  constexpr int TC = BULK_STAGE / 16 / W;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < BULK_STAGES; ++s)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(bars + s)) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  // Phase 0: this rank's partial is complete (stream order after the row GEMM).
+  if ((int)threadIdx.x < W) {
+    __threadfence_system();
+    store_release(flag(a, threadIdx.x, READY, a.rank), a.epoch);
+  }
+  bool ok = wait_all(a, READY, false);  // also orders the barrier initialisation
+  const int64_t chunks = a.width >> 3;
+  const int64_t total = (a.row_end - a.row_begin) * chunks;
+  const int64_t first = a.row_begin * chunks;
+  const uint64_t block_off = (uint64_t)a.partial_off + (uint64_t)first * 16;
+  const int64_t tiles = (total + TC - 1) / TC;
+  const int64_t mine = (ok && blockIdx.x < tiles) ? (tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  if (threadIdx.x == 0)
+    for (int64_t k = 0; k < mine && k < BULK_STAGES; ++k)
+      bulk_issue<W>(a, stages, bars, blockIdx.x + k * gridDim.x, (int)k, total, block_off);
+  uint4* res = reinterpret_cast<uint4*>(a.residual);
+  uint64_t deadline = 0;
+  int64_t k = 0;
+  for (; k < mine; ++k) {
+    const int s = (int)(k % BULK_STAGES);
+    const bool landed = bulk_wait(smem_u32(bars + s), (uint32_t)((k / BULK_STAGES) & 1), deadline);
+    if (!__syncthreads_and(landed)) {
+      ok = false;
+      break;
+    }
+    const int64_t c0 = (blockIdx.x + k * gridDim.x) * TC;
+    const int n = (int)min((int64_t)TC, total - c0);
+    const uint4* st = reinterpret_cast<const uint4*>(stages + (int64_t)s * W * TC * 16);
+    for (int j = threadIdx.x; j < n; j += BULK_THREADS) {
+      uint4 u[W];
+#pragma unroll
+      for (int w = 0; w < W; ++w) u[w] = st[w * TC + j];
+      const int64_t e = first + c0 + j;  // uint4 index of the chunk in [rows][width]
+      const int64_t r = e / chunks;
+      const int64_t cc = (e - r * chunks) << 3;
+      int32_t q[8];
+      restore_fp16<W>(a, u, q);
+      const uint4 y = epilogue_chunk(a, q, r, cc, res[e]);
+      res[e] = y;
+#pragma unroll
+      for (int w = 0; w < W; ++w)
+        if (w != a.rank) reinterpret_cast<uint4*>(a.bases[w] + a.final_off)[e] = y;
+    }
+    __syncthreads();  // stage s has been read by every thread
+    if (threadIdx.x == 0 && k + BULK_STAGES < mine)
+      bulk_issue<W>(a, stages, bars, blockIdx.x + (k + BULK_STAGES) * gridDim.x, s, total,
+                    block_off);
+  }
+  if (!ok && threadIdx.x == 0) {
+    report_error(a.err, H3_ERR_TIMEOUT);
+    // the copies this CTA issued land in its shared memory: wait for them (bounded)
+    uint64_t drain = 0;
+    for (int64_t kk = k; kk < mine && kk < k + BULK_STAGES; ++kk)
+      bulk_wait(smem_u32(bars + kk % BULK_STAGES), (uint32_t)((kk / BULK_STAGES) & 1), drain);
+  }
+  // done publication as in reduce_kernel
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned int* counter =
+        reinterpret_cast<unsigned int*>(a.bases[a.rank] + a.flags_off + COUNTER);
+    const unsigned int old = atomicAdd(counter, ok ? 1u : 0x10000u);
+    const unsigned int seen = (old & 0xffffu) + (old >> 16);
+    if (seen == gridDim.x - 1) {
+      const bool all_ok = ok && (old >> 16) == 0;
+      *reinterpret_cast<volatile unsigned int*>(counter) = 0;
+      __threadfence_system();
+      if (all_ok)
+        for (int w = 0; w < W; ++w) store_release(flag(a, w, DONE, a.rank), a.epoch);
+    }
+  }
+}
+
 template <int W>
 __global__ void __launch_bounds__(THREADS) gather_kernel(const Args a) {
   if (!wait_all(a, DONE, true)) {
@@ -382,10 +529,44 @@ __global__ void __launch_bounds__(THREADS) gather_kernel(const Args a) {
   }
 }
 
+// The bulk-copy pull reduce is the p2p default; H3_PEER_BULK=0 selects the lane-load
+// reduce_kernel (the same bits), read once per process.
+static bool bulk_pull() {
+  static const bool on = [] {
+    const char* e = getenv("H3_PEER_BULK");
+    return e == nullptr || e[0] != '0';
+  }();
+  return on;
+}
+
 template <int W>
-cudaError_t launch(const Args& a, int blocks, bool gather, int payload, cudaStream_t st) {
+cudaError_t launch_bulk(const Args& a, int dev, cudaStream_t st) {
+  constexpr int TC = BULK_STAGE / 16 / W;
+  const size_t smem = (size_t)BULK_STAGES * BULK_STAGE;
+  static bool attr[64] = {false};
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(reduce_bulk_kernel<W>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr[dev] = true;
+  }
+  const int64_t total = (a.row_end - a.row_begin) * (a.width >> 3);
+  const int64_t tiles = (total + TC - 1) / TC;
+  // three CTAs an SM (64 KB of stages each): 48 tiles of 16 KB in flight per SM
+  const int blocks = (int)std::max<int64_t>(
+      1, std::min<int64_t>(tiles, (int64_t)h3host::sm_count(dev) * 3));
+  reduce_bulk_kernel<W><<<blocks, BULK_THREADS, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <int W>
+cudaError_t launch(const Args& a, int blocks, bool gather, int payload, int dev,
+                   cudaStream_t st) {
   if (gather)
     gather_kernel<W><<<blocks, THREADS, 0, st>>>(a);
+  else if (payload == FP16_P2P && bulk_pull())
+    return launch_bulk<W>(a, dev, st);
   else if (payload == INT8_P2P)
     reduce_kernel<W, INT8_P2P><<<blocks, THREADS, 0, st>>>(a);
   else if (payload == FP16_NVLS)
@@ -454,9 +635,9 @@ int run(const void* const* bases, const void* mc, int world, int rank, int64_t f
   const int blocks = (int)std::max<int64_t>(
       1, std::min<int64_t>((items + THREADS - 1) / THREADS, (int64_t)h3host::sm_count(dev) * 16));
   cudaStream_t st = (cudaStream_t)stream;
-  cudaError_t e = world == 2 ? launch<2>(a, blocks, gather, payload, st)
-                  : world == 4 ? launch<4>(a, blocks, gather, payload, st)
-                               : launch<8>(a, blocks, gather, payload, st);
+  cudaError_t e = world == 2 ? launch<2>(a, blocks, gather, payload, dev, st)
+                  : world == 4 ? launch<4>(a, blocks, gather, payload, dev, st)
+                               : launch<8>(a, blocks, gather, payload, dev, st);
   return e == cudaSuccess ? H3_OK : H3_ERR_CUDA;
 }
 
