@@ -15,8 +15,9 @@
 // One call with epoch e (the same on every rank, increasing by one per call):
 //   reduce kernel  each CTA stores e into ready[rank] of every rank (release, system
 //                  scope), waits until its own ready[w] >= e for every w, then loads
-//                  the rows it owns from every rank's partial (coalesced NVLink
-//                  loads), sums them in rank order 0..world-1 (fp32, one fp16 rounding
+//                  the rows it owns from every rank's partial (bulk copies into shared
+//                  memory, reduce_bulk_kernel; or coalesced 16-byte loads per lane,
+//                  reduce_kernel), sums them in rank order 0..world-1 (fp32, one fp16 rounding
 //                  at the end, the bits of an NCCL fp16 SUM at world 2), decodes,
 //                  dequantises and applies the gated residual to those rows of the
 //                  local residual, and stores the finished rows into every peer's final
