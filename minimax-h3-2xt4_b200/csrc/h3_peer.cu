@@ -371,10 +371,7 @@ __global__ void __launch_bounds__(THREADS) reduce_kernel(const Args a) {
 // ones, and no thread holds a register while they are in flight.  The copies read the
 // peers' memory directly and carry no multicast.  BULK_STAGES tiles of BULK_STAGE bytes
 // (the W ranks' slices of BULK_STAGE / 16 / W chunks) are in flight per CTA; the sum,
-// decode and epilogue are those of reduce_kernel, and the finished rows of a tile leave
-// for the peers' final areas the same way, one bulk store per peer from a shared-memory
-// output buffer (the CTA waits for those stores to complete before it counts itself
-// done).  Every wait is
+// decode, epilogue and final-row stores are those of reduce_kernel.  Every wait is
 // bounded; a CTA that gives up records H3_ERR_TIMEOUT, waits (bounded again) for the
 // copies it issued to land before it leaves, and publishes no done flag.
 // ---------------------------------------------------------------------------
@@ -456,17 +453,11 @@ __global__ void __launch_bounds__(BULK_THREADS) reduce_bulk_kernel(const Args a)
     for (int64_t k = 0; k < mine && k < BULK_STAGES; ++k)
       bulk_issue<W>(a, stages, bars, blockIdx.x + k * gridDim.x, (int)k, total, block_off);
   uint4* res = reinterpret_cast<uint4*>(a.residual);
-  // finished rows of each stage, written back to the peers by bulk stores
-  uint8_t* outs = stages + (int64_t)BULK_STAGES * BULK_STAGE;
-  const uint64_t fin_off = (uint64_t)a.final_off + (uint64_t)first * 16;
   uint64_t deadline = 0;
   int64_t k = 0;
   for (; k < mine; ++k) {
     const int s = (int)(k % BULK_STAGES);
     const bool landed = bulk_wait(smem_u32(bars + s), (uint32_t)((k / BULK_STAGES) & 1), deadline);
-    // the bulk stores of tile k - BULK_STAGES have read this stage's output buffer
-    if (threadIdx.x == 0)
-      asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(BULK_STAGES - 1) : "memory");
     if (!__syncthreads_and(landed)) {
       ok = false;
       break;
@@ -474,7 +465,6 @@ __global__ void __launch_bounds__(BULK_THREADS) reduce_bulk_kernel(const Args a)
     const int64_t c0 = (blockIdx.x + k * gridDim.x) * TC;
     const int n = (int)min((int64_t)TC, total - c0);
     const uint4* st = reinterpret_cast<const uint4*>(stages + (int64_t)s * W * TC * 16);
-    uint4* out = reinterpret_cast<uint4*>(outs + (int64_t)s * TC * 16);
     for (int j = threadIdx.x; j < n; j += BULK_THREADS) {
       uint4 u[W];
 #pragma unroll
@@ -486,38 +476,21 @@ __global__ void __launch_bounds__(BULK_THREADS) reduce_bulk_kernel(const Args a)
       restore_fp16<W>(a, u, q);
       const uint4 y = epilogue_chunk(a, q, r, cc, res[e]);
       res[e] = y;
-      out[j] = y;
-    }
-    // generic-proxy writes of the output buffer, then the bulk (async-proxy) reads of it
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncthreads();  // stage s has been read and its output written by every thread
-    if (threadIdx.x == 0) {
-      const uint32_t src = smem_u32(out);
 #pragma unroll
-      for (int w = 0; w < W; ++w) {
-        if (w == a.rank) continue;
-        const uint64_t dst = a.bases[w] + fin_off + (uint64_t)c0 * 16;
-        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
-                     "r"(src), "r"((uint32_t)(n * 16))
-                     : "memory");
-      }
-      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-      if (k + BULK_STAGES < mine)
-        bulk_issue<W>(a, stages, bars, blockIdx.x + (k + BULK_STAGES) * gridDim.x, s, total,
-                      block_off);
+      for (int w = 0; w < W; ++w)
+        if (w != a.rank) reinterpret_cast<uint4*>(a.bases[w] + a.final_off)[e] = y;
     }
+    __syncthreads();  // stage s has been read by every thread
+    if (threadIdx.x == 0 && k + BULK_STAGES < mine)
+      bulk_issue<W>(a, stages, bars, blockIdx.x + (k + BULK_STAGES) * gridDim.x, s, total,
+                    block_off);
   }
-  if (threadIdx.x == 0) {
-    if (!ok) {
-      report_error(a.err, H3_ERR_TIMEOUT);
-      // the copies this CTA issued land in its shared memory: wait for them (bounded)
-      uint64_t drain = 0;
-      for (int64_t kk = k; kk < mine && kk < k + BULK_STAGES; ++kk)
-        bulk_wait(smem_u32(bars + kk % BULK_STAGES), (uint32_t)((kk / BULK_STAGES) & 1), drain);
-    }
-    // the finished rows are written at the peers before this CTA counts as done
-    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-    asm volatile("fence.proxy.async.global;" ::: "memory");
+  if (!ok && threadIdx.x == 0) {
+    report_error(a.err, H3_ERR_TIMEOUT);
+    // the copies this CTA issued land in its shared memory: wait for them (bounded)
+    uint64_t drain = 0;
+    for (int64_t kk = k; kk < mine && kk < k + BULK_STAGES; ++kk)
+      bulk_wait(smem_u32(bars + kk % BULK_STAGES), (uint32_t)((kk / BULK_STAGES) & 1), drain);
   }
   // done publication as in reduce_kernel
   __threadfence_system();
@@ -570,8 +543,7 @@ static bool bulk_pull() {
 template <int W>
 cudaError_t launch_bulk(const Args& a, int dev, cudaStream_t st) {
   constexpr int TC = BULK_STAGE / 16 / W;
-  // input stages, then one output buffer (a rank's slice of a tile) per stage
-  const size_t smem = (size_t)BULK_STAGES * BULK_STAGE + (size_t)BULK_STAGES * TC * 16;
+  const size_t smem = (size_t)BULK_STAGES * BULK_STAGE;
   static bool attr[64] = {false};
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr[dev]) {
@@ -582,7 +554,7 @@ cudaError_t launch_bulk(const Args& a, int dev, cudaStream_t st) {
   }
   const int64_t total = (a.row_end - a.row_begin) * (a.width >> 3);
   const int64_t tiles = (total + TC - 1) / TC;
-  // up to three CTAs an SM (64 KB of input stages each, plus the output buffers)
+  // three CTAs an SM (64 KB of stages each): 48 tiles of 16 KB in flight per SM
   const int blocks = (int)std::max<int64_t>(
       1, std::min<int64_t>(tiles, (int64_t)h3host::sm_count(dev) * 3));
   reduce_bulk_kernel<W><<<blocks, BULK_THREADS, smem, st>>>(a);
