@@ -44,7 +44,8 @@ OUT = HERE / "_ref"
 SRC = OUT / "tilelang_ref.cu"
 MANIFEST = OUT / "tilelang_ref.json"
 LIB = OUT / "libh3ref_tilelang.so"
-REFERENCE = Path(os.environ.get("H3_REFERENCE_DIR", "/root/reference"))
+# the reference checkout: H3_REFERENCE_DIR, else a `reference` directory beside this repository
+REFERENCE = Path(os.environ.get("H3_REFERENCE_DIR", str(HERE.parents[1] / "reference")))
 
 # (name, module under patches/, factory, positional arguments).  Shapes are the ones
 # the GPU tests feed; every factory is the reference's own.
