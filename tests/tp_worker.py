@@ -123,3 +123,89 @@ def dead_rank_case(rank, world, port, outdir):
     except Exception as e:  # gloo raises on timeout / peer loss
         Path(outdir, "r0.txt").write_text(f"error after {time.time() - t0:.1f}s: {type(e).__name__}")
     os._exit(0)
+
+
+def _full_block(H, heads, hd, F, T, seed=3):
+    """A stand-in for the reference's full (unsharded) DiT block: the parameters
+    TPDiTBlockINT8.load_from_full_block reads, under the names it reads them by."""
+    import torch
+    from torch import nn
+    g = torch.Generator().manual_seed(seed)
+
+    def proj(n, k, div=1.0):
+        m = nn.Module()
+        m.register_buffer("weight", torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8))
+        m.register_buffer("weight_scale", (torch.rand((n, 1), generator=g) * 9e-3 + 1e-3) / div)
+        return m
+
+    def norm(n):
+        m = nn.Module()
+        m.weight = nn.Parameter(1.0 + 0.1 * torch.randn(n, generator=g))
+        return m
+
+    blk = nn.Module()
+    blk.norm1, blk.norm2 = norm(H), norm(H)
+    blk.attn = nn.Module()
+    blk.attn.q_norm, blk.attn.k_norm = norm(hd), norm(hd)
+    blk.attn.qkv_proj = proj(3 * heads * hd, H)
+    blk.attn.out_proj = proj(H, heads * hd, 64.0)
+    blk.mlp = nn.Module()
+    blk.mlp.fc1 = proj(2 * F, H)
+    blk.mlp.fc2 = proj(H, F, 64.0)
+    blk.adaln_proj = nn.Module()
+    blk.adaln_proj.apply_silu = True
+    blk.adaln_proj.linear = nn.Linear(T, 6 * 3 * H)
+    with torch.no_grad():
+        blk.adaln_proj.linear.weight.copy_(0.05 * torch.randn(6 * 3 * H, T, generator=g))
+        blk.adaln_proj.linear.bias.copy_(0.05 * torch.randn(6 * 3 * H, generator=g))
+    return blk
+
+
+def reference_block_case(rank, world, port, outdir, refdir):
+    """The reference's own TPDiTBlockINT8 (patches/tp_dit.py) with this library's
+    projection modules swapped in as INTEGRATION.md shows: the block is built, loaded
+    with load_from_full_block and run by the reference's code; only the four projections
+    are ours (their kernels replaced by the oracle-backed stand-in on CPU ranks).
+    `comfy_kitchen` is imported at the top of the reference module but used only by
+    the RoPE branch, which this case does not take; an empty module stands in for it."""
+    import types
+    import torch
+    try:
+        dist = _init(rank, world, port)
+        sys.modules.setdefault("comfy_kitchen", types.ModuleType("comfy_kitchen"))
+        if refdir not in sys.path:
+            sys.path.insert(0, refdir)
+        import patches.tp_dit as ref_tp_dit
+        from h3tp import tp_dit as b200, swiglu_quant
+        # The fused FC2 route checks for an sm_100 device before it runs; on these CPU
+        # ranks the same contract minus the device check lets the route (and its MAX
+        # all-reduce) run on the stand-in kernels.
+        def cpu_supported(x, weight, weight_scale, world_size, groupsize):
+            try:
+                _, kl = swiglu_quant.input_kind(x, weight.shape[1])
+            except ValueError:
+                return False
+            return (kl % 256 == 0 and kl == weight.shape[1] and groupsize == 256
+                    and world_size in (1, 2, 4, 8))
+        swiglu_quant.supported = cpu_supported
+        ref_tp_dit.ColumnParallelLinearINT8 = b200.ColumnParallelLinearINT8
+        ref_tp_dit.RowParallelLinearINT8 = b200.RowParallelLinearINT8
+        H, heads, hd, F, T, S = 512, 4, 128, 1024, 8, 48
+        blk = ref_tp_dit.TPDiTBlockINT8(hidden=H, heads=heads, head_dim=hd, ffn=F, t_dim=T,
+                                        rank=rank, world_size=world, device="cpu")
+        for name in ("qkv_proj", "out_proj", "fc1", "fc2"):
+            assert type(getattr(blk, name)).__module__ == "h3tp.tp_dit", name
+        blk.load_from_full_block(_full_block(H, heads, hd, F, T))
+        g = torch.Generator().manual_seed(11)
+        x = torch.randn((S, H), generator=g)
+        t_emb = torch.randn((3, T), generator=g)
+        segments = [(0, 20, 0), (20, 33, 2), (33, S, 1)]
+        with torch.no_grad():
+            out = blk(x.clone(), t_emb, segments)
+        assert out.shape == (S, H) and out.dtype == torch.float32
+        np.save(os.path.join(outdir, f"r{rank}.npy"), out.numpy())
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        Path(outdir, f"err{rank}.txt").write_text(traceback.format_exc())
+        raise
