@@ -143,6 +143,28 @@ H3_DEV void load_activation2(const void* x, int64_t row, int64_t width, int64_t 
   for (int j = 0; j < 16; ++j) p[j] = pk2(a[j], b[j]);
 }
 
+// L2 prefetch of this thread's blocks of row `row` (the CTA's next row): the loads that
+// follow one iteration later then find the row in L2, with no register held meanwhile.
+template <int KIND>
+H3_DEV void prefetch_activation2(const void* x, int64_t row, int64_t width, int64_t blk0,
+                                 int64_t blk1, bool ok0, bool ok1) {
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    if (!(e == 0 ? ok0 : ok1)) continue;
+    const int64_t blk = e == 0 ? blk0 : blk1;
+    const char* p;
+    if (KIND == H3_IN_ACT_F32)
+      p = reinterpret_cast<const char*>(reinterpret_cast<const float*>(x) + row * width + blk * 16);
+    else if (KIND == H3_IN_ACT_F16)
+      p = reinterpret_cast<const char*>(reinterpret_cast<const __half*>(x) + row * width + blk * 16);
+    else
+      p = reinterpret_cast<const char*>(reinterpret_cast<const __half*>(x) + row * 2 * width + blk * 16);
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+    if (KIND == H3_IN_GATEUP_F16)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p + width * 2));
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Row staging (the persistent producers).  A CTA keeps ROW_STAGES rows of its input in
 // flight: each row is copied global -> shared memory by TMA (cp.async.bulk.tensor,
@@ -432,6 +454,12 @@ __global__ void __launch_bounds__(512) swiglu_rotate_kernel(
         stage_activation2<KIND>(stg, width, blk[p][0], blk[p][1], ok[p][0], ok[p][1], v[p]);
       stage_next(&map, st, stages, bars, it, row, rows);
     }
+    if (!STAGED && row + gridDim.x < rows) {
+#pragma unroll
+      for (int p = 0; p < NP; ++p)
+        prefetch_activation2<KIND>(x, row + gridDim.x, width, blk[p][0], blk[p][1], ok[p][0],
+                                   ok[p][1]);
+    }
     float m_nan = 0.0f;
 #pragma unroll
     for (int p = 0; p < NP; ++p) {
@@ -514,6 +542,12 @@ __global__ void __launch_bounds__(512) swiglu_rotate_peer_kernel(
     float m = 0.0f;
     f32x2 v[NP][16];
     if (have) {
+      if (row + gridDim.x < rows) {
+#pragma unroll
+        for (int p = 0; p < NP; ++p)
+          prefetch_activation2<KIND>(x, row + gridDim.x, width, blk[p][0], blk[p][1], ok[p][0],
+                                     ok[p][1]);
+      }
       float m_nan = 0.0f;
 #pragma unroll
       for (int p = 0; p < NP; ++p) {
@@ -692,6 +726,14 @@ __global__ void __launch_bounds__(512) column_quantize_kernel(
         stage_activation2<H3_IN_ACT_F16>(stg, k, blk[p][0], blk[p][1], ok[p][0], ok[p][1], v[p]);
       stage_next(&map, st, stages, bars, it, row, rows);
     } else {
+      // the modulated-norm form spends long enough on a row for an L2 prefetch of the
+      // next one to pay (measured 3-4% faster); the plain quantiser measured 5% slower
+      if (NORM && row + gridDim.x < rows) {
+#pragma unroll
+        for (int p = 0; p < NP; ++p)
+          prefetch_activation2<H3_IN_ACT_F16>(x, row + gridDim.x, k, blk[p][0], blk[p][1],
+                                              ok[p][0], ok[p][1]);
+      }
 #pragma unroll
       for (int p = 0; p < NP; ++p)
         load_activation2<H3_IN_ACT_F16>(x, row, k, blk[p][0], blk[p][1], ok[p][0], ok[p][1], v[p]);
