@@ -646,6 +646,20 @@ def test_column_and_int32_dequantize(cuda_device, oracle):
                 oracle.dequantize_i32(C, a, w, out="f16"))
 
 
+def test_sm_clock_probe(cuda_device):
+    """h3_sm_clock_probe: it sleeps at least the requested time and reports the SM
+    cycles of that interval; the clock they give lies in the part's range."""
+    from h3tp import ops
+    out = torch.zeros(2, dtype=torch.int64, device=cuda_device)
+    ops.sm_clock_probe(out, 2_000_000, torch.cuda.current_stream(cuda_device))
+    torch.cuda.synchronize()
+    ns, cycles = out.tolist()
+    assert 2_000_000 <= ns < 200_000_000
+    assert 200.0 < cycles / ns * 1e3 < 2500.0
+    with pytest.raises(ValueError):
+        ops.sm_clock_probe(out, 0, torch.cuda.current_stream(cuda_device))
+
+
 def test_no_device_error_after_suite(cuda_device):
     from h3tp import _native
     torch.cuda.synchronize()
