@@ -485,13 +485,22 @@ def run_ours(args):
         if record:
             ev[0].record(stream)
         shift = T.shift_for(ffn // world, world)
-        push = args.transport == "p2p" and P.pushes(world)  # the route row_linear takes
+        # the route row_linear takes
+        form = P.exchange_form(world) if args.transport == "p2p" else "pull"
+        push = form == "push"
         if push:
             ws.encode_push(q, mlp.fc2.weight, shift)
         else:
             ops.int8_gemm_row_encode(q, mlp.fc2.weight, shift, out=ws.partial(M))
         if record:
             ev[1].record(stream)
+        if form == "dma":
+            ws.reduce_and_gather_dma(M, shift, scale, mlp.fc2.weight_scale.reshape(-1), xres)
+            if record:
+                ev[2].record(stream)
+                ev[3].record(stream)
+                sub_events.append(ev)
+            return
         ws.epoch = P.next_epoch(ws.epoch)
         ops.peer_reduce(ws.bases, ws.world, ws.rank, 0, ws.partial_off, ws.final_off, M, hidden,
                         shift, scale, mlp.fc2.weight_scale.reshape(-1), xres, None, None, ws.epoch,
@@ -787,11 +796,15 @@ def run_ours(args):
                                         "gather"))},
             "fc2_chain_note": "[min, max] over ranks of the mean per step; the reduce includes "
                               "the wait for the slowest rank's ready flag",
-            "fc2_exchange": ("push: the row GEMM stores each partial row into its owner's "
-                             "buffer over NVLink, the owner reduces from local memory"
-                             if args.transport == "p2p" and P.pushes(world) else
-                             "pull: the row GEMM writes locally, each owner loads its rows "
-                             "from every peer")}
+            "fc2_exchange": {"push": "push: the row GEMM stores each partial row into its "
+                                     "owner's buffer over NVLink, the owner reduces from local "
+                                     "memory",
+                             "dma": "dma: copy engines pull the peers' rows of the owned block "
+                                    "and, after the reduce, the peers' finished rows (the "
+                                    "reduce column holds the whole exchange)",
+                             "pull": "pull: the row GEMM writes locally, each owner loads its "
+                                     "rows from every peer"}[
+                P.exchange_form(world) if args.transport == "p2p" else "pull"]}
            if sub_events else {}),
         "device_error": err,
         **({"sm_clock_in_kernel": sm_clock} if sm_clock else {}),

@@ -309,6 +309,30 @@ int h3_peer_reduce_pushed(const void* const* bases, int world, int rank, int64_t
                           int shift, const float* row_scale, const float* weight_scale,
                           void* residual_f16, const float* gate, int64_t gate_rows,
                           const int32_t* labels, uint32_t epoch, void* stream);
+/* The copy-engine ("dma") form of the exchange, four steps on one stream per rank:
+ *   1. h3_peer_signal(which = 0, publish = 1): this rank's partial (h3_int8_gemm_row_encode
+ *      at partial_off) is complete; wait (bounded) until every rank's is;
+ *   2. h3_copy_async per peer w: rank w's rows of this rank's block, from w's partial area,
+ *      into slot w of this rank's staging area at stage_off ([world][per][width] fp16);
+ *   3. h3_peer_reduce_staged: the rank-order reduce + epilogue of the block from the
+ *      staging slots (this rank's own rows read in place at own_off), the finished rows
+ *      stored into this rank's own final area, then done published to every rank;
+ *   4. h3_peer_signal(which = 1, publish = 0): wait (bounded) for every peer's done, then
+ *      h3_copy_async per peer: its finished rows from its final area into residual_f16.
+ * Copies between GPUs go through the copy engines (cudaMemcpyAsync), which carry NVLink
+ * traffic faster than loads and stores issued by the SMs.  Same bits as h3_peer_reduce.
+ * A wait that gives up records H3_ERR_TIMEOUT; the copies that follow it then move
+ * whatever the buffers hold, and the error word says so. */
+int h3_peer_signal(const void* const* bases, int world, int rank, int64_t flags_off, int which,
+                   uint32_t epoch, int publish, void* stream);
+int h3_peer_reduce_staged(const void* const* bases, int world, int rank, int64_t flags_off,
+                          int64_t stage_off, int64_t own_off, int64_t final_off, int64_t rows,
+                          int64_t width, int shift, const float* row_scale,
+                          const float* weight_scale, void* residual_f16, const float* gate,
+                          int64_t gate_rows, const int32_t* labels, uint32_t epoch,
+                          void* stream);
+/* cudaMemcpyAsync device to device (either side may be a peer's mapped buffer). */
+int h3_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
 int h3_peer_reduce_nvls(const void* const* bases, const void* multicast, int world, int rank,
                         int64_t flags_off, int64_t partial_off, int64_t final_off, int64_t rows,
                         int64_t width, int shift, const float* row_scale,

@@ -75,6 +75,8 @@ struct Args {
   int64_t gate_rows;
   const int32_t* labels;
   uint32_t epoch;
+  int64_t own_off;  // FP16_PUSHED: this rank's own rows of its block (slot `rank`)
+  int final_local;  // finished rows into this rank's own final area (the peers pull them)
   int* err;
 };
 
@@ -301,7 +303,8 @@ __global__ void __launch_bounds__(THREADS) reduce_kernel(const Args a) {
           // chunk i of slot w (rank w's rows of this block) in this rank's own buffer
 #pragma unroll
           for (int w = 0; w < L; ++w)
-            u[k][w] = load_received(own, a.partial_off + (w * a.per * chunks + i) * 16);
+            u[k][w] = load_received(own, w == a.rank ? a.own_off + i * 16
+                                                     : a.partial_off + (w * a.per * chunks + i) * 16);
         } else {
 #pragma unroll
           for (int w = 0; w < L; ++w)
@@ -333,6 +336,8 @@ __global__ void __launch_bounds__(THREADS) reduce_kernel(const Args a) {
         res[e] = y;
         if (PAYLOAD == FP16_NVLS) {
           store_all_nvls(a.mc, a.final_off + e * 16, y);
+        } else if (a.final_local) {
+          reinterpret_cast<uint4*>(own + a.final_off)[e] = y;
         } else {
 #pragma unroll
           for (int w = 0; w < W; ++w)
@@ -583,7 +588,7 @@ int run(const void* const* bases, const void* mc, int world, int rank, int64_t f
         int64_t partial_off, int64_t final_off, int64_t rows, int64_t width, int shift,
         const float* row_scale, const float* weight_scale, void* residual_f16, const float* gate,
         int64_t gate_rows, const int32_t* labels, uint32_t epoch, bool gather, int payload,
-        void* stream) {
+        void* stream, int64_t own_off = -1, bool final_local = false) {
   const bool packed = payload == INT8_P2P;
   if (payload == FP16_NVLS && (mc == nullptr || !h3host::aligned(mc, 16))) return H3_ERR_INVALID;
   if (bases == nullptr || residual_f16 == nullptr || (world != 2 && world != 4 && world != 8) ||
@@ -627,6 +632,10 @@ int run(const void* const* bases, const void* mc, int world, int rank, int64_t f
   a.gate_rows = gate_rows;
   a.labels = labels;
   a.epoch = epoch;
+  // own rows: slot `rank` of the owner-routed layout unless given
+  a.own_off = own_off >= 0 ? own_off : partial_off + rank * a.per * (width / 8) * 16;
+  a.final_local = final_local ? 1 : 0;
+  if (own_off >= 0 && own_off % 16 != 0) return H3_ERR_INVALID;
   a.err = h3host::error_word(dev);
   if (a.err == nullptr) return H3_ERR_CUDA;
   // Enough CTAs to keep every SM's load slots busy; the flags make any grid size safe
@@ -644,6 +653,64 @@ int run(const void* const* bases, const void* mc, int world, int rank, int64_t f
 
 }  // namespace peer
 }  // namespace h3
+
+namespace h3 {
+namespace peer {
+// One warp: optionally stores `epoch` into flag `region`[rank] of every rank, then waits
+// (bounded) until this rank's flags region[w] >= epoch for every other rank w.  Orders
+// the copy-engine pulls of the dma exchange after the peers' matching kernels.
+__global__ void signal_kernel(const Args a, int64_t region, int publish) {
+  if (publish && (int)threadIdx.x < a.world) {
+    __threadfence_system();
+    store_release(flag(a, threadIdx.x, region, a.rank), a.epoch);
+  }
+  if (!wait_all(a, region, true) && threadIdx.x == 0) report_error(a.err, H3_ERR_TIMEOUT);
+}
+}  // namespace peer
+}  // namespace h3
+
+extern "C" int h3_peer_signal(const void* const* bases, int world, int rank, int64_t flags_off,
+                              int which, uint32_t epoch, int publish, void* stream) {
+  if (bases == nullptr || (world != 2 && world != 4 && world != 8) || rank < 0 ||
+      rank >= world || epoch == 0 || flags_off < 0 || flags_off % 16 || (which != 0 && which != 1))
+    return H3_ERR_INVALID;
+  h3::peer::Args a{};
+  for (int w = 0; w < world; ++w) {
+    if (bases[w] == nullptr || !h3host::aligned(bases[w], 16)) return H3_ERR_INVALID;
+    a.bases[w] = reinterpret_cast<uint64_t>(bases[w]);
+  }
+  int dev;
+  h3host::DeviceScope scope;
+  if (int s = scope.bind(bases[rank], &dev)) return s;
+  a.flags_off = flags_off;
+  a.world = world;
+  a.rank = rank;
+  a.epoch = epoch;
+  a.err = h3host::error_word(dev);
+  if (a.err == nullptr) return H3_ERR_CUDA;
+  h3::peer::signal_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(a, which ? h3::peer::DONE : h3::peer::READY,
+                                                             publish);
+  return h3host::check_launch();
+}
+
+extern "C" int h3_peer_reduce_staged(const void* const* bases, int world, int rank,
+                                     int64_t flags_off, int64_t stage_off, int64_t own_off,
+                                     int64_t final_off, int64_t rows, int64_t width, int shift,
+                                     const float* row_scale, const float* weight_scale,
+                                     void* residual_f16, const float* gate, int64_t gate_rows,
+                                     const int32_t* labels, uint32_t epoch, void* stream) {
+  if (own_off < 0) return H3_ERR_INVALID;
+  return h3::peer::run(bases, nullptr, world, rank, flags_off, stage_off, final_off, rows, width,
+                       shift, row_scale, weight_scale, residual_f16, gate, gate_rows, labels,
+                       epoch, false, h3::peer::FP16_PUSHED, stream, own_off, true);
+}
+
+extern "C" int h3_copy_async(void* dst, const void* src, int64_t bytes, void* stream) {
+  if (dst == nullptr || src == nullptr || bytes < 0) return H3_ERR_INVALID;
+  if (bytes == 0) return H3_OK;
+  return cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDeviceToDevice,
+                         (cudaStream_t)stream) == cudaSuccess ? H3_OK : H3_ERR_CUDA;
+}
 
 extern "C" int h3_peer_reduce(const void* const* bases, int world, int rank, int64_t flags_off,
                               int64_t partial_off, int64_t final_off, int64_t rows,

@@ -70,6 +70,10 @@ SIGNATURES = {
     "h3_peer_reduce_pushed": [_PP, _I, _I, _I64, _I64, _I64, _I64, _I64, _I, _P, _P, _P, _P, _I64, _P,
                        _U32, _P],
     "h3_int8_gemm_row_encode_push": [_P, _P, _I64, _I64, _I64, _I, _PP, _I, _I, _I64, _P],
+    "h3_peer_signal": [_PP, _I, _I, _I64, _I, _U32, _I, _P],
+    "h3_peer_reduce_staged": [_PP, _I, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I, _P, _P, _P, _P,
+                              _I64, _P, _U32, _P],
+    "h3_copy_async": [_P, _P, _I64, _P],
     "h3_peer_reduce_nvls": [_PP, _P, _I, _I, _I64, _I64, _I64, _I64, _I64, _I, _P, _P, _P, _P,
                             _I64, _P, _U32, _P],
     "h3_peer_gather": [_PP, _I, _I, _I64, _I64, _I64, _I64, _P, _U32, _P],
@@ -124,7 +128,8 @@ def check(status: int, name: str) -> None:
 # Entry points that enqueue exactly one kernel per successful call.
 _LAUNCHING = {n for n in SIGNATURES if n not in (
     "h3_abi_version", "h3_status_string", "h3_device_error", "h3_device_error_peek",
-    "h3_transport_shift", "h3_column_linear_noalloc_error", "h3_sm_clock_probe")}
+    "h3_transport_shift", "h3_column_linear_noalloc_error", "h3_sm_clock_probe",
+    "h3_copy_async")}
 _launches = 0
 
 

@@ -509,6 +509,40 @@ def peer_reduce(bases, world: int, rank: int, flags_off: int, partial_off: int, 
     return residual
 
 
+def peer_signal(bases, world: int, rank: int, flags_off: int, which: int, epoch: int,
+                publish: bool, like: torch.Tensor) -> None:
+    """h3_peer_signal on the stream of `like`'s device: optionally publish flag `which`
+    (0 ready, 1 done) of this rank to every rank, then wait (bounded) for every peer's."""
+    arr = (ctypes.c_void_p * world)(*bases)
+    N.call("h3_peer_signal", arr, world, rank, int(flags_off), int(which), int(epoch),
+           1 if publish else 0, _stream(like))
+
+
+def peer_reduce_staged(bases, world: int, rank: int, flags_off: int, stage_off: int,
+                       own_off: int, final_off: int, rows: int, width: int, shift: int,
+                       row_scale, weight_scale, residual, gate=None, labels=None,
+                       epoch: int = 1):
+    """The reduce of the copy-engine exchange (h3_peer_reduce_staged): the peers' rows of
+    this rank's block from the staging slots, its own rows at own_off, the finished rows
+    into this rank's own final area."""
+    a = _vec(row_scale, rows, "row_scale")
+    ws = _vec(weight_scale, width, "weight_scale")
+    if not residual.is_contiguous():
+        raise ValueError("residual must be contiguous (updated in place)")
+    res, g, grows, lab = _gate_args(residual, gate, labels, rows, width)
+    arr = (ctypes.c_void_p * world)(*bases)
+    N.call("h3_peer_reduce_staged", arr, world, rank, int(flags_off), int(stage_off),
+           int(own_off), int(final_off), rows, width, int(shift), a.data_ptr(), ws.data_ptr(),
+           res.data_ptr(), _ptr(g), grows, _ptr(lab), int(epoch), _stream(res))
+    return residual
+
+
+def copy_async(dst: int, src: int, nbytes: int, like: torch.Tensor) -> None:
+    """cudaMemcpyAsync of nbytes between device addresses (either may be a peer's mapped
+    buffer) on the stream of `like`'s device."""
+    N.call("h3_copy_async", int(dst), int(src), int(nbytes), _stream(like))
+
+
 def peer_reduce_int8(bases, world: int, rank: int, flags_off: int, partial_off: int,
                      final_off: int, rows: int, width: int, row_scale, weight_scale, residual,
                      gate=None, labels=None, epoch: int = 1):

@@ -39,11 +39,17 @@ _ALIGN = 256
 _EXCHANGE = os.environ.get("H3_P2P_EXCHANGE", "")
 
 
+def exchange_form(world: int) -> str:
+    """The form the p2p route takes at `world` ranks: 'pull', 'push' or 'dma' (the
+    copy-engine form, reduce_and_gather_dma)."""
+    if _EXCHANGE in ("push", "pull", "dma"):
+        return _EXCHANGE
+    return "pull"
+
+
 def pushes(world: int) -> bool:
     """Whether the p2p route at `world` ranks takes the push form."""
-    if _EXCHANGE in ("push", "pull"):
-        return _EXCHANGE == "push"
-    return False
+    return exchange_form(world) == "push"
 
 
 def _group_name(group) -> str:
@@ -81,8 +87,11 @@ def layout(width: int, rows: int) -> dict:
     # (encode_push) of up to 8 ranks fit the partial area
     region = -(-(rows + 8) * width * 2 // _ALIGN) * _ALIGN
     slots = -(-rows * 8 * 8 // _ALIGN) * _ALIGN
+    # the copy-engine exchange stages the peers' rows of this rank's block after the slots
     return {"partial_off": FLAGS_BYTES, "final_off": FLAGS_BYTES + region,
-            "slots_off": FLAGS_BYTES + 2 * region, "nbytes": FLAGS_BYTES + 2 * region + slots}
+            "slots_off": FLAGS_BYTES + 2 * region,
+            "stage_off": FLAGS_BYTES + 2 * region + slots,
+            "nbytes": FLAGS_BYTES + 3 * region + slots}
 
 
 class PeerWorkspace:
@@ -101,6 +110,7 @@ class PeerWorkspace:
         self.partial_off = lay["partial_off"]
         self.final_off = lay["final_off"]
         self.slots_off = lay["slots_off"]
+        self.stage_off = lay["stage_off"]
         nbytes = lay["nbytes"]
         with torch.cuda.device(self.device):
             self.buf = symm.empty(nbytes, dtype=torch.uint8, device=self.device)
@@ -193,6 +203,38 @@ class PeerWorkspace:
             raise ValueError(f"{rows} rows exceed the workspace capacity {self.capacity}")
         ops.int8_gemm_row_encode_push(q, weight, shift, self.bases, self.world, self.rank,
                                       self.partial_off)
+
+    def reduce_and_gather_dma(self, rows: int, shift: int, row_scale, weight_scale, residual,
+                              gate=None, labels=None):
+        """The copy-engine form of reduce_and_gather for the fp16 partials in partial():
+        after every rank's ready, this rank pulls the peers' rows of its block into its
+        staging slots with cudaMemcpyAsync, reduces them (with its own rows) into its
+        residual rows and its own final area, and after every peer's done pulls the
+        peers' finished rows into the residual.  Same bits as reduce_and_gather."""
+        self.epoch = next_epoch(self.epoch)
+        world, rank = self.world, self.rank
+        per = -(-rows // world)
+        pitch = self.width * 2
+        b0, b1 = min(rows, rank * per), min(rows, (rank + 1) * per)
+        own = self.bases[rank]
+        ops.peer_signal(self.bases, world, rank, 0, 0, self.epoch, True, residual)
+        for k in range(1, world):
+            w = (rank + k) % world
+            ops.copy_async(own + self.stage_off + w * per * pitch,
+                           self.bases[w] + self.partial_off + b0 * pitch, (b1 - b0) * pitch,
+                           residual)
+        ops.peer_reduce_staged(self.bases, world, rank, 0, self.stage_off,
+                               self.partial_off + b0 * pitch, self.final_off, rows, self.width,
+                               shift, row_scale, weight_scale, residual, gate, labels,
+                               self.epoch)
+        ops.peer_signal(self.bases, world, rank, 0, 1, self.epoch, False, residual)
+        base = residual.data_ptr()
+        for k in range(1, world):
+            w = (rank + k) % world
+            w0, w1 = min(rows, w * per), min(rows, (w + 1) * per)
+            ops.copy_async(base + w0 * pitch, self.bases[w] + self.final_off + w0 * pitch,
+                           (w1 - w0) * pitch, residual)
+        return residual
 
     def reduce_and_gather(self, rows: int, shift: int, row_scale, weight_scale, residual,
                           gate=None, labels=None, packed: bool = False, nvls: bool = False,

@@ -141,13 +141,17 @@ def _finish_quantized(q, scale, weight, weight_scale, comm, scaled_transport=Tru
             # nvls): the GEMM writes locally and the reduce reads the peers.
             rows = q.shape[0]
             ws = P.workspace(comm, q.device, weight.shape[0], rows)
-            push = transport == "p2p" and P.pushes(world)
+            form = P.exchange_form(world) if transport == "p2p" else "pull"
+            push = form == "push"
             with label("int8_gemm_scaled_fp16_encode"):
                 if push:
                     ws.encode_push(q, weight, shift)
                 else:
                     ops.int8_gemm_row_encode(q, weight, shift, out=ws.partial(rows))
             with label("scaled_fp16_peer_reduce_gather"):
+                if form == "dma":
+                    return ws.reduce_and_gather_dma(rows, shift, scale, weight_scale, residual,
+                                                    gate, labels)
                 return ws.reduce_and_gather(rows, shift, scale, weight_scale, residual, gate, labels,
                                             nvls=transport == "nvls", pushed=push)
         with label("int8_gemm_scaled_fp16_encode"):

@@ -142,6 +142,75 @@ def test_peer_transport_pushed_bit_exact(cuda_device, oracle, world, rows, width
     assert _native.device_error(dev.index or 0) == 0
 
 
+@pytest.mark.parametrize("world,rows,width,k", [(2, 130, 512, 512), (4, 77, 264, 256),
+                                                (8, 99, 1024, 256)])
+def test_peer_transport_copy_engine_bit_exact(cuda_device, oracle, world, rows, width, k):
+    """The copy-engine exchange: each emulated rank pulls the other ranks' rows of its
+    block into its staging slots (h3_copy_async), reduces them with its own rows into its
+    residual rows and its own final area (h3_peer_reduce_staged), then pulls the other
+    ranks' finished rows into its residual.  The flags h3_peer_signal waits for are set
+    before it runs, so no kernel waits for another."""
+    from h3tp import _native, ops, transport
+    rng = np.random.default_rng(world + 80)
+    shift = transport.shift_for(k, world)
+    qs = [rng.integers(-128, 128, size=(rows, k), dtype=np.int8) for _ in range(world)]
+    ws = [rng.integers(-127, 128, size=(width, k), dtype=np.int8) for _ in range(world)]
+    enc = np.stack([oracle.fp16_encode(oracle.int8_gemm(q, w), shift) for q, w in zip(qs, ws)])
+    a = rng.uniform(1e-4, 1e-2, size=rows).astype(np.float32)
+    s = rng.uniform(1e-5, 1e-4, size=width).astype(np.float32)
+    X = rng.standard_normal((rows, width)).astype(np.float16)
+    G = rng.standard_normal((3, width)).astype(np.float32)
+    labels = rng.integers(0, 3, size=rows).astype(np.int32)
+    ref = X.copy()
+    oracle.row_reduce_finish(enc, shift, a, s, out="residual", residual=ref, gate=G, labels=labels)
+
+    dev = cuda_device
+    per = -(-rows // world)
+    pitch = width * 2
+    roff = FLAGS
+    foff = roff + _region(rows, width)
+    soff = foff + _region(rows, width)
+    nbytes = soff + _region(world * per, width)
+    bufs = [torch.zeros(nbytes, dtype=torch.uint8, device=dev) for _ in range(world)]
+    bases = [b.data_ptr() for b in bufs]
+    A, S = torch.from_numpy(a).to(dev), torch.from_numpy(s).to(dev)
+    Gd, L = torch.from_numpy(G).to(dev), torch.from_numpy(labels).to(dev)
+    qd = [torch.from_numpy(q).to(dev) for q in qs]
+    wd = [torch.from_numpy(w).to(dev) for w in ws]
+    res = [torch.from_numpy(X.copy()).to(dev) for _ in range(world)]
+    blocks = [(min(rows, r * per), min(rows, (r + 1) * per)) for r in range(world)]
+    for epoch in (1, 2):
+        for r in range(world):
+            res[r].copy_(torch.from_numpy(X))
+            part = bufs[r][roff:roff + rows * pitch].view(torch.float16).view(rows, width)
+            ops.int8_gemm_row_encode(qd[r], wd[r], shift, out=part)
+        for b in bufs:
+            _set(b, READY, range(world), epoch)
+        for r in range(world):
+            ops.peer_signal(bases, world, r, 0, 0, epoch, True, res[r])
+            b0, b1 = blocks[r]
+            for k_ in range(1, world):
+                w = (r + k_) % world
+                ops.copy_async(bases[r] + soff + w * per * pitch, bases[w] + roff + b0 * pitch,
+                               (b1 - b0) * pitch, res[r])
+        for r in range(world):
+            b0, _ = blocks[r]
+            ops.peer_reduce_staged(bases, world, r, 0, soff, roff + b0 * pitch, foff, rows, width,
+                                   shift, A, S, res[r], Gd, L, epoch)
+        for r in range(world):
+            ops.peer_signal(bases, world, r, 0, 1, epoch, False, res[r])
+            for k_ in range(1, world):
+                w = (r + k_) % world
+                w0, w1 = blocks[w]
+                ops.copy_async(res[r].data_ptr() + w0 * pitch, bases[w] + foff + w0 * pitch,
+                               (w1 - w0) * pitch, res[r])
+        torch.cuda.synchronize()
+        for r in range(world):
+            got = res[r].cpu().numpy()
+            assert np.array_equal(got.view(np.uint16), ref.view(np.uint16)), f"rank {r} epoch {epoch}"
+    assert _native.device_error(dev.index or 0) == 0
+
+
 @pytest.mark.parametrize("world,rows,width,k", [(2, 130, 512, 512), (8, 99, 1024, 256)])
 def test_peer_transport_packed_int8_bit_exact(cuda_device, oracle, world, rows, width, k):
     """The same exchange with the packed INT8 payload ('int8_gather'): the row GEMM packs
