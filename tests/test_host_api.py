@@ -217,10 +217,11 @@ def test_p2p_exchange_form_override(monkeypatch):
     H3_P2P_EXCHANGE (read at import); either form gives the same bits."""
     import importlib
     from h3tp import peer
-    for env, want in (("push", True), ("pull", False)):
+    for env, want in (("push", True), ("pull", False), ("dma", False)):
         monkeypatch.setenv("H3_P2P_EXCHANGE", env)
         importlib.reload(peer)
         assert all(peer.pushes(w) is want for w in (2, 4, 8))
+        assert all(peer.exchange_form(w) == env for w in (2, 4, 8))
     monkeypatch.delenv("H3_P2P_EXCHANGE", raising=False)
     importlib.reload(peer)
     assert all(isinstance(peer.pushes(w), bool) for w in (2, 4, 8))
