@@ -3,20 +3,22 @@
 The reference sums the per-rank scaled-FP16 partials with NCCL's fp16 all-reduce and
 then runs the fused row-gate epilogue (tilelang_swiglu_quant.py:119-124,
 tilelang_dit_fusion.py:146-151).  Over NVSwitch every GPU can load from and store
-into every peer's HBM directly, so here the exchange is two kernels of our own
-(csrc/h3_peer.cu):
+into every peer's HBM directly, so here the exchange is kernels of our own
+(csrc/h3_peer.cu).  The default ('pull') form:
 
-  1. the row GEMM's encode epilogue stores every partial row straight into the
-     peer-mapped buffer of the rank that owns that row (h3_int8_gemm_row_encode_push:
-     the reduce-scatter rides on the GEMM, NVLink stores overlapping its tensor work);
-  2. h3_peer_reduce_pushed: each rank sums the slots of its rows from local memory in
-     rank order, decodes, dequantises and updates its rows of the gated residual (the
-     same bits as h3_row_reduce_finish), and stores the finished rows into every peer
-     (NVLink stores);
+  1. the row GEMM's encode epilogue writes this rank's partial into its peer-mapped
+     buffer (no staging copy);
+  2. h3_peer_reduce: each rank copies its rows of every rank's partial into shared
+     memory (cp.async.bulk over NVLink), sums them in rank order, decodes, dequantises
+     and updates its rows of the gated residual (the same bits as
+     h3_row_reduce_finish), and stores the finished rows into every peer;
   3. h3_peer_gather: each rank copies the peers' finished rows into its residual.
-That is the push form (`pushes(world)`); in the pull form, and with nvls, step 1 writes
-the partial locally and step 2 loads the owned rows from every peer instead
-(h3_peer_reduce / h3_peer_reduce_nvls).
+
+exchange_form(world) may instead select 'push' (the GEMM epilogue stores every partial
+row into its owner's buffer, h3_int8_gemm_row_encode_push + h3_peer_reduce_pushed) or
+'dma' (copy engines pull the owned rows and the finished rows, reduce_and_gather_dma);
+with nvls the sum is taken in the NVSwitch (h3_peer_reduce_nvls).  All give the same
+bits at TP2, and every form but nvls at every TP size.
 
 The buffers are torch symmetric memory (one allocation per rank, mapped into every
 rank); synchronisation is by epoch flags in the same buffers, with bounded waits.
