@@ -458,10 +458,6 @@ __global__ void __launch_bounds__(BULK_THREADS) reduce_bulk_kernel(const Args a)
     for (int64_t k = 0; k < mine && k < BULK_STAGES; ++k)
       bulk_issue<W>(a, stages, bars, blockIdx.x + k * gridDim.x, (int)k, total, block_off);
   uint4* res = reinterpret_cast<uint4*>(a.residual);
-  // pairs of chunks start on 32-byte boundaries of every peer's final area
-  bool pairs = (first % 2 == 0) && (a.final_off % 32 == 0);
-#pragma unroll
-  for (int w = 0; w < W; ++w) pairs = pairs && (a.bases[w] % 32 == 0);
   uint64_t deadline = 0;
   int64_t k = 0;
   for (; k < mine; ++k) {
@@ -474,56 +470,20 @@ __global__ void __launch_bounds__(BULK_THREADS) reduce_bulk_kernel(const Args a)
     const int64_t c0 = (blockIdx.x + k * gridDim.x) * TC;
     const int n = (int)min((int64_t)TC, total - c0);
     const uint4* st = reinterpret_cast<const uint4*>(stages + (int64_t)s * W * TC * 16);
-    if (pairs) {
-      // two adjacent chunks a thread: each finished 32-byte pair leaves for a peer as one
-      // 256-bit store (half the NVLink write requests of 16-byte stores)
-      for (int j = 2 * threadIdx.x; j < n; j += 2 * BULK_THREADS) {
-        const int m = min(2, n - j);
-        uint4 y2[2];
+    for (int j = threadIdx.x; j < n; j += BULK_THREADS) {
+      uint4 u[W];
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          if (t >= m) break;
-          uint4 u[W];
+      for (int w = 0; w < W; ++w) u[w] = st[w * TC + j];
+      const int64_t e = first + c0 + j;  // uint4 index of the chunk in [rows][width]
+      const int64_t r = e / chunks;
+      const int64_t cc = (e - r * chunks) << 3;
+      int32_t q[8];
+      restore_fp16<W>(a, u, q);
+      const uint4 y = epilogue_chunk(a, q, r, cc, res[e]);
+      res[e] = y;
 #pragma unroll
-          for (int w = 0; w < W; ++w) u[w] = st[w * TC + j + t];
-          const int64_t e = first + c0 + j + t;
-          const int64_t r = e / chunks;
-          const int64_t cc = (e - r * chunks) << 3;
-          int32_t q[8];
-          restore_fp16<W>(a, u, q);
-          y2[t] = epilogue_chunk(a, q, r, cc, res[e]);
-          res[e] = y2[t];
-        }
-        const int64_t e0 = first + c0 + j;
-#pragma unroll
-        for (int w = 0; w < W; ++w) {
-          if (w == a.rank) continue;
-          uint4* dst = reinterpret_cast<uint4*>(a.bases[w] + a.final_off) + e0;
-          if (m == 2)
-            asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst),
-                         "r"(y2[0].x), "r"(y2[0].y), "r"(y2[0].z), "r"(y2[0].w), "r"(y2[1].x),
-                         "r"(y2[1].y), "r"(y2[1].z), "r"(y2[1].w)
-                         : "memory");
-          else
-            *dst = y2[0];
-        }
-      }
-    } else {
-      for (int j = threadIdx.x; j < n; j += BULK_THREADS) {
-        uint4 u[W];
-#pragma unroll
-        for (int w = 0; w < W; ++w) u[w] = st[w * TC + j];
-        const int64_t e = first + c0 + j;  // uint4 index of the chunk in [rows][width]
-        const int64_t r = e / chunks;
-        const int64_t cc = (e - r * chunks) << 3;
-        int32_t q[8];
-        restore_fp16<W>(a, u, q);
-        const uint4 y = epilogue_chunk(a, q, r, cc, res[e]);
-        res[e] = y;
-#pragma unroll
-        for (int w = 0; w < W; ++w)
-          if (w != a.rank) reinterpret_cast<uint4*>(a.bases[w] + a.final_off)[e] = y;
-      }
+      for (int w = 0; w < W; ++w)
+        if (w != a.rank) reinterpret_cast<uint4*>(a.bases[w] + a.final_off)[e] = y;
     }
     __syncthreads();  // stage s has been read by every thread
     if (threadIdx.x == 0 && k + BULK_STAGES < mine)
